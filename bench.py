@@ -1,0 +1,806 @@
+"""Benchmark of the quantised-linear hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload NAME]
+
+Multi-GPU: launched by torchrun (one rank per GPU, NCCL); RANK / LOCAL_RANK /
+WORLD_SIZE come from the environment. Rank 0 prints one JSON line.
+
+Default workload ``llama7b_stack_quant`` = BASELINE config 2: block-INT8
+quantisation of a Llama-2-7B-shaped bf16 weight stack (32 layers x [4 x
+4096x4096, 2 x 11008x4096, 4096x11008], N(0, 0.02) with 0.1% of entries x20),
+block 64 along the input dimension, layers sharded across ranks with no
+communication ("strong" scaling: the stack is fixed, each rank quantises
+32/N layers). Metric: aggregate algorithmic GB/s = 3.0625 B/element (2 B bf16
+read, 1 B code + 4/64 B scale written) x elements / max-over-ranks time.
+
+Other workloads (``--workload``) time the remaining BASELINE configs for the
+design notes; the driver's default line is config 2.
+
+Timing rules: W >= 3 warm-up steps; the timed region is K steps bracketed by a
+barrier and torch.cuda.synchronize() on both sides, timed with CUDA events on
+the launching stream, max over ranks. Inputs are larger than L2 (126 MB) for
+every workload listed as such in ``config.l2``; the others flush L2 between
+steps by writing a 256 MiB buffer (outside the per-launch events).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+BYTES_PER_ELEM_BF16_QUANT = 2 + 1 + 4 / 64
+
+
+def load_peaks() -> tuple[dict, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        return json.loads(path.read_text()), "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def load_traffic() -> dict:
+    path = ROOT / "profiles" / "traffic.json"
+    return json.loads(path.read_text()) if path.exists() else {}
+
+
+# ---------------------------------------------------------------------------
+# Distributed plumbing
+# ---------------------------------------------------------------------------
+class Dist:
+    def __init__(self, n_gpus: int):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+        if self.world != n_gpus and not (self.world == 1 and n_gpus == 1):
+            if self.world == 1:
+                raise SystemExit(f"--gpus {n_gpus} needs torchrun with {n_gpus} processes")
+        self.pg = None
+        if self.world > 1:
+            import torch.distributed as dist
+
+            torch.cuda.set_device(self.local_rank)
+            dist.init_process_group("nccl", device_id=torch.device("cuda", self.local_rank))
+            self.pg = dist
+
+    @property
+    def device(self) -> torch.device:
+        return torch.device("cuda", self.local_rank)
+
+    def barrier(self) -> None:
+        if self.pg is not None:
+            self.pg.barrier()
+
+    def max(self, value: float) -> float:
+        if self.pg is None:
+            return value
+        t = torch.tensor([value], dtype=torch.float64, device=self.device)
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return t.item()
+
+    def sum(self, value: float) -> float:
+        if self.pg is None:
+            return value
+        t = torch.tensor([value], dtype=torch.float64, device=self.device)
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.SUM)
+        return t.item()
+
+    def close(self) -> None:
+        if self.pg is not None:
+            self.pg.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# Clock sampling during the timed region (NVML)
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {
+        "sw_power_cap": 0x4,
+        "hw_slowdown": 0x8,
+        "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40,
+        "hw_power_brake_slowdown": 0x80,
+    }
+
+    def __init__(self, index: int, period_s: float = 0.02):
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+            phys = int(visible.split(",")[index]) if visible else index
+            self._handle = pynvml.nvmlDeviceGetHandleByIndex(phys)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
+        except Exception:  # noqa: BLE001 - clocks are reported as unavailable
+            self._nvml = None
+        self.period = period_s
+
+    def _run(self) -> None:
+        n = self._nvml
+        while not self._stop.is_set():
+            try:
+                mhz = n.nvmlDeviceGetClockInfo(self._handle, n.NVML_CLOCK_SM)
+                reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self._handle)
+                self.samples.append((mhz, reasons))
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self._nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"]}
+        reasons = set()
+        for _, mask in self.samples:
+            for name, bit in self.REASONS.items():
+                if mask & bit:
+                    reasons.add(name)
+        return {
+            "sm_mhz": statistics.median(m for m, _ in self.samples),
+            "sm_max_mhz": self.max_mhz,
+            "reasons": sorted(reasons),
+            "samples": len(self.samples),
+        }
+
+
+# ---------------------------------------------------------------------------
+# Workload: BASELINE config 2 (Llama-2-7B stack, bf16, layer-sharded quantise)
+# ---------------------------------------------------------------------------
+LLAMA7B_LAYER = [(4096, 4096)] * 4 + [(11008, 4096)] * 2 + [(4096, 11008)]
+LLAMA7B_LAYERS = 32
+
+
+def llama_layer_weights(layer: int, device: torch.device, seed: int = 2026) -> list[torch.Tensor]:
+    """N(0, 0.02) bf16 weights with 0.1% of entries multiplied by 20, seeded per layer."""
+    g = torch.Generator(device=device).manual_seed(seed + layer)
+    out = []
+    for shape in LLAMA7B_LAYER:
+        w = torch.randn(shape, device=device, generator=g, dtype=torch.float32) * 0.02
+        mask = torch.rand(shape, device=device, generator=g) < 0.001
+        w = torch.where(mask, w * 20.0, w).to(torch.bfloat16)
+        out.append(w)
+        del mask
+    return out
+
+
+class LlamaStackQuant:
+    name = "llama7b_stack_quant"
+    metric = "INT8 block quantise GB/s (Llama-2-7B bf16 stack)"
+    unit = "GB/s"
+    dtype = "bf16->int8"
+    kernel = "quantize_tma_kernel<bf16>"
+    bound = "hbm"
+    scaling = "strong"
+    flush_l2 = False
+
+    def __init__(self, dist: Dist, n_layers: int = LLAMA7B_LAYERS):
+        self.dist = dist
+        self.n_layers = n_layers
+        self.layers = [l for l in range(n_layers) if l % dist.world == dist.rank]
+        self.elems_per_layer = sum(a * b for a, b in LLAMA7B_LAYER)
+
+    def config(self) -> dict:
+        return {
+            "workload": "BASELINE config 2: Llama-2-7B bf16 weight stack block-INT8 quantise",
+            "layers": self.n_layers,
+            "layer_shapes": [list(s) for s in LLAMA7B_LAYER],
+            "block": 64,
+            "elements": self.elems_per_layer * self.n_layers,
+            "values": "N(0,0.02), 0.1% x20 outliers, seeded per layer",
+            "parallelism": f"layer-sharded over {self.dist.world} GPU(s), no communication",
+            "l2": "inputs larger than L2 (each step streams the rank's whole stack)",
+        }
+
+    def setup(self) -> None:
+        from cuda_force_b200 import _abi
+
+        dev = self.dist.device
+        self.lib = _abi.load()
+        self.inputs, self.codes, self.scales = [], [], []
+        for layer in self.layers:
+            for w in llama_layer_weights(layer, dev):
+                self.inputs.append(w)
+                self.codes.append(torch.empty(w.shape, dtype=torch.int8, device=dev))
+                self.scales.append(torch.empty(w.numel() // 64, dtype=torch.float32, device=dev))
+        n = len(self.inputs)
+        self.segs = (_abi.QuantSegment * n)(*[
+            _abi.QuantSegment(i.data_ptr(), c.data_ptr(), s.data_ptr(), i.numel())
+            for i, c, s in zip(self.inputs, self.codes, self.scales)
+        ])
+        self.nseg = n
+        self.launches_per_step = (n + _abi.CF_MAX_SEGMENTS - 1) // _abi.CF_MAX_SEGMENTS
+        self.work_per_step = BYTES_PER_ELEM_BF16_QUANT * self.elems_per_layer * len(self.layers)
+
+    def step(self, stream: torch.cuda.Stream) -> None:
+        from cuda_force_b200 import _abi
+
+        _abi.check(self.lib.cf_quantize_int8_many(self.segs, self.nseg, _abi.CF_DTYPE_BF16,
+                                                  stream.cuda_stream), "quantize_many")
+
+    def verify(self) -> None:
+        """Spot-check the timed outputs against the oracle (sampled blocks)."""
+        from oracle import quant_ref
+
+        g = torch.Generator().manual_seed(self.dist.rank)
+        for idx in range(len(self.inputs)):
+            flat_in = self.inputs[idx].reshape(-1)
+            nblocks = flat_in.numel() // 64
+            picks = torch.randint(0, nblocks, (8,), generator=g).tolist() + [nblocks - 1]
+            for b in picks:
+                x = flat_in[b * 64:(b + 1) * 64].cpu().view(torch.int16).numpy().view("uint16")
+                rc, rs = quant_ref.quantize(x)
+                got = self.codes[idx].reshape(-1)[b * 64:(b + 1) * 64].cpu().numpy()
+                if not (got == rc).all() or self.scales[idx][b].item() != rs[0]:
+                    raise SystemExit(f"parity failure in segment {idx} block {b}")
+
+    # -- end to end through the public API with host buffers -----------------
+    def e2e(self, steps: int) -> dict:
+        import cuda_force_b200 as cf
+
+        dev = self.dist.device
+        host_in = [w.cpu().pin_memory() for w in self.inputs[:7]]  # one layer's tensors
+        per_layer = len(host_in)
+        n_layers = len(self.layers)
+        host_codes = [torch.empty(w.shape, dtype=torch.int8).pin_memory() for w in host_in]
+        host_scales = [torch.empty(w.numel() // 64).pin_memory() for w in host_in]
+        copy_stream = torch.cuda.Stream(device=dev)
+        h2d = sum(t.numel() * 2 for t in host_in) * n_layers
+        d2h = sum(c.numel() + s.numel() * 4 for c, s in zip(host_codes, host_scales)) * n_layers
+
+        def one_step() -> None:
+            # Layer-pipelined: H2D of layer i+1 on a copy stream overlaps the
+            # quantisation and D2H of layer i on the compute stream.
+            compute = torch.cuda.current_stream(dev)
+            staged = [t.to(dev, non_blocking=True) for t in host_in]
+            for layer in range(n_layers):
+                ready = torch.cuda.Event()
+                ready.record(compute)
+                outs = cf.quantize_int8_many(staged)
+                if layer + 1 < n_layers:
+                    copy_stream.wait_stream(compute)
+                    with torch.cuda.stream(copy_stream):
+                        nxt = [t.to(dev, non_blocking=True) for t in host_in]
+                    compute.wait_stream(copy_stream)
+                    staged = nxt
+                for (c, s), hc, hs in zip(outs, host_codes, host_scales):
+                    hc.copy_(c, non_blocking=True)
+                    hs.copy_(s, non_blocking=True)
+
+        one_step()
+        torch.cuda.synchronize(dev)
+        self.dist.barrier()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            one_step()
+        torch.cuda.synchronize(dev)
+        self.dist.barrier()
+        elapsed = self.dist.max(time.perf_counter() - t0)
+        total_bytes = self.dist.sum(self.work_per_step) * steps
+        return {
+            "value": total_bytes / elapsed / 1e9,
+            "unit": self.unit,
+            "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(d2h),
+            "steps": steps,
+            "api": "cuda_force_b200.quantize_int8_many per layer, pinned host in/out",
+            "note": "each layer's host source is one pinned layer-sized buffer re-sent per layer",
+        }
+
+    # -- CPU: the reference's own CPU implementation --------------------------
+    def cpu_sample(self):
+        """(fn, algorithmic bytes per call, kind, description) for the reference CPU path."""
+        x = self.inputs[0].cpu()  # one [4096, 4096] bf16 projection
+        fn, kind = reference_quantize_fn()
+
+        def run() -> None:
+            fn(x)
+
+        return (run, BYTES_PER_ELEM_BF16_QUANT * x.numel(), kind,
+                "one 4096x4096 bf16 projection of layer 0 per call")
+
+
+def reference_quantize_fn():
+    """The reference's CPU quantiser: its compiled CPU operator if built, else the port."""
+    from oracle import build_ref
+
+    if build_ref.load():
+        return (lambda x: torch.ops.cudaforge_ref.quantize_int8(x)), "reference"
+    from oracle import quant_ref
+
+    return (lambda x: quant_ref.quantize(x.view(torch.int16).numpy().view("uint16")
+                                         if x.dtype == torch.bfloat16 else x.numpy())), "port"
+
+
+class Config1Quant:
+    """fp32 [4096, 4096] N(0,1) block-INT8 quantise (or dequantise)."""
+
+    name = "config1_quant_f32"
+    unit = "GB/s"
+    bound = "hbm"
+    scaling = "weak"
+    flush_l2 = True
+    dequant = False
+
+    def __init__(self, dist: Dist, _layers: int = 0):
+        self.dist = dist
+        op = "dequantise" if self.dequant else "quantise"
+        self.metric = f"INT8 block {op} GB/s (fp32 4096x4096)"
+        self.dtype = "int8->f32" if self.dequant else "f32->int8"
+        self.kernel = "dequantize_vec_kernel" if self.dequant else "quantize_tma_kernel<f32>"
+
+    def config(self) -> dict:
+        return {"workload": f"BASELINE config 1: fp32 [4096,4096] N(0,1) block-64 "
+                            f"{'dequantise' if self.dequant else 'quantise'}",
+                "block": 64, "bytes_per_element": 4 + 1 + 4 / 64,
+                "l2": "flushed between steps (256 MiB write outside the timed events)",
+                "parallelism": f"{self.dist.world} independent replica(s)"}
+
+    def setup(self) -> None:
+        from cuda_force_b200 import _abi
+
+        dev = self.dist.device
+        self.lib = _abi.load()
+        g = torch.Generator(device=dev).manual_seed(1)
+        self.x = torch.randn(4096, 4096, device=dev, generator=g)
+        self.codes = torch.empty(4096, 4096, dtype=torch.int8, device=dev)
+        self.scales = torch.empty(4096 * 64, device=dev)
+        self.out = torch.empty(4096, 4096, device=dev)
+        _abi.check(self.lib.cf_quantize_int8(self.x.data_ptr(), 0, self.codes.data_ptr(),
+                                             self.scales.data_ptr(), self.x.numel(), None), "q")
+        self.work_per_step = (4 + 1 + 4 / 64) * self.x.numel()
+        self.launches_per_step = 1
+
+    def step(self, stream) -> None:
+        from cuda_force_b200 import _abi
+
+        if self.dequant:
+            st = self.lib.cf_dequantize_int8(self.codes.data_ptr(), self.scales.data_ptr(),
+                                             self.out.data_ptr(), self.x.numel(), stream.cuda_stream)
+        else:
+            st = self.lib.cf_quantize_int8(self.x.data_ptr(), 0, self.codes.data_ptr(),
+                                           self.scales.data_ptr(), self.x.numel(), stream.cuda_stream)
+        _abi.check(st, self.name)
+
+    def verify(self) -> None:
+        from oracle import quant_ref
+
+        rc, rs = quant_ref.quantize(self.x.cpu().numpy())
+        assert (self.codes.cpu().numpy().reshape(-1) == rc).all(), "codes differ from oracle"
+        if self.dequant:
+            ref = quant_ref.dequantize(rc, rs)
+            assert (self.out.cpu().numpy().reshape(-1) == ref).all(), "dequant differs"
+
+    def e2e(self, steps: int) -> dict:
+        import cuda_force_b200 as cf
+
+        dev = self.dist.device
+        if self.dequant:
+            h_in = [self.codes.cpu().pin_memory(), self.scales.cpu().pin_memory()]
+            h_out = torch.empty(4096, 4096).pin_memory()
+        else:
+            h_in = [self.x.cpu().pin_memory()]
+            h_out = [torch.empty(4096, 4096, dtype=torch.int8).pin_memory(),
+                     torch.empty(4096 * 64).pin_memory()]
+
+        def one():
+            d = [t.to(dev, non_blocking=True) for t in h_in]
+            if self.dequant:
+                h_out.copy_(cf.dequantize_int8(*d), non_blocking=True)
+            else:
+                c, s = cf.quantize_int8(d[0])
+                h_out[0].copy_(c, non_blocking=True)
+                h_out[1].copy_(s, non_blocking=True)
+
+        h2d = sum(t.numel() * t.element_size() for t in h_in)
+        d2h = (h_out.numel() * 4 if self.dequant
+               else sum(t.numel() * t.element_size() for t in h_out))
+        return timed_e2e(self, one, steps, h2d, d2h, "cuda_force_b200.(de)quantize_int8")
+
+    def cpu_sample(self):
+        x = self.x.cpu()
+        from oracle import build_ref
+
+        if build_ref.load():
+            kind = "reference"
+            if self.dequant:
+                c, s = torch.ops.cudaforge_ref.quantize_int8(x)
+                fn = lambda: torch.ops.cudaforge_ref.dequantize_int8(c, s)  # noqa: E731
+            else:
+                fn = lambda: torch.ops.cudaforge_ref.quantize_int8(x)  # noqa: E731
+        else:
+            from oracle import quant_ref
+
+            kind = "port"
+            fn = lambda: quant_ref.quantize(x.numpy())  # noqa: E731
+        return fn, self.work_per_step, kind, "the full 4096x4096 tensor per call"
+
+
+class Config1Dequant(Config1Quant):
+    name = "config1_dequant_f32"
+    dequant = True
+
+
+def timed_e2e(wl, one_step, steps: int, h2d: int, d2h: int, api: str) -> dict:
+    dev = wl.dist.device
+    one_step()
+    torch.cuda.synchronize(dev)
+    wl.dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        one_step()
+    torch.cuda.synchronize(dev)
+    wl.dist.barrier()
+    elapsed = wl.dist.max(time.perf_counter() - t0)
+    total = wl.dist.sum(wl.work_per_step) * steps
+    scale = 1e9 if wl.unit == "GB/s" else 1e12
+    return {"value": total / elapsed / scale, "unit": wl.unit, "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(d2h), "steps": steps, "api": api}
+
+
+class LoraLinear:
+    """BASELINE config 3 (bf16 LoRA linear) and config 4 (W8 + LoRA, decode / prefill)."""
+
+    name = "lora_bf16_8192x4096x4096"
+    unit = "TFLOP/s"
+    bound = "tensor"
+    scaling = "weak"
+    flush_l2 = True
+    m, k, n, r, alpha = 8192, 4096, 4096, 16, 32.0
+    int8 = False
+    x_std, w_std, ab_std = 1.0, 0.02, 0.01
+
+    def __init__(self, dist: Dist, _layers: int = 0):
+        self.dist = dist
+        self.metric = (f"{'W8+LoRA' if self.int8 else 'LoRA'} linear "
+                       f"{'GB/s' if self.unit == 'GB/s' else 'TFLOP/s'} "
+                       f"(x [{self.m},{self.k}], W [{self.n},{self.k}], r {self.r})")
+        self.dtype = "bf16 x int8->bf16 (fp32 acc)" if self.int8 else "bf16 (fp32 acc)"
+        self.kernel = "lora_gemm_kernel (down-projection + main, one call)"
+
+    def flops(self) -> float:
+        return 2.0 * self.m * self.n * self.k + 2.0 * self.m * self.r * (self.k + self.n)
+
+    def bytes(self) -> float:
+        w = self.n * self.k * (1 + 4 / 64) if self.int8 else self.n * self.k * 2
+        return w + 2 * (self.m * self.k + self.k * self.r + self.r * self.n + self.m * self.n)
+
+    def config(self) -> dict:
+        return {"workload": self.__doc__.strip().splitlines()[0] + f" [{self.name}]",
+                "m": self.m, "k": self.k, "n": self.n, "rank": self.r, "alpha": self.alpha,
+                "weight": "block-64 int8 codes + fp32 scales" if self.int8 else "bf16 [out, in]",
+                "l2": "flushed between steps (256 MiB write outside the timed events)",
+                "parallelism": f"{self.dist.world} independent replica(s)"}
+
+    def setup(self) -> None:
+        import cuda_force_b200 as cf
+
+        dev = self.dist.device
+        g = torch.Generator(device=dev).manual_seed(3)
+        self.x = (torch.randn(self.m, self.k, device=dev, generator=g) * self.x_std).to(torch.bfloat16)
+        w = (torch.randn(self.n, self.k, device=dev, generator=g) * self.w_std).to(torch.bfloat16)
+        self.a = (torch.randn(self.k, self.r, device=dev, generator=g) * self.ab_std).to(torch.bfloat16)
+        self.b = (torch.randn(self.r, self.n, device=dev, generator=g) * self.ab_std).to(torch.bfloat16)
+        if self.int8:
+            self.codes, self.scales = cf.quantize_int8(w)
+            self.w = None
+        else:
+            self.w = w
+        self.scale = self.alpha / self.r
+        from cuda_force_b200 import _abi
+
+        self.lib = _abi.load()
+        self.y = torch.empty(self.m, self.n, dtype=torch.bfloat16, device=dev)
+        self.ws_bytes = self.lib.cf_lora_linear_workspace_bytes(self.m, self.r)
+        self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=dev)
+        self.work_per_step = self.bytes() if self.unit == "GB/s" else self.flops()
+        self.launches_per_step = 2
+
+    def step(self, stream) -> None:
+        from cuda_force_b200 import _abi
+
+        if self.int8:
+            st = self.lib.cf_lora_linear_int8(
+                self.x.data_ptr(), self.codes.data_ptr(), self.scales.data_ptr(), self.a.data_ptr(),
+                _abi.CF_LAYOUT_REF, self.b.data_ptr(), _abi.CF_LAYOUT_REF, self.y.data_ptr(),
+                self.m, self.k, self.n, self.r, self.scale, _abi.CF_DTYPE_BF16, self.ws.data_ptr(),
+                self.ws_bytes, stream.cuda_stream)
+        else:
+            st = self.lib.cf_lora_linear(
+                self.x.data_ptr(), self.w.data_ptr(), _abi.CF_LAYOUT_T, self.a.data_ptr(),
+                _abi.CF_LAYOUT_REF, self.b.data_ptr(), _abi.CF_LAYOUT_REF, self.y.data_ptr(),
+                self.m, self.k, self.n, self.r, self.scale, _abi.CF_DTYPE_BF16, self.ws.data_ptr(),
+                self.ws_bytes, stream.cuda_stream)
+        _abi.check(st, self.name)
+
+    def _w_t(self):
+        from oracle import linear_ref
+
+        if self.int8:
+            return linear_ref.dequantized_weight_t(self.codes, self.scales)
+        return self.w.t()
+
+    def verify(self) -> None:
+        from oracle import linear_ref
+
+        rows = torch.randperm(self.m, generator=torch.Generator().manual_seed(0))[:128]
+        rows = rows.to(self.x.device)
+        ref = linear_ref.lora_linear(self.x[rows], self._w_t(), self.a, self.b, self.scale)
+        err = linear_ref.max_rel_error(self.y[rows], ref)
+        assert err <= 2e-2, f"{self.name}: max relative error {err}"
+
+    def e2e(self, steps: int) -> dict:
+        import cuda_force_b200 as cf
+
+        dev = self.dist.device
+        hx = self.x.cpu().pin_memory()
+        hy = torch.empty(self.m, self.n, dtype=torch.bfloat16).pin_memory()
+
+        def one():
+            x = hx.to(dev, non_blocking=True)
+            if self.int8:
+                y = cf.lora_linear_int8(x, self.codes, self.scales, self.a, self.b, self.scale)
+            else:
+                y = cf.lora_linear(x, self.w.t(), self.a, self.b, self.scale)
+            hy.copy_(y, non_blocking=True)
+
+        return timed_e2e(self, one, steps, hx.numel() * 2, hy.numel() * 2,
+                         "cuda_force_b200.lora_linear%s (weights resident, x in / y out)"
+                         % ("_int8" if self.int8 else ""))
+
+    def cpu_sample(self):
+        from oracle import build_ref
+
+        rows = min(self.m, 256)
+        x = self.x[:rows].float().cpu()
+        a, b = self.a.float().cpu(), self.b.float().cpu()
+        have_ref = build_ref.load()
+        kind = "reference" if have_ref else "port"
+        if self.int8:
+            codes, scales = self.codes.cpu(), self.scales.cpu()
+        else:
+            w_t = self.w.float().cpu().t().contiguous()
+
+        def fn():
+            if self.int8:
+                wt = (torch.ops.cudaforge_ref.dequantize_int8(codes, scales) if have_ref
+                      else codes.float()).reshape(self.n, self.k).t()
+            else:
+                wt = w_t
+            if have_ref:
+                torch.ops.cudaforge_ref.lora_linear(x, wt, a, b, self.scale)
+            else:
+                x @ wt + self.scale * ((x @ a) @ b)
+
+        work = self.work_per_step * rows / self.m
+        if self.unit == "GB/s":
+            work = self.work_per_step  # decode: the sample is the whole problem
+        return fn, work, kind, (f"{rows} of {self.m} rows in fp32 through the reference's CPU "
+                                f"{'dequantize_int8 + ' if self.int8 else ''}lora_linear")
+
+
+class W8Decode(LoraLinear):
+    """BASELINE config 4 decode: W8 + LoRA, x [32, 4096], W [11008, 4096] int8."""
+
+    name = "w8_lora_decode_32x4096x11008"
+    unit = "GB/s"
+    bound = "hbm"
+    m, k, n, r = 32, 4096, 11008, 16
+    int8 = True
+
+
+class W8Prefill(LoraLinear):
+    """BASELINE config 4 prefill: W8 + LoRA, x [4096, 4096], W [11008, 4096] int8."""
+
+    name = "w8_lora_prefill_4096x4096x11008"
+    m, k, n, r = 4096, 4096, 11008, 16
+    int8 = True
+
+
+WORKLOADS = {w.name: w for w in (LlamaStackQuant, Config1Quant, Config1Dequant, LoraLinear,
+                                W8Decode, W8Prefill)}
+
+
+# ---------------------------------------------------------------------------
+# Runs
+# ---------------------------------------------------------------------------
+def time_cpu(fn, min_seconds: float = 10.0, max_calls: int = 50) -> float:
+    fn()  # warm-up
+    times = []
+    t_start = time.perf_counter()
+    while len(times) < 3 or (time.perf_counter() - t_start < min_seconds and len(times) < max_calls):
+        t0 = time.perf_counter()
+        fn()
+        times.append(time.perf_counter() - t0)
+    return statistics.median(times)
+
+
+def run_ours(args, dist: Dist) -> dict | None:
+    wl = WORKLOADS[args.workload](dist, args.layers)
+    torch.cuda.set_device(dist.device)
+    wl.setup()
+    stream = torch.cuda.Stream(device=dist.device)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dist.device) if wl.flush_l2 else None
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            wl.step(stream)
+    torch.cuda.synchronize(dist.device)
+    wl.verify()
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    dist.barrier()
+    torch.cuda.synchronize(dist.device)
+    with ClockSampler(dist.local_rank) as clocks:
+        with torch.cuda.stream(stream):
+            for i in range(args.steps):
+                if flush is not None:
+                    flush.fill_(i & 0xFF)  # evict L2 outside the timed events
+                starts[i].record(stream)
+                wl.step(stream)
+                ends[i].record(stream)
+        torch.cuda.synchronize(dist.device)
+    dist.barrier()
+    per_step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    if flush is not None:
+        total_ms = sum(per_step_ms)
+    else:
+        total_ms = starts[0].elapsed_time(ends[-1])
+    total_ms = dist.max(total_ms)
+    scale = 1e9 if wl.unit == "GB/s" else 1e12
+    work_all = dist.sum(wl.work_per_step) * args.steps
+    value = work_all / (total_ms * 1e-3) / scale
+
+    peaks, peak_src = load_peaks()
+    step_ms = statistics.mean(per_step_ms)
+    achieved = wl.work_per_step / (step_ms * 1e-3) / scale
+    if wl.bound == "hbm":
+        peak, peak_key, peak_unit = peaks["hbm_gbs"], "hbm_gbs", "GB/s"
+    else:
+        peak, peak_key, peak_unit = peaks["bf16_tflops"], "bf16_tflops (burst)", "TFLOP/s"
+    traffic_info = load_traffic().get(wl.name)
+    traffic = traffic_info.get("dram_bytes_per_step") if traffic_info else None
+
+    e2e = wl.e2e(max(1, min(args.steps, args.e2e_steps)))
+
+    cpu = None
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        fn, work, kind, sample = wl.cpu_sample()
+        t = time_cpu(fn)
+        cpu = {"value": work / t / scale, "unit": wl.unit, "cores": torch.get_num_threads(),
+               "kind": kind, "sample": sample + ", median of >=3 calls over ~10 s"}
+    result = {
+        "metric": wl.metric,
+        "value": round(value, 3),
+        "unit": wl.unit,
+        "n_gpus": dist.world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(total_ms / args.steps, 5),
+        "higher_is_better": True,
+        "scaling": wl.scaling,
+        "vs_baseline": None,
+        "dtype": wl.dtype,
+        "data": "synthetic (seeded on device)",
+        "config": wl.config(),
+        "roofline": {
+            "bound": wl.bound,
+            "kernel": wl.kernel,
+            "achieved": round(achieved, 2),
+            "peak": peak,
+            "peak_source": f"{peak_src} {peak_key}",
+            "unit": peak_unit,
+            "frac": round(achieved / peak, 4),
+            "traffic": traffic,
+            "algorithmic_per_launch_step": wl.work_per_step,
+            "launches_per_step": wl.launches_per_step,
+        },
+        "e2e": e2e,
+        "gpu_launches": wl.launches_per_step * args.steps,
+        "clocks": clocks.summary(),
+        "cpu_baseline": cpu,
+    }
+    return result if dist.rank == 0 else None
+
+
+def run_reference(args, dist: Dist) -> dict | None:
+    """The reference's own CPU implementation of the path on this host's cores."""
+    if dist.rank != 0:
+        return None
+    torch.cuda.set_device(dist.device)
+    torch.set_num_threads(os.cpu_count() or 1)
+    wl = WORKLOADS[args.workload](dist, args.layers)
+    if isinstance(wl, LlamaStackQuant):
+        # generate only the sampled projection (layer 0), not the whole stack
+        x = llama_layer_weights(0, dist.device)[0].cpu()
+        qfn, kind = reference_quantize_fn()
+        fn = lambda: qfn(x)  # noqa: E731
+        work = BYTES_PER_ELEM_BF16_QUANT * x.numel()
+        sample = "one 4096x4096 bf16 projection of layer 0 per step"
+    else:
+        wl.setup()
+        fn, work, kind, sample = wl.cpu_sample()
+    scale = 1e9 if wl.unit == "GB/s" else 1e12
+    for _ in range(max(1, args.warmup)):
+        fn()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        fn()
+        times.append(time.perf_counter() - t0)
+    value = work * len(times) / sum(times) / scale
+    return {
+        "impl": "reference",
+        "metric": wl.metric,
+        "value": round(value, 6),
+        "unit": wl.unit,
+        "n_gpus": dist.world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(1e3 * sum(times) / len(times), 3),
+        "higher_is_better": True,
+        "scaling": wl.scaling,
+        "vs_baseline": None,
+        "dtype": wl.dtype,
+        "data": "synthetic (seeded)",
+        "config": {**wl.config(), "reference_sample": sample},
+        "cpu_baseline": {"value": round(value, 6), "unit": wl.unit,
+                         "cores": torch.get_num_threads(), "kind": kind, "sample": sample},
+        "e2e": {"value": round(value, 6), "unit": wl.unit, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=100)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    parser.add_argument("--workload", choices=sorted(WORKLOADS), default=LlamaStackQuant.name)
+    parser.add_argument("--e2e-steps", type=int, default=2)
+    parser.add_argument("--layers", type=int, default=LLAMA7B_LAYERS,
+                        help="stack depth (default 32 = BASELINE config 2; smaller only "
+                             "for profiling captures)")
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    args = parser.parse_args()
+    if args.warmup < 3:
+        parser.error("--warmup must be >= 3")
+
+    dist = Dist(args.gpus)
+    try:
+        result = run_reference(args, dist) if args.impl == "reference" else run_ours(args, dist)
+    finally:
+        dist.close()
+    if result is not None:
+        print(json.dumps(result), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,51 @@
+// Shared host/device helpers for the sm_100a kernels: status plumbing, the
+// device-side error word, and small launch utilities.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "cudaforge_b200.h"
+
+namespace cfb {
+
+// Elements sharing one scale. Must equal QUANT_BLOCK_SIZE in
+// cuda_force_b200/ops.py; tests/test_host.py parses both.
+inline constexpr int kQuantBlockSize = 64;
+
+inline constexpr int kWarp = 32;
+
+// Device-side error word, one per device (file-scope __device__ variable in
+// abi.cu). A kernel whose bounded wait runs out ORs a code in and returns.
+enum DeviceError : unsigned {
+  kDevErrNone = 0u,
+  kDevErrTimeout = 1u,
+};
+
+// Sets the calling thread's last CUDA error and returns CF_ERR_CUDA.
+int record_cuda_error(cudaError_t err);
+
+// Checks the launch that was just issued. CF_OK or CF_ERR_CUDA.
+inline int check_launch() {
+  cudaError_t err = cudaGetLastError();
+  return err == cudaSuccess ? CF_OK : record_cuda_error(err);
+}
+
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+// Address of the current device's error word (cached per device).
+unsigned *device_error_word();
+
+inline bool aligned_to(const void *p, uintptr_t bytes) {
+  return (reinterpret_cast<uintptr_t>(p) & (bytes - 1)) == 0;
+}
+
+}  // namespace cfb
+
+#define CFB_TRY_CUDA(expr)                                   \
+  do {                                                       \
+    cudaError_t cfb_err_ = (expr);                           \
+    if (cfb_err_ != cudaSuccess) return ::cfb::record_cuda_error(cfb_err_); \
+  } while (0)

@@ -1,0 +1,649 @@
+// LoRA linear on the 5th-generation tensor cores (tcgen05 + TMEM + TMA), sm_100a.
+//
+//   y[m, n] = sum_k x[m,k] W[k,n] + scale * sum_j (sum_k x[m,k] A[k,j]) B[j,n]
+//
+// Semantics follow the reference's lora_linear (python/cudaforge/ops.py:178-185,
+// cpp/src/bindings.cpp:255-258, CUDA launcher cuda/src/lora_linear.cu:237-277);
+// the W8 variant computes lora_linear(x, dequantize_int8(codes, scales)^T, ...)
+// with the reference's dequantisation (bindings.cpp:320-329) applied in shared
+// memory: q * s in fp32 exactly as the dequantiser does, then rounded to the
+// activation dtype for the MMA.
+//
+// Two launches per call, both of the same persistent warp-specialised kernel:
+//   1. down-projection  P = scale * x A  -> workspace [M, r] (bf16/f16), tile N = r;
+//   2. main product     y = x W^T + P B  with the adapter folded into the MMA as
+//      r/16 extra K-steps at the end of every output tile (A operand = P tile,
+//      B operand = B slice), so the rank-r update costs no epilogue arithmetic.
+//
+// Kernel structure (one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer: x tile + W tile (or int8 code tile) per k-block
+//               into a kStages-deep shared-memory ring (mbarrier full/empty);
+//   warp 1      TMEM allocator and single-thread MMA issuer
+//               (tcgen05.mma.cta_group::1.kind::f16, 128 x BN x 16 per instruction);
+//   warps 4-7   epilogue: tcgen05.ld the fp32 accumulator (thread = output row),
+//               round to bf16/f16, store; double-buffered TMEM accumulators let
+//               the next tile's mainloop run under this epilogue;
+//   warps 8-15  (W8 only) converters: int8 codes -> q*s (fp32) -> bf16/f16 into
+//               the 128B-swizzled K-major operand layout the MMA reads.
+// Every mbarrier wait is bounded (2 s of global time); on expiry the kernel
+// records CF_ERR_DEVICE_TIMEOUT in the device error word and unwinds.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstring>
+
+#include "cf_common.cuh"
+#include "ptx.cuh"
+
+namespace cfb {
+namespace {
+
+constexpr int kBM = 128;        // tile rows (MMA M)
+constexpr int kBK = 64;         // k-block: 64 x 16-bit = one 128-byte swizzle row
+constexpr int kUmmaK = 16;      // K per tcgen05.mma (kind::f16)
+constexpr int kEpiWarp0 = 4;    // first epilogue warp (warp % 4 = TMEM lane quarter)
+constexpr int kConvWarp0 = 8;   // first converter warp (W8 only)
+constexpr int kConvThreads = 256;
+
+enum BSource : int { kBKMajor = 0, kBMNMajor = 1, kBInt8 = 2 };
+
+template <int BN, bool kInt8>
+struct GemmCfg {
+  static constexpr int kABytes = kBM * kBK * 2;                // 16 KB
+  static constexpr int kBBytes = (BN < 64 ? 64 : BN) * kBK * 2;  // >= 8 KB so extras fit
+  static constexpr int kRawBytes = kInt8 ? BN * kBK : 0;       // int8 code tile
+  static constexpr int kStageBytes = kABytes + kBBytes + kRawBytes;
+  static constexpr int kStages = kInt8 ? 3 : (BN >= 128 ? 4 : 8);
+  static constexpr int kThreads = kInt8 ? 512 : 256;
+  static constexpr int kTmemCols = (2 * BN) <= 32 ? 32 : (2 * BN) <= 64 ? 64
+                                   : (2 * BN) <= 128 ? 128 : (2 * BN) <= 256 ? 256 : 512;
+  static constexpr size_t kSmemBytes = 1024 /*alignment slack*/ +
+                                       static_cast<size_t>(kStages) * kStageBytes + 256;
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "MMA N");
+};
+
+struct GemmParams {
+  int M, N, K;
+  int num_kb;          // ceil(K / 64)
+  int extra_ksteps;    // adapter K-steps (rank / 16); 0 = none
+  int rank;            // adapter rank (16, 32 or 64)
+  int b_src;           // BSource of the main B operand
+  int extra_b_mn;      // adapter B operand stored MN-major ([rank, N])
+  int is_bf16;
+  float out_scale;     // multiplier applied in the epilogue
+  void *out;           // [M, ldo] row-major, 16-bit
+  int ldo;
+  const float *w_scales;  // W8: [N, K/64]
+  int kb_per_row;         // W8: K / 64
+  int n_tiles_n;
+  int n_tiles;
+  unsigned *err;
+};
+
+__device__ __forceinline__ uint32_t swizzle_for_row_bytes(int row_bytes) {
+  return row_bytes >= 128 ? ptx::kSwizzle128B : row_bytes == 64 ? ptx::kSwizzle64B
+                                                                 : ptx::kSwizzle32B;
+}
+
+// Shared-memory descriptor of a K-major operand whose rows are `row_bytes`
+// (32/64/128) long and swizzled at that width; 8-row core groups are
+// 8 * row_bytes apart. k-step `ks` (16 elements = 32 bytes) advances the start
+// address inside the swizzle atom.
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int row_bytes, int ks) {
+  return ptx::make_smem_desc(base + ks * 32, 16, 8 * row_bytes, swizzle_for_row_bytes(row_bytes));
+}
+
+// Descriptor of an MN-major operand stored as chunks of `chunk_elems` MN
+// elements (chunk_elems * 2 = row bytes, swizzled at that width) x k rows;
+// chunks are `chunk_stride` bytes apart. k-step `ks` = 16 rows further.
+__device__ __forceinline__ uint64_t mnmajor_desc(uint32_t base, int row_bytes, int chunk_stride,
+                                                 int ks) {
+  return ptx::make_smem_desc(base + ks * 16 * row_bytes, chunk_stride, 8 * row_bytes,
+                             swizzle_for_row_bytes(row_bytes));
+}
+
+__device__ __forceinline__ void record_timeout(unsigned *err, int *abort_flag) {
+  atomicOr(err, kDevErrTimeout);
+  *reinterpret_cast<volatile int *>(abort_flag) = 1;
+}
+
+__device__ __forceinline__ bool aborted(const int *abort_flag) {
+  return *reinterpret_cast<const volatile int *>(abort_flag) != 0;
+}
+
+template <int BN, bool kBf16, bool kInt8>
+__global__ void __launch_bounds__(GemmCfg<BN, kInt8>::kThreads, 1)
+    lora_gemm_kernel(const __grid_constant__ CUtensorMap tm_a,
+                     const __grid_constant__ CUtensorMap tm_b,
+                     const __grid_constant__ CUtensorMap tm_pa,
+                     const __grid_constant__ CUtensorMap tm_pb, const GemmParams p) {
+  using C = GemmCfg<BN, kInt8>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kStages * C::kStageBytes);
+  uint64_t *full = bars;                       // [kStages] TMA -> consumers
+  uint64_t *empty = bars + C::kStages;         // [kStages] MMA -> producer
+  uint64_t *conv_full = bars + 2 * C::kStages; // [kStages] converters -> MMA (W8)
+  uint64_t *tmem_full = bars + 3 * C::kStages; // [2] MMA -> epilogue
+  uint64_t *tmem_empty = tmem_full + 2;        // [2] epilogue -> MMA
+  uint64_t *drain = tmem_empty + 2;             // [1] MMA retirement on abort
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  int *abort_flag = reinterpret_cast<int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / kWarp;
+  const int lane = threadIdx.x % kWarp;
+  const int num_iters = p.num_kb + (p.extra_ksteps > 0 ? 1 : 0);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      ptx::mbar_init(&full[s], 1);
+      ptx::mbar_init(&empty[s], 1);
+      ptx::mbar_init(&conv_full[s], kConvThreads);
+    }
+    for (int a = 0; a < 2; ++a) {
+      ptx::mbar_init(&tmem_full[a], 1);
+      ptx::mbar_init(&tmem_empty[a], 4 * kWarp);
+    }
+    ptx::mbar_init(drain, 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    ptx::prefetch_tensor_map(&tm_a);
+    ptx::prefetch_tensor_map(&tm_b);
+    if (p.extra_ksteps > 0) {
+      ptx::prefetch_tensor_map(&tm_pa);
+      ptx::prefetch_tensor_map(&tm_pb);
+    }
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, C::kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t outstanding = 0, issue_parity = 0;
+      const int extra_a_bytes = kBM * p.rank * 2;
+      const int extra_b_bytes = BN * p.rank * 2;
+      for (int tile = blockIdx.x; tile < p.n_tiles && !aborted(abort_flag); tile += gridDim.x) {
+        const int m0 = (tile / p.n_tiles_n) * kBM;
+        const int n0 = (tile % p.n_tiles_n) * BN;
+        for (int it = 0; it < num_iters; ++it) {
+          if (!ptx::mbar_wait(&empty[stage], phase ^ 1)) {
+            record_timeout(p.err, abort_flag);
+            break;
+          }
+          uint8_t *sa = smem + stage * C::kStageBytes;
+          uint8_t *sb = sa + C::kABytes;
+          if (it < p.num_kb) {
+            const int k0 = it * kBK;
+            const int b_bytes = kInt8 ? C::kRawBytes : BN * kBK * 2;
+            ptx::mbar_expect_tx(&full[stage], C::kABytes + b_bytes);
+            ptx::tma_load_2d(sa, &tm_a, &full[stage], k0, m0);
+            if (kInt8) {
+              ptx::tma_load_2d(sb + C::kBBytes, &tm_b, &full[stage], k0, n0);
+            } else if (p.b_src == kBMNMajor) {
+              // chunks of min(BN, 64) columns x 64 k-rows, one swizzle row each
+              constexpr int kChunkCols = BN < 64 ? BN : 64;
+              for (int c = 0; c < BN / kChunkCols; ++c) {
+                ptx::tma_load_2d(sb + c * (kBK * kChunkCols * 2), &tm_b, &full[stage],
+                                 n0 + c * kChunkCols, k0);
+              }
+            } else {
+              ptx::tma_load_2d(sb, &tm_b, &full[stage], k0, n0);
+            }
+          } else {
+            ptx::mbar_expect_tx(&full[stage], extra_a_bytes + extra_b_bytes);
+            ptx::tma_load_2d(sa, &tm_pa, &full[stage], 0, m0);
+            if (p.extra_b_mn) {
+              for (int c = 0; c < BN / 64; ++c) {
+                ptx::tma_load_2d(sb + c * (p.rank * 128), &tm_pb, &full[stage], n0 + c * 64, 0);
+              }
+            } else {
+              ptx::tma_load_2d(sb, &tm_pb, &full[stage], 0, n0);
+            }
+          }
+          outstanding |= 1u << stage;
+          issue_parity = (issue_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (aborted(abort_flag)) {
+        // Let loads already issued land before the CTA's shared memory goes away.
+        for (int s = 0; s < C::kStages; ++s) {
+          if (outstanding & (1u << s)) ptx::mbar_wait(&full[s], (issue_parity >> s) & 1u, 200000000ull);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const bool bf16 = kBf16;
+      const uint32_t idesc_main = ptx::make_idesc_f16(bf16, kBM, BN, false, p.b_src == kBMNMajor);
+      const uint32_t idesc_extra = ptx::make_idesc_f16(bf16, kBM, BN, false, p.extra_b_mn != 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t conv_parity = 0;
+      int local = 0;
+      for (int tile = blockIdx.x; tile < p.n_tiles && !aborted(abort_flag);
+           tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
+        if (!ptx::mbar_wait(&tmem_empty[acc], acc_phase ^ 1)) {
+          record_timeout(p.err, abort_flag);
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int it = 0; it < num_iters; ++it) {
+          const bool main_kb = it < p.num_kb;
+          // conv_full[s] completes once per *main* k-block on stage s (the adapter
+          // block skips the converters), so its parity is tracked per stage.
+          const bool via_conv = kInt8 && main_kb;
+          const uint32_t want = via_conv ? (conv_parity >> stage) & 1u : phase;
+          if (via_conv) conv_parity ^= 1u << stage;
+          if (!ptx::mbar_wait(via_conv ? &conv_full[stage] : &full[stage], want)) {
+            record_timeout(p.err, abort_flag);
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint32_t sa = ptx::smem_addr(smem + stage * C::kStageBytes);
+          const uint32_t sb = sa + C::kABytes;
+          if (main_kb) {
+            for (int ks = 0; ks < kBK / kUmmaK; ++ks) {
+              const uint64_t adesc = kmajor_desc(sa, 128, ks);
+              constexpr int kChunkCols = BN < 64 ? BN : 64;
+              const uint64_t bdesc =
+                  (!kInt8 && p.b_src == kBMNMajor)
+                      ? mnmajor_desc(sb, kChunkCols * 2, kBK * kChunkCols * 2, ks)
+                      : kmajor_desc(sb, 128, ks);
+              ptx::mma_f16(d_tmem, adesc, bdesc, idesc_main, (it > 0 || ks > 0) ? 1u : 0u);
+            }
+          } else {
+            const int row_bytes = p.rank * 2;
+            for (int ks = 0; ks < p.extra_ksteps; ++ks) {
+              const uint64_t adesc = kmajor_desc(sa, row_bytes, ks);
+              const uint64_t bdesc = p.extra_b_mn ? mnmajor_desc(sb, 128, p.rank * 128, ks)
+                                                  : kmajor_desc(sb, row_bytes, ks);
+              ptx::mma_f16(d_tmem, adesc, bdesc, idesc_extra, (it > 0 || ks > 0) ? 1u : 0u);
+            }
+          }
+          ptx::mma_commit(&empty[stage]);
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        ptx::mma_commit(&tmem_full[acc]);
+      }
+      if (aborted(abort_flag)) {
+        // Retire MMAs still in flight before TMEM is released.
+        ptx::mma_commit(drain);
+        ptx::mbar_wait(drain, 0, 200000000ull);
+      }
+    }
+  } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) {
+    // ------------------------------------------------------------------ epilogue
+    const int quarter = warp % 4;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
+      const bool ok = ptx::mbar_wait(&tmem_full[acc], acc_phase);
+      if (__any_sync(0xffffffffu, !ok)) {
+        if (lane == 0) record_timeout(p.err, abort_flag);
+        break;
+      }
+      ptx::tc_fence_after();
+      const int m0 = (tile / p.n_tiles_n) * kBM;
+      const int n0 = (tile % p.n_tiles_n) * BN;
+      const int row = m0 + quarter * 32 + lane;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
+      uint16_t *out_row = static_cast<uint16_t *>(p.out) + static_cast<int64_t>(row) * p.ldo;
+      constexpr int kChunk = BN >= 32 ? 32 : 16;
+#pragma unroll 1
+      for (int c = 0; c < BN / kChunk; ++c) {
+        uint32_t v[32];
+        if constexpr (kChunk == 32) {
+          ptx::tmem_ld_32x32b_x32(t_row + c * 32, v);
+        } else {
+          ptx::tmem_ld_32x32b_x16(t_row + c * 16, v);
+        }
+        ptx::tmem_ld_wait();
+        uint32_t packed[kChunk / 2];
+#pragma unroll
+        for (int e = 0; e < kChunk / 2; ++e) {
+          const float lo = __uint_as_float(v[2 * e]) * p.out_scale;
+          const float hi = __uint_as_float(v[2 * e + 1]) * p.out_scale;
+          packed[e] = kBf16 ? ptx::pack_bf16x2(lo, hi) : ptx::pack_f16x2(lo, hi);
+        }
+        if (row < p.M) {
+          const int col0 = n0 + c * kChunk;
+#pragma unroll
+          for (int q = 0; q < kChunk / 8; ++q) {
+            if (col0 + q * 8 < p.N) {
+              *reinterpret_cast<uint4 *>(out_row + col0 + q * 8) =
+                  make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+            }
+          }
+        }
+      }
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(&tmem_empty[acc]);
+    }
+  } else if (kInt8 && warp >= kConvWarp0) {
+    // ------------------------------------------------------------------ converters
+    // Lane l of a converter warp handles row (group * 8 + l / 4) and 16-code
+    // chunk (l % 4) of the int8 tile; it writes 32 bytes (two 16-byte chunks)
+    // of the 128B-swizzled bf16 row: logical chunk c sits at c ^ (row % 8).
+    const int cw = warp - kConvWarp0;
+    const int sub_row = lane / 4;
+    const int chunk = lane % 4;
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x) {
+      const int n0 = (tile % p.n_tiles_n) * BN;
+      bool ok = true;
+      for (int it = 0; it < num_iters; ++it) {
+        if (it < p.num_kb) {
+          const bool got = ptx::mbar_wait(&full[stage], phase);
+          if (__any_sync(0xffffffffu, !got)) {
+            if (lane == 0) record_timeout(p.err, abort_flag);
+            ok = false;
+            break;
+          }
+          uint8_t *sb = smem + stage * C::kStageBytes + C::kABytes;
+          const uint8_t *raw = sb + C::kBBytes;
+#pragma unroll
+          for (int g = cw; g < BN / 8; g += (kConvThreads / kWarp)) {
+            const int r = g * 8 + sub_row;
+            const int n = n0 + r;
+            const float s = n < p.N ? __ldg(p.w_scales + static_cast<int64_t>(n) * p.kb_per_row + it)
+                                    : 0.0f;
+            const uint4 codes = *reinterpret_cast<const uint4 *>(raw + r * kBK + chunk * 16);
+            const uint32_t words[4] = {codes.x, codes.y, codes.z, codes.w};
+            uint32_t outw[8];
+#pragma unroll
+            for (int wd = 0; wd < 4; ++wd) {
+              const uint32_t u = words[wd] ^ 0x80808080u;
+              float f[4];
+#pragma unroll
+              for (int b = 0; b < 4; ++b) {
+                // 2^23 + (q + 128) as a float, minus (2^23 + 128): exactly q.
+                const float biased = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7440u | b));
+                f[b] = __fmul_rn(biased - 8388736.0f, s);
+              }
+              outw[2 * wd] = kBf16 ? ptx::pack_bf16x2(f[0], f[1]) : ptx::pack_f16x2(f[0], f[1]);
+              outw[2 * wd + 1] = kBf16 ? ptx::pack_bf16x2(f[2], f[3]) : ptx::pack_f16x2(f[2], f[3]);
+            }
+            uint8_t *dst_row = sb + r * 128;
+            const int sw = r & 7;
+            *reinterpret_cast<uint4 *>(dst_row + (((2 * chunk) ^ sw) << 4)) =
+                make_uint4(outw[0], outw[1], outw[2], outw[3]);
+            *reinterpret_cast<uint4 *>(dst_row + (((2 * chunk + 1) ^ sw) << 4)) =
+                make_uint4(outw[4], outw[5], outw[6], outw[7]);
+          }
+          ptx::fence_proxy_async_smem();
+          ptx::mbar_arrive(&conv_full[stage]);
+        }
+        if (++stage == C::kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!ok) break;
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side: tensor maps and launches.
+// ---------------------------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static std::atomic<EncodeTiledFn> cached{nullptr};
+  EncodeTiledFn fn = cached.load(std::memory_order_acquire);
+  if (fn != nullptr) return fn;
+  void *sym = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &sym, cudaEnableDefault, &q) !=
+          cudaSuccess ||
+      q != cudaDriverEntryPointSuccess || sym == nullptr) {
+    return nullptr;
+  }
+  fn = reinterpret_cast<EncodeTiledFn>(sym);
+  cached.store(fn, std::memory_order_release);
+  return fn;
+}
+
+CUtensorMapSwizzle swizzle_for(int inner_bytes) {
+  switch (inner_bytes) {
+    case 32: return CU_TENSOR_MAP_SWIZZLE_32B;
+    case 64: return CU_TENSOR_MAP_SWIZZLE_64B;
+    case 128: return CU_TENSOR_MAP_SWIZZLE_128B;
+    default: return CU_TENSOR_MAP_SWIZZLE_NONE;
+  }
+}
+
+// 2-D row-major tensor [outer, inner] with element size esize, box [box_outer, box_inner].
+int make_map(CUtensorMap *map, const void *base, int esize, int64_t inner, int64_t outer,
+             int box_inner, int box_outer, bool swizzle) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return record_cuda_error(cudaErrorNotSupported);
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(inner) * esize};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_outer)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType dt =
+      esize == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
+  const CUresult r = fn(map, dt, 2, const_cast<void *>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swizzle ? swizzle_for(box_inner * esize) : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? CF_OK : CF_ERR_UNSUPPORTED;
+}
+
+template <int BN, bool kBf16, bool kInt8>
+int launch_gemm(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &pa,
+                const CUtensorMap &pb, const GemmParams &params, cudaStream_t stream) {
+  using C = GemmCfg<BN, kInt8>;
+  auto kernel = lora_gemm_kernel<BN, kBf16, kInt8>;
+  CFB_TRY_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(C::kSmemBytes)));
+  const int grid = std::max(1, std::min(params.n_tiles, sm_count()));
+  kernel<<<grid, C::kThreads, C::kSmemBytes, stream>>>(a, b, pa, pb, params);
+  return check_launch();
+}
+
+size_t workspace_bytes(int64_t m, int64_t r) {
+  if (m <= 0 || r <= 0) return 0;
+  const size_t bytes = static_cast<size_t>(m) * static_cast<size_t>(r) * 2;
+  return (bytes + 255) & ~static_cast<size_t>(255);
+}
+
+struct LinearArgs {
+  const void *x;
+  const void *w;          // bf16/f16 weight, or int8 codes
+  int w_layout;           // CF_LAYOUT_REF ([K, N]) or CF_LAYOUT_T ([N, K]); int8: [N, K]
+  const float *w_scales;  // int8 only
+  const void *a;
+  int a_layout;
+  const void *b;
+  int b_layout;
+  void *y;
+  int64_t m, k, n, r;
+  float scale;
+  int dtype;
+  void *ws;
+  size_t ws_bytes;
+  bool int8;
+};
+
+template <int BN, bool kBf16>
+int launch_down_projection(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
+  CUtensorMap tm_x, tm_a;
+  if (int st = make_map(&tm_x, L.x, 2, L.k, L.m, kBK, kBM, true)) return st;
+  GemmParams p{};
+  p.M = static_cast<int>(L.m);
+  p.N = BN;
+  p.K = static_cast<int>(L.k);
+  p.num_kb = static_cast<int>((L.k + kBK - 1) / kBK);
+  p.rank = BN;
+  p.is_bf16 = kBf16;
+  p.out_scale = L.scale;
+  p.out = L.ws;
+  p.ldo = BN;
+  p.n_tiles_n = 1;
+  p.n_tiles = static_cast<int>((L.m + kBM - 1) / kBM);
+  p.err = err;
+  if (L.a_layout == CF_LAYOUT_REF) {
+    // a [K, r]: r contiguous -> MN-major B operand, one chunk of r columns.
+    if (int st = make_map(&tm_a, L.a, 2, BN, L.k, BN, kBK, true)) return st;
+    p.b_src = kBMNMajor;
+  } else {
+    // a^T [r, K]: K contiguous -> K-major B operand.
+    if (int st = make_map(&tm_a, L.a, 2, L.k, BN, kBK, BN, true)) return st;
+    p.b_src = kBKMajor;
+  }
+  return launch_gemm<BN, kBf16, false>(tm_x, tm_a, tm_x, tm_x, p, stream);
+}
+
+template <bool kBf16>
+int run_linear(const LinearArgs &L, cudaStream_t stream) {
+  unsigned *err = device_error_word();
+  if (err == nullptr) return record_cuda_error(cudaGetLastError());
+  int st = CF_OK;
+  switch (L.r) {
+    case 16: st = launch_down_projection<16, kBf16>(L, err, stream); break;
+    case 32: st = launch_down_projection<32, kBf16>(L, err, stream); break;
+    default: st = launch_down_projection<64, kBf16>(L, err, stream); break;
+  }
+  if (st != CF_OK) return st;
+
+  constexpr int BN = 256;
+  const int r = static_cast<int>(L.r);
+  CUtensorMap tm_x, tm_w, tm_p, tm_b;
+  if ((st = make_map(&tm_x, L.x, 2, L.k, L.m, kBK, kBM, true))) return st;
+  GemmParams p{};
+  if (L.int8) {
+    if ((st = make_map(&tm_w, L.w, 1, L.k, L.n, kBK, BN, false))) return st;
+    p.b_src = kBInt8;
+  } else if (L.w_layout == CF_LAYOUT_T) {
+    if ((st = make_map(&tm_w, L.w, 2, L.k, L.n, kBK, BN, true))) return st;
+    p.b_src = kBKMajor;
+  } else {
+    if ((st = make_map(&tm_w, L.w, 2, L.n, L.k, 64, kBK, true))) return st;
+    p.b_src = kBMNMajor;
+  }
+  if ((st = make_map(&tm_p, L.ws, 2, r, L.m, r, kBM, true))) return st;
+  if (L.b_layout == CF_LAYOUT_REF) {
+    // b [r, N]: N contiguous -> MN-major, chunks of 64 columns x r rows.
+    if ((st = make_map(&tm_b, L.b, 2, L.n, r, 64, r, true))) return st;
+    p.extra_b_mn = 1;
+  } else {
+    // b^T [N, r]: r contiguous -> K-major rows of r elements.
+    if ((st = make_map(&tm_b, L.b, 2, r, L.n, r, BN, true))) return st;
+    p.extra_b_mn = 0;
+  }
+  p.M = static_cast<int>(L.m);
+  p.N = static_cast<int>(L.n);
+  p.K = static_cast<int>(L.k);
+  p.num_kb = static_cast<int>((L.k + kBK - 1) / kBK);
+  p.extra_ksteps = r / kUmmaK;
+  p.rank = r;
+  p.is_bf16 = kBf16;
+  p.out_scale = 1.0f;
+  p.out = L.y;
+  p.ldo = static_cast<int>(L.n);
+  p.w_scales = L.w_scales;
+  p.kb_per_row = static_cast<int>(L.k / kBK);
+  p.n_tiles_n = static_cast<int>((L.n + BN - 1) / BN);
+  p.n_tiles = static_cast<int>((L.m + kBM - 1) / kBM) * p.n_tiles_n;
+  p.err = err;
+  if (L.int8) return launch_gemm<BN, kBf16, true>(tm_x, tm_w, tm_p, tm_b, p, stream);
+  return launch_gemm<BN, kBf16, false>(tm_x, tm_w, tm_p, tm_b, p, stream);
+}
+
+int validate_and_run(const LinearArgs &L, cf_stream_t stream) {
+  if (L.m < 0 || L.k < 0 || L.n < 0 || L.r < 0) return CF_ERR_INVALID_ARGUMENT;
+  if (L.m == 0 || L.n == 0) return CF_OK;
+  if (L.x == nullptr || L.w == nullptr || L.a == nullptr || L.b == nullptr || L.y == nullptr ||
+      (L.int8 && L.w_scales == nullptr)) {
+    return CF_ERR_INVALID_ARGUMENT;
+  }
+  if (L.dtype != CF_DTYPE_BF16 && L.dtype != CF_DTYPE_F16) return CF_ERR_UNSUPPORTED;
+  if (L.r != 16 && L.r != 32 && L.r != 64) return CF_ERR_UNSUPPORTED;
+  if (L.k == 0 || L.k % (L.int8 ? kBK : 8) != 0 || L.n % 8 != 0) return CF_ERR_UNSUPPORTED;
+  if ((L.w_layout != CF_LAYOUT_REF && L.w_layout != CF_LAYOUT_T) ||
+      (L.a_layout != CF_LAYOUT_REF && L.a_layout != CF_LAYOUT_T) ||
+      (L.b_layout != CF_LAYOUT_REF && L.b_layout != CF_LAYOUT_T)) {
+    return CF_ERR_INVALID_ARGUMENT;
+  }
+  if (L.m > INT32_MAX || L.n > INT32_MAX || L.k > INT32_MAX) return CF_ERR_UNSUPPORTED;
+  for (const void *ptr : {L.x, L.w, L.a, L.b, static_cast<const void *>(L.y)}) {
+    if (!aligned_to(ptr, 16)) return CF_ERR_MISALIGNED;
+  }
+  if (L.ws == nullptr || L.ws_bytes < workspace_bytes(L.m, L.r)) return CF_ERR_WORKSPACE;
+  if (!aligned_to(L.ws, 16)) return CF_ERR_MISALIGNED;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  return L.dtype == CF_DTYPE_BF16 ? run_linear<true>(L, s) : run_linear<false>(L, s);
+}
+
+}  // namespace
+}  // namespace cfb
+
+extern "C" {
+
+size_t cf_lora_linear_workspace_bytes(int64_t m, int64_t rank) {
+  return cfb::workspace_bytes(m, rank);
+}
+
+int cf_lora_linear(const void *x, const void *w, int w_layout, const void *a, int a_layout,
+                   const void *b, int b_layout, void *y, int64_t m, int64_t k, int64_t n,
+                   int64_t rank, float scale, int dtype, void *workspace, size_t workspace_bytes,
+                   cf_stream_t stream) {
+  cfb::LinearArgs L{x, w, w_layout, nullptr, a, a_layout, b, b_layout, y, m, k, n, rank,
+                    scale, dtype, workspace, workspace_bytes, false};
+  return cfb::validate_and_run(L, stream);
+}
+
+int cf_lora_linear_int8(const void *x, const int8_t *w_codes, const float *w_scales,
+                        const void *a, int a_layout, const void *b, int b_layout, void *y,
+                        int64_t m, int64_t k, int64_t n, int64_t rank, float scale, int dtype,
+                        void *workspace, size_t workspace_bytes, cf_stream_t stream) {
+  cfb::LinearArgs L{x, w_codes, CF_LAYOUT_T, w_scales, a, a_layout, b, b_layout, y, m, k, n,
+                    rank, scale, dtype, workspace, workspace_bytes, true};
+  if (w_scales != nullptr && !cfb::aligned_to(w_scales, 4)) return CF_ERR_MISALIGNED;
+  return cfb::validate_and_run(L, stream);
+}
+
+}  // extern "C"

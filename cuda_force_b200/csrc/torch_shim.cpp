@@ -1,0 +1,275 @@
+// PyTorch dispatcher shim over the C ABI.
+//
+// Registers the reference's operator schemas in the `cudaforge` namespace
+// (reference cpp/src/bindings.cpp:342-355), byte-identical for the three
+// hot-path ops, plus three additive ops. Only the CUDA key has kernels: there
+// is deliberately no CPU implementation, so a CPU tensor fails loudly in the
+// dispatcher instead of taking a silent host path. The Autograd key raises
+// (autogradNotImplementedFallback), as the reference does (bindings.cpp:369-377).
+//
+// Each impl validates like the reference's CUDA impl (TORCH_CHECK messages that
+// name the operand), allocates its outputs on the input's device, and launches
+// on PyTorch's current stream.
+#include <ATen/ATen.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+#include <torch/csrc/autograd/autograd_not_implemented_fallback.h>
+#include <torch/library.h>
+
+#include <vector>
+
+#include "cudaforge_b200.h"
+
+namespace {
+
+cf_stream_t current_stream() {
+  return reinterpret_cast<cf_stream_t>(at::cuda::getCurrentCUDAStream().stream());
+}
+
+void check_status(int status, const char *op) {
+  if (status == CF_OK) return;
+  if (status == CF_ERR_CUDA) {
+    TORCH_CHECK(false, op, ": ", cf_status_string(status), " (cudaError ", cf_last_cuda_error(),
+                ")");
+  }
+  TORCH_CHECK(false, op, ": ", cf_status_string(status));
+}
+
+int dtype_code(const at::Tensor &t, const char *name) {
+  switch (t.scalar_type()) {
+    case at::kFloat: return CF_DTYPE_F32;
+    case at::kHalf: return CF_DTYPE_F16;
+    case at::kBFloat16: return CF_DTYPE_BF16;
+    default:
+      TORCH_CHECK(false, name, " must be float32, float16 or bfloat16, got ", t.scalar_type());
+  }
+  return -1;
+}
+
+void check_contiguous(const at::Tensor &t, const char *name) {
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous; call .contiguous() first");
+}
+
+void check_cuda(const at::Tensor &t, const char *name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor (this build has no CPU path)");
+}
+
+// Storage order of a 2-D operand that is either contiguous (REF) or the
+// transpose of a contiguous tensor (T). Anything else is rejected.
+int layout_of(const at::Tensor &t, const char *name) {
+  TORCH_CHECK(t.dim() == 2, name, " must be 2-D, got ", t.dim(), " dimensions");
+  if (t.is_contiguous()) return CF_LAYOUT_REF;
+  if (t.t().is_contiguous()) return CF_LAYOUT_T;
+  TORCH_CHECK(false, name, " must be contiguous (or the transpose of a contiguous tensor)");
+  return -1;
+}
+
+// The kernels take ranks 16, 32 and 64 (the MMA's K granularity). A smaller
+// rank is zero-padded to the next of those, which leaves the product unchanged.
+int64_t padded_rank(int64_t r) {
+  TORCH_CHECK(r >= 1 && r <= 64, "rank must be between 1 and 64, got ", r);
+  return r <= 16 ? 16 : r <= 32 ? 32 : 64;
+}
+
+void pad_adapter(at::Tensor &a, at::Tensor &b, int &al, int &bl, int64_t r, int64_t rp) {
+  if (rp == r) return;
+  at::Tensor ap = at::zeros({a.size(0), rp}, a.options());
+  ap.narrow(1, 0, r).copy_(a);
+  at::Tensor bp = at::zeros({rp, b.size(1)}, b.options());
+  bp.narrow(0, 0, r).copy_(b);
+  a = ap;
+  b = bp;
+  al = CF_LAYOUT_REF;
+  bl = CF_LAYOUT_REF;
+}
+
+std::vector<at::Tensor> quantize_int8_cuda(const at::Tensor &input) {
+  check_cuda(input, "input");
+  check_contiguous(input, "input");
+  const int dtype = dtype_code(input, "input");
+  const c10::cuda::CUDAGuard guard(input.device());
+  const int64_t count = input.numel();
+  at::Tensor codes = at::empty(input.sizes(), input.options().dtype(at::kChar));
+  at::Tensor scales = at::empty({cf_quant_scale_count(count)}, input.options().dtype(at::kFloat));
+  check_status(cf_quantize_int8(input.data_ptr(), dtype, codes.data_ptr<int8_t>(),
+                                scales.data_ptr<float>(), count, current_stream()),
+               "quantize_int8");
+  return {codes, scales};
+}
+
+at::Tensor dequantize_int8_cuda(const at::Tensor &quantised, const at::Tensor &scales) {
+  check_cuda(quantised, "quantised");
+  check_cuda(scales, "scales");
+  TORCH_CHECK(quantised.scalar_type() == at::kChar, "quantised must be int8");
+  TORCH_CHECK(scales.scalar_type() == at::kFloat, "scales must be float32, got ",
+              scales.scalar_type());
+  check_contiguous(quantised, "quantised");
+  check_contiguous(scales, "scales");
+  const int64_t count = quantised.numel();
+  TORCH_CHECK(scales.numel() == cf_quant_scale_count(count), "expected ",
+              cf_quant_scale_count(count), " block scales, got ", scales.numel());
+  const c10::cuda::CUDAGuard guard(quantised.device());
+  at::Tensor out = at::empty(quantised.sizes(), scales.options());
+  check_status(cf_dequantize_int8(quantised.data_ptr<int8_t>(), scales.data_ptr<float>(),
+                                  out.data_ptr<float>(), count, current_stream()),
+               "dequantize_int8");
+  return out;
+}
+
+at::Tensor quantize_dequantize_cuda(const at::Tensor &input) {
+  check_cuda(input, "input");
+  check_contiguous(input, "input");
+  const int dtype = dtype_code(input, "input");
+  const c10::cuda::CUDAGuard guard(input.device());
+  at::Tensor out = at::empty(input.sizes(), input.options().dtype(at::kFloat));
+  check_status(cf_quantize_dequantize(input.data_ptr(), dtype, out.data_ptr<float>(),
+                                      input.numel(), current_stream()),
+               "quantize_dequantize");
+  return out;
+}
+
+std::vector<at::Tensor> quantize_int8_many_cuda(at::TensorList inputs) {
+  std::vector<at::Tensor> result;
+  if (inputs.empty()) return result;
+  const int dtype = dtype_code(inputs[0], "inputs[0]");
+  const c10::cuda::CUDAGuard guard(inputs[0].device());
+  std::vector<cf_quant_segment> segs;
+  segs.reserve(inputs.size());
+  result.reserve(2 * inputs.size());
+  for (const at::Tensor &t : inputs) {
+    check_cuda(t, "inputs[i]");
+    check_contiguous(t, "inputs[i]");
+    TORCH_CHECK(t.scalar_type() == inputs[0].scalar_type(), "all inputs must share one dtype");
+    TORCH_CHECK(t.device() == inputs[0].device(), "all inputs must be on one device");
+    at::Tensor codes = at::empty(t.sizes(), t.options().dtype(at::kChar));
+    at::Tensor scales = at::empty({cf_quant_scale_count(t.numel())}, t.options().dtype(at::kFloat));
+    segs.push_back({t.data_ptr(), codes.data_ptr<int8_t>(), scales.data_ptr<float>(), t.numel()});
+    result.push_back(codes);
+    result.push_back(scales);
+  }
+  check_status(cf_quantize_int8_many(segs.data(), static_cast<int>(segs.size()), dtype,
+                                     current_stream()),
+               "quantize_int8_many");
+  return result;
+}
+
+// Shapes are those of the reference op: x [M, K], w [K, N], a [K, r], b [r, N]
+// (reference cpp/src/bindings.cpp:94-127). w, a and b may also be transposed
+// views of contiguous tensors, which is how nn.Linear-layout weights arrive.
+at::Tensor lora_linear_cuda(const at::Tensor &x, const at::Tensor &w, const at::Tensor &a,
+                            const at::Tensor &b, double scale) {
+  for (const auto &[t, name] : std::vector<std::pair<at::Tensor, const char *>>{
+           {x, "x"}, {w, "w"}, {a, "a"}, {b, "b"}}) {
+    check_cuda(t, name);
+  }
+  TORCH_CHECK(x.dim() == 2, "x must be 2-D, got ", x.dim(), " dimensions");
+  check_contiguous(x, "x");
+  const int dtype = dtype_code(x, "x");
+  TORCH_CHECK(dtype != CF_DTYPE_F32,
+              "lora_linear: float32 inputs are not supported by the tensor-core path; "
+              "pass bfloat16 or float16");
+  for (const at::Tensor *t : {&w, &a, &b}) {
+    TORCH_CHECK(t->scalar_type() == x.scalar_type(), "x, w, a and b must share one dtype");
+  }
+  const int wl = layout_of(w, "w");
+  const int al = layout_of(a, "a");
+  const int bl = layout_of(b, "b");
+  const int64_t m = x.size(0), k = x.size(1), n = w.size(1), r = a.size(1);
+  TORCH_CHECK(w.size(0) == k, "w must be [in_features, out_features]; got [", w.size(0), ", ",
+              w.size(1), "] for in_features=", k);
+  TORCH_CHECK(a.size(0) == k, "a must be [in_features, rank]; got [", a.size(0), ", ", a.size(1),
+              "] for in_features=", k);
+  TORCH_CHECK(b.size(0) == r && b.size(1) == n, "b must be [rank, out_features] = [", r, ", ", n,
+              "]; got [", b.size(0), ", ", b.size(1), "]");
+  const c10::cuda::CUDAGuard guard(x.device());
+  at::Tensor ap = a, bp = b;
+  int alp = al, blp = bl;
+  const int64_t rp = padded_rank(r);
+  pad_adapter(ap, bp, alp, blp, r, rp);
+  at::Tensor y = at::empty({m, n}, x.options());
+  const size_t ws_bytes = cf_lora_linear_workspace_bytes(m, rp);
+  at::Tensor ws = at::empty({static_cast<int64_t>(ws_bytes)}, x.options().dtype(at::kByte));
+  check_status(cf_lora_linear(x.data_ptr(), w.data_ptr(), wl, ap.data_ptr(), alp, bp.data_ptr(),
+                              blp, y.data_ptr(), m, k, n, rp, static_cast<float>(scale), dtype,
+                              ws.data_ptr(), ws_bytes, current_stream()),
+               "lora_linear");
+  return y;
+}
+
+// x [M, K]; w_codes int8 [N, K] (nn.Linear layout, blocks of 64 along K);
+// w_scales float32 [N*K/64]; a [K, r]; b [r, N].
+at::Tensor lora_linear_int8_cuda(const at::Tensor &x, const at::Tensor &w_codes,
+                                 const at::Tensor &w_scales, const at::Tensor &a,
+                                 const at::Tensor &b, double scale) {
+  for (const auto &[t, name] : std::vector<std::pair<at::Tensor, const char *>>{
+           {x, "x"}, {w_codes, "w_codes"}, {w_scales, "w_scales"}, {a, "a"}, {b, "b"}}) {
+    check_cuda(t, name);
+  }
+  TORCH_CHECK(x.dim() == 2, "x must be 2-D, got ", x.dim(), " dimensions");
+  check_contiguous(x, "x");
+  const int dtype = dtype_code(x, "x");
+  TORCH_CHECK(dtype != CF_DTYPE_F32, "lora_linear_int8: x must be bfloat16 or float16");
+  TORCH_CHECK(a.scalar_type() == x.scalar_type() && b.scalar_type() == x.scalar_type(),
+              "x, a and b must share one dtype");
+  TORCH_CHECK(w_codes.scalar_type() == at::kChar, "w_codes must be int8");
+  TORCH_CHECK(w_scales.scalar_type() == at::kFloat, "w_scales must be float32");
+  TORCH_CHECK(w_codes.dim() == 2, "w_codes must be 2-D [out_features, in_features]");
+  check_contiguous(w_codes, "w_codes");
+  check_contiguous(w_scales, "w_scales");
+  const int al = layout_of(a, "a");
+  const int bl = layout_of(b, "b");
+  const int64_t m = x.size(0), k = x.size(1), n = w_codes.size(0), r = a.size(1);
+  TORCH_CHECK(w_codes.size(1) == k, "w_codes must be [out_features, in_features]; got [",
+              w_codes.size(0), ", ", w_codes.size(1), "] for in_features=", k);
+  TORCH_CHECK(w_scales.numel() == cf_quant_scale_count(n * k), "expected ",
+              cf_quant_scale_count(n * k), " block scales, got ", w_scales.numel());
+  TORCH_CHECK(a.size(0) == k, "a must be [in_features, rank]; got [", a.size(0), ", ", a.size(1),
+              "] for in_features=", k);
+  TORCH_CHECK(b.size(0) == r && b.size(1) == n, "b must be [rank, out_features] = [", r, ", ", n,
+              "]; got [", b.size(0), ", ", b.size(1), "]");
+  const c10::cuda::CUDAGuard guard(x.device());
+  at::Tensor ap = a, bp = b;
+  int alp = al, blp = bl;
+  const int64_t rp = padded_rank(r);
+  pad_adapter(ap, bp, alp, blp, r, rp);
+  at::Tensor y = at::empty({m, n}, x.options());
+  const size_t ws_bytes = cf_lora_linear_workspace_bytes(m, rp);
+  at::Tensor ws = at::empty({static_cast<int64_t>(ws_bytes)}, x.options().dtype(at::kByte));
+  check_status(cf_lora_linear_int8(x.data_ptr(), w_codes.data_ptr<int8_t>(),
+                                   w_scales.data_ptr<float>(), ap.data_ptr(), alp, bp.data_ptr(),
+                                   blp, y.data_ptr(), m, k, n, rp, static_cast<float>(scale), dtype,
+                                   ws.data_ptr(), ws_bytes, current_stream()),
+               "lora_linear_int8");
+  return y;
+}
+
+}  // namespace
+
+TORCH_LIBRARY(cudaforge, m) {
+  // Byte-identical to the reference (cpp/src/bindings.cpp:344, 352-353).
+  m.def("lora_linear(Tensor x, Tensor w, Tensor a, Tensor b, float scale) -> Tensor");
+  m.def("quantize_int8(Tensor input) -> Tensor[]");
+  m.def("dequantize_int8(Tensor quantised, Tensor scales) -> Tensor");
+  // Additive.
+  m.def(
+      "lora_linear_int8(Tensor x, Tensor w_codes, Tensor w_scales, Tensor a, Tensor b, "
+      "float scale) -> Tensor");
+  m.def("quantize_dequantize(Tensor input) -> Tensor");
+  m.def("quantize_int8_many(Tensor[] inputs) -> Tensor[]");
+}
+
+TORCH_LIBRARY_IMPL(cudaforge, Autograd, m) {
+  for (const char *name : {"lora_linear", "quantize_int8", "dequantize_int8", "lora_linear_int8",
+                           "quantize_dequantize", "quantize_int8_many"}) {
+    m.impl(name, torch::autograd::autogradNotImplementedFallback());
+  }
+}
+
+TORCH_LIBRARY_IMPL(cudaforge, CUDA, m) {
+  m.impl("lora_linear", &lora_linear_cuda);
+  m.impl("quantize_int8", &quantize_int8_cuda);
+  m.impl("dequantize_int8", &dequantize_int8_cuda);
+  m.impl("lora_linear_int8", &lora_linear_int8_cuda);
+  m.impl("quantize_dequantize", &quantize_dequantize_cuda);
+  m.impl("quantize_int8_many", &quantize_int8_many_cuda);
+}

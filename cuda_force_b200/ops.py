@@ -1,0 +1,235 @@
+"""Operator API of the quantised-linear hot path, mirroring ``cudaforge.ops``.
+
+Same function names, argument meaning and ``ValueError`` messages as the
+reference wrapper (python/cudaforge/ops.py: ``QUANT_BLOCK_SIZE`` :41,
+``lora_linear`` :289-332, ``quantize_int8`` :449-460, ``dequantize_int8``
+:463-476, ``quantization_error`` :479-488, ``backend_report`` :109-122), with
+three differences that are deliberate:
+
+* there is no host fallback. The reference drops to an ATen composition when
+  the extension is absent, the tensor is on the CPU, the dtype is not float32,
+  or autograd is needed. Here every call runs the sm_100a kernels through
+  ``torch.ops.cudaforge``; a CPU tensor, a missing extension or a
+  grad-requiring input raises instead of silently changing implementation;
+* bfloat16 and float16 reach the kernels (the reference gates its CUDA path on
+  float32, ops.py:329 and :457);
+* ``lora_linear`` accepts ``weight``/``lora_a``/``lora_b`` either contiguous in
+  the reference's layout or as the transpose of a contiguous tensor (the
+  nn.Linear / ``training/lora.py`` storage), without copying.
+
+Additive ops: ``lora_linear_int8`` (W as block-INT8 codes + scales),
+``quantize_dequantize`` (fake quantisation) and ``quantize_int8_many``.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from pathlib import Path
+
+import torch
+
+# Block size for int8 quantisation. Must match kQuantBlockSize in
+# cuda_force_b200/csrc/cf_common.cuh and CF_QUANT_BLOCK_SIZE in
+# include/cudaforge_b200.h.
+QUANT_BLOCK_SIZE = 64
+
+_SHIM = Path(__file__).resolve().parent / "_C.so"
+
+
+def _load_extension() -> tuple[bool, str]:
+    if not _SHIM.exists():
+        return False, f"{_SHIM.name} not built; run `python -m cuda_force_b200._build`"
+    try:
+        torch.ops.load_library(str(_SHIM))
+    except OSError as error:  # pragma: no cover - surfaced through backend_report
+        return False, f"extension present but failed to load: {error}"
+    return True, "extension loaded with sm_100a kernels"
+
+
+_EXTENSION_LOADED, _LOAD_MESSAGE = _load_extension()
+
+#: True when the extension is loaded and a CUDA device is visible.
+CUDA_KERNELS_AVAILABLE: bool = _EXTENSION_LOADED and torch.cuda.is_available()
+
+#: Storage dtypes with a kernel. Quantisation accepts all three; the linears
+#: run on the tensor cores and take float16 / bfloat16.
+KERNEL_DTYPES: frozenset[torch.dtype] = frozenset({torch.float32, torch.float16, torch.bfloat16})
+LINEAR_DTYPES: frozenset[torch.dtype] = frozenset({torch.float16, torch.bfloat16})
+
+
+@dataclass(frozen=True)
+class BackendReport:
+    """Which implementation runs, and why."""
+
+    extension_loaded: bool
+    cuda_compiled: bool
+    cuda_device_available: bool
+    device_name: str | None
+    message: str
+
+    @property
+    def using_custom_kernels(self) -> bool:
+        return self.extension_loaded and self.cuda_compiled and self.cuda_device_available
+
+    def __str__(self) -> str:
+        path = "custom CUDA kernels" if self.using_custom_kernels else "no usable kernels"
+        return f"cuda_force_b200: {path} on {self.device_name or 'no GPU'} ({self.message})"
+
+
+def backend_report() -> BackendReport:
+    available = torch.cuda.is_available()
+    return BackendReport(
+        extension_loaded=_EXTENSION_LOADED,
+        cuda_compiled=_EXTENSION_LOADED,
+        cuda_device_available=available,
+        device_name=torch.cuda.get_device_name(0) if available else None,
+        message=_LOAD_MESSAGE,
+    )
+
+
+def kernel_supports(dtype: torch.dtype) -> bool:
+    return dtype in KERNEL_DTYPES
+
+
+def _require(op: str, *tensors: torch.Tensor) -> None:
+    if not _EXTENSION_LOADED:
+        raise RuntimeError(f"{op}: {_LOAD_MESSAGE}")
+    for t in tensors:
+        if not t.is_cuda:
+            raise RuntimeError(f"{op}: CUDA tensors required (this build has no CPU path)")
+    if torch.is_grad_enabled() and any(t.requires_grad for t in tensors):
+        raise RuntimeError(f"{op}: inference-only kernels; no backward is implemented")
+
+
+def _as_stored(t: torch.Tensor) -> torch.Tensor:
+    """Contiguous, or the transpose of a contiguous 2-D tensor; otherwise a copy."""
+    if t.is_contiguous() or (t.dim() == 2 and t.t().is_contiguous()):
+        return t
+    return t.contiguous()
+
+
+def quantize_int8(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Block-wise symmetric int8 quantisation.
+
+    Returns ``(quantised, scales)``: int8 codes shaped like ``x`` and float32
+    scales, one per ``QUANT_BLOCK_SIZE`` elements of the flattened tensor.
+    """
+    _require("quantize_int8", x)
+    quantised, scales = torch.ops.cudaforge.quantize_int8(x.contiguous())
+    return quantised, scales
+
+
+def dequantize_int8(quantised: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """Inverse of :func:`quantize_int8` (float32 output). Lossy by construction."""
+    expected = (quantised.numel() + QUANT_BLOCK_SIZE - 1) // QUANT_BLOCK_SIZE
+    if scales.numel() != expected:
+        raise ValueError(
+            f"expected {expected} block scales for {quantised.numel()} elements, "
+            f"got {scales.numel()}"
+        )
+    _require("dequantize_int8", quantised, scales)
+    return torch.ops.cudaforge.dequantize_int8(quantised.contiguous(), scales.contiguous())
+
+
+def quantize_dequantize(x: torch.Tensor) -> torch.Tensor:
+    """Fake quantisation: ``dequantize_int8(*quantize_int8(x))`` in one pass."""
+    _require("quantize_dequantize", x)
+    return torch.ops.cudaforge.quantize_dequantize(x.contiguous())
+
+
+def quantize_int8_many(tensors: list[torch.Tensor]) -> list[tuple[torch.Tensor, torch.Tensor]]:
+    """Quantise several tensors of one dtype in one launch."""
+    if not tensors:
+        return []
+    _require("quantize_int8_many", *tensors)
+    flat = torch.ops.cudaforge.quantize_int8_many([t.contiguous() for t in tensors])
+    return [(flat[2 * i], flat[2 * i + 1]) for i in range(len(tensors))]
+
+
+def quantization_error(x: torch.Tensor) -> torch.Tensor:
+    """Maximum absolute round-trip error of int8 quantisation (<= scale / 2 per block)."""
+    quantised, scales = quantize_int8(x)
+    restored = dequantize_int8(quantised, scales)
+    return (x.float() - restored).abs().max()
+
+
+def _check_lora_shapes(
+    x: torch.Tensor, in_features: int, out_features: int, lora_a: torch.Tensor, lora_b: torch.Tensor
+) -> None:
+    if x.shape[-1] != in_features:
+        raise ValueError(f"x has {x.shape[-1]} input features but weight expects {in_features}")
+    if lora_a.shape[0] != in_features:
+        raise ValueError(
+            f"lora_a must be [in_features, rank] with in_features={in_features}, "
+            f"got {tuple(lora_a.shape)}"
+        )
+    if lora_b.shape[0] != lora_a.shape[1] or lora_b.shape[1] != out_features:
+        raise ValueError(
+            f"lora_b must be [rank, out_features] = "
+            f"[{lora_a.shape[1]}, {out_features}], got {tuple(lora_b.shape)}"
+        )
+
+
+def _flatten_tokens(x: torch.Tensor) -> tuple[torch.Tensor, tuple[int, ...]]:
+    lead = tuple(x.shape[:-1])
+    return x.reshape(-1, x.shape[-1]).contiguous(), lead
+
+
+def lora_linear(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    lora_a: torch.Tensor,
+    lora_b: torch.Tensor,
+    scale: float = 1.0,
+) -> torch.Tensor:
+    """LoRA-adapted linear layer: ``x @ weight + scale * (x @ lora_a) @ lora_b``.
+
+    Args:
+        x: ``[..., in_features]`` (bfloat16 or float16).
+        weight: ``[in_features, out_features]`` — contiguous, or ``W.t()`` of an
+            nn.Linear weight ``W [out_features, in_features]``.
+        lora_a: ``[in_features, rank]`` (or the transpose of ``[rank, in_features]``).
+        lora_b: ``[rank, out_features]`` (or the transpose of ``[out_features, rank]``).
+        scale: usually ``alpha / rank``.
+    """
+    _check_lora_shapes(x, weight.shape[0], weight.shape[1], lora_a, lora_b)
+    _require("lora_linear", x, weight, lora_a, lora_b)
+    x2, lead = _flatten_tokens(x)
+    y = torch.ops.cudaforge.lora_linear(
+        x2, _as_stored(weight), _as_stored(lora_a), _as_stored(lora_b), float(scale)
+    )
+    return y.reshape(*lead, y.shape[-1])
+
+
+def lora_linear_int8(
+    x: torch.Tensor,
+    w_codes: torch.Tensor,
+    w_scales: torch.Tensor,
+    lora_a: torch.Tensor,
+    lora_b: torch.Tensor,
+    scale: float = 1.0,
+) -> torch.Tensor:
+    """``lora_linear(x, dequantize_int8(w_codes, w_scales).T, lora_a, lora_b, scale)``.
+
+    Args:
+        w_codes: int8 ``[out_features, in_features]``, the codes
+            :func:`quantize_int8` returns for an nn.Linear weight.
+        w_scales: float32 block scales of ``w_codes`` (1-D).
+    """
+    if w_codes.dim() != 2:
+        raise ValueError(f"w_codes must be [out_features, in_features], got {tuple(w_codes.shape)}")
+    out_features, in_features = w_codes.shape
+    _check_lora_shapes(x, in_features, out_features, lora_a, lora_b)
+    expected = (w_codes.numel() + QUANT_BLOCK_SIZE - 1) // QUANT_BLOCK_SIZE
+    if w_scales.numel() != expected:
+        raise ValueError(
+            f"expected {expected} block scales for {w_codes.numel()} elements, "
+            f"got {w_scales.numel()}"
+        )
+    _require("lora_linear_int8", x, w_codes, w_scales, lora_a, lora_b)
+    x2, lead = _flatten_tokens(x)
+    y = torch.ops.cudaforge.lora_linear_int8(
+        x2, w_codes.contiguous(), w_scales.contiguous().reshape(-1), _as_stored(lora_a),
+        _as_stored(lora_b), float(scale)
+    )
+    return y.reshape(*lead, y.shape[-1])

@@ -1,0 +1,161 @@
+/*
+ * cudaforge_b200.h — C ABI of the B200 (sm_100a) quantised-linear hot path.
+ *
+ * Every entry point takes plain device pointers, 64-bit element counts, a
+ * dtype code and a CUDA stream, launches asynchronously on that stream and
+ * returns a cf_status code. Nothing here allocates device memory: outputs and
+ * the optional workspace are owned by the caller, exactly like the launchers
+ * of the reference (CudaForge) whose interfaces these entry points replace.
+ *
+ * Counts are int64_t. The reference launchers take `int count`
+ * (cuda/include/cudaforge/quantization.cuh:40-48; cpp/src/bindings.cpp:202,217),
+ * which overflows for tensors above 2^31 elements.
+ *
+ * Block quantisation contract (identical to the reference):
+ *   blocks of CF_QUANT_BLOCK_SIZE consecutive elements of the flattened tensor,
+ *   scale_b = fl32(absmax_b / 127), replaced by 1.0 when it is not > 0,
+ *   code_i  = clamp(rint_half_even(fl32(x_i / scale_b)), -127, 127), NaN -> 0,
+ *   dequant = fl32(code_i * scale_b).
+ */
+#ifndef CUDAFORGE_B200_H_
+#define CUDAFORGE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define CF_API __attribute__((visibility("default")))
+#else
+#define CF_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same value as kQuantBlockSize (reference cuda/include/cudaforge/quantization.cuh:18). */
+#define CF_QUANT_BLOCK_SIZE 64
+
+/* A cudaStream_t. Declared here so the header needs no CUDA include. */
+typedef struct CUstream_st *cf_stream_t;
+
+typedef enum cf_status {
+  CF_OK = 0,
+  CF_ERR_INVALID_ARGUMENT = 1, /* null pointer, negative size, shape mismatch   */
+  CF_ERR_UNSUPPORTED = 2,      /* dtype / layout / shape this build cannot run */
+  CF_ERR_MISALIGNED = 3,       /* a pointer violates the documented alignment  */
+  CF_ERR_CUDA = 4,             /* a CUDA runtime call failed; see cf_last_cuda_error() */
+  CF_ERR_DEVICE_TIMEOUT = 5,   /* a bounded device-side wait gave up            */
+  CF_ERR_WORKSPACE = 6,        /* workspace missing or smaller than required    */
+  CF_ERR_NO_DEVICE = 7         /* current device is not an sm_100 part          */
+} cf_status;
+
+typedef enum cf_dtype {
+  CF_DTYPE_F32 = 0,
+  CF_DTYPE_F16 = 1,
+  CF_DTYPE_BF16 = 2
+} cf_dtype;
+
+/* Storage order of a 2-D operand. "REF" is the order the reference op uses,
+ * "T" is its transpose (contiguous). For W: REF = [in, out] (reference
+ * lora_linear, cuda/include/cudaforge/lora_linear.cuh:22-31), T = [out, in]
+ * (nn.Linear). For A: REF = [in, rank], T = [rank, in]. For B: REF =
+ * [rank, out], T = [out, rank]. T is what training/lora.py stores. */
+typedef enum cf_layout {
+  CF_LAYOUT_REF = 0,
+  CF_LAYOUT_T = 1
+} cf_layout;
+
+/* ---- block INT8 quantisation -------------------------------------------- */
+
+/* Number of block scales for `count` elements: ceil(count / 64), 0 for count <= 0.
+ * Replaces quant_scale_count (reference cuda/src/quantization.cu:80-82). */
+CF_API int64_t cf_quant_scale_count(int64_t count);
+
+/* input: `count` elements of `dtype` (f32, f16 or bf16); codes: int8[count];
+ * scales: float[cf_quant_scale_count(count)].
+ * Replaces launch_quantize_int8 (reference cuda/include/cudaforge/quantization.cuh:40-41,
+ * kernel cuda/src/quantization.cu:18-47), which accepts f32 only. */
+CF_API int cf_quantize_int8(const void *input, int dtype, int8_t *codes, float *scales,
+                     int64_t count, cf_stream_t stream);
+
+/* codes: int8[count]; scales: float[cf_quant_scale_count(count)]; output: float[count].
+ * Replaces launch_dequantize_int8 (reference quantization.cuh:44-45, kernel
+ * quantization.cu:49-57). */
+CF_API int cf_dequantize_int8(const int8_t *codes, const float *scales, float *output,
+                       int64_t count, cf_stream_t stream);
+
+/* Quantise then dequantise in one pass ("fake quantisation"); output float[count].
+ * Replaces launch_quantize_dequantize (reference quantization.cuh:50-51,
+ * kernel quantization.cu:59-76). */
+CF_API int cf_quantize_dequantize(const void *input, int dtype, float *output, int64_t count,
+                           cf_stream_t stream);
+
+/* One tensor of a grouped quantisation. */
+typedef struct cf_quant_segment {
+  const void *input;
+  int8_t *codes;
+  float *scales;
+  int64_t count;
+} cf_quant_segment;
+
+/* Quantises `nseg` independent tensors of one dtype in a single launch (the
+ * segment table travels as a kernel parameter, at most CF_MAX_SEGMENTS per
+ * launch; longer lists are split into several launches). Each segment has the
+ * semantics of cf_quantize_int8. No counterpart launcher in the reference: it
+ * is the batched form of launch_quantize_int8 used to quantise a whole layer
+ * stack without one launch per tensor. */
+#define CF_MAX_SEGMENTS 256
+CF_API int cf_quantize_int8_many(const cf_quant_segment *segments, int nseg, int dtype,
+                          cf_stream_t stream);
+
+/* ---- LoRA linear --------------------------------------------------------- */
+
+/* y[m, n] = sum_k x[m,k] W[k,n] + scale * sum_j (sum_k x[m,k] A[k,j]) B[j,n]
+ * x: [m, k] row-major, y: [m, n] row-major, both of `dtype` (f16 or bf16),
+ * fp32 accumulation. `w`, `a`, `b` are stored as described by cf_layout.
+ * Requirements: k % 64 == 0, n % 16 == 0, rank in {16, 32, 64} (rank < 16 and
+ * other ranks are zero-padded by the caller), all pointers 16-byte aligned.
+ * Workspace: cf_lora_linear_workspace_bytes(m, rank) bytes of device memory,
+ * 16-byte aligned, holding the down-projection P = scale * x A between two
+ * launches. Replaces launch_lora_linear (reference
+ * cuda/include/cudaforge/lora_linear.cuh:45-48) and lora_workspace_bytes
+ * (cuda/src/lora_linear.cu:218-223); the reference supports f32 only. */
+CF_API size_t cf_lora_linear_workspace_bytes(int64_t m, int64_t rank);
+CF_API int cf_lora_linear(const void *x, const void *w, int w_layout, const void *a, int a_layout,
+                   const void *b, int b_layout, void *y, int64_t m, int64_t k, int64_t n,
+                   int64_t rank, float scale, int dtype, void *workspace,
+                   size_t workspace_bytes, cf_stream_t stream);
+
+/* Same product with W given as block-INT8: w_codes int8[n, k] (the output of
+ * cf_quantize_int8 on an nn.Linear weight [out, in]) and w_scales
+ * float[n * k / 64]. Semantics: lora_linear(x, dequantize(w_codes, w_scales)^T,
+ * a, b, scale). No counterpart in the reference, which has no INT8-weight
+ * linear; its semantic definition composes the reference's dequantize_int8
+ * (cpp/src/bindings.cpp:320-329) with lora_linear (bindings.cpp:255-258). */
+CF_API int cf_lora_linear_int8(const void *x, const int8_t *w_codes, const float *w_scales,
+                        const void *a, int a_layout, const void *b, int b_layout, void *y,
+                        int64_t m, int64_t k, int64_t n, int64_t rank, float scale, int dtype,
+                        void *workspace, size_t workspace_bytes, cf_stream_t stream);
+
+/* ---- status -------------------------------------------------------------- */
+
+/* Human-readable text for a cf_status value. */
+CF_API const char *cf_status_string(int status);
+
+/* The cudaError_t of the most recent CF_ERR_CUDA returned on this thread. */
+CF_API int cf_last_cuda_error(void);
+
+/* Reads and clears the device-side error word of the current device (set by a
+ * kernel whose bounded wait gave up). Synchronises with the device. Returns
+ * CF_OK or CF_ERR_DEVICE_TIMEOUT (CF_ERR_CUDA if the read itself fails). */
+CF_API int cf_device_status(void);
+
+/* Build information: "sm_100a" architecture tag and version string. */
+CF_API const char *cf_build_info(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CUDAFORGE_B200_H_ */

@@ -1,0 +1,161 @@
+"""Host-side checks that need no GPU: the C-ABI library loads and exports every
+symbol the header declares, argument validation, constants, and the Python
+wrapper's error behaviour (mirroring the reference's tests/python/test_ops.py
+ValueError cases)."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+import cuda_force_b200 as cf
+from cuda_force_b200 import _abi
+from cuda_force_b200 import ops
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "cudaforge_b200.h"
+
+
+def declared_functions() -> list[str]:
+    text = HEADER.read_text()
+    return re.findall(r"^CF_API\s+[\w\s\*]+?\b(cf_\w+)\(", text, flags=re.M)
+
+
+def test_header_declares_the_abi():
+    names = declared_functions()
+    assert "cf_quantize_int8" in names and "cf_lora_linear_int8" in names
+    assert len(names) == len(set(names))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _abi.load()
+    for name in declared_functions():
+        assert hasattr(lib, name), f"{name} declared in the header but not exported"
+    assert set(declared_functions()) == set(_abi.SIGNATURES), "ctypes binding out of sync"
+
+
+def test_build_info_names_the_architecture():
+    assert b"sm_100a" in _abi.load().cf_build_info()
+
+
+def test_block_size_agrees_across_languages():
+    cuh = (ROOT / "cuda_force_b200" / "csrc" / "cf_common.cuh").read_text()
+    m = re.search(r"inline\s+constexpr\s+\w+\s+kQuantBlockSize\s*=\s*(\d+)\s*;", cuh)
+    assert m and int(m.group(1)) == ops.QUANT_BLOCK_SIZE
+    h = re.search(r"#define\s+CF_QUANT_BLOCK_SIZE\s+(\d+)", HEADER.read_text())
+    assert h and int(h.group(1)) == ops.QUANT_BLOCK_SIZE
+
+
+@pytest.mark.parametrize(("count", "expected"), [(0, 0), (1, 1), (64, 1), (65, 2), (-5, 0),
+                                                 (2**31 + 1, 2**25 + 1)])
+def test_scale_count_known_answers(count, expected):
+    assert _abi.load().cf_quant_scale_count(count) == expected
+
+
+def test_status_strings():
+    lib = _abi.load()
+    assert lib.cf_status_string(_abi.CF_OK) == b"ok"
+    assert b"timed out" in lib.cf_status_string(_abi.CF_ERR_DEVICE_TIMEOUT)
+    assert lib.cf_status_string(99) == b"unknown status"
+
+
+def test_abi_validates_arguments_before_touching_the_device():
+    lib = _abi.load()
+    null = None
+    assert lib.cf_quantize_int8(null, 0, null, null, 0, null) == _abi.CF_OK  # empty is a no-op
+    assert lib.cf_quantize_int8(null, 0, null, null, 64, null) == _abi.CF_ERR_INVALID_ARGUMENT
+    assert lib.cf_quantize_int8(null, 0, null, null, -1, null) == _abi.CF_ERR_INVALID_ARGUMENT
+    assert lib.cf_dequantize_int8(null, null, null, 64, null) == _abi.CF_ERR_INVALID_ARGUMENT
+    assert lib.cf_quantize_dequantize(null, 0, null, 64, null) == _abi.CF_ERR_INVALID_ARGUMENT
+    fake = ctypes.c_void_p(0x1000)
+    assert lib.cf_quantize_int8(fake, 7, fake, fake, 64, null) == _abi.CF_ERR_UNSUPPORTED
+    segs = (_abi.QuantSegment * 1)(_abi.QuantSegment(None, None, None, 64))
+    assert lib.cf_quantize_int8_many(segs, 1, 0, null) == _abi.CF_ERR_INVALID_ARGUMENT
+    assert lib.cf_quantize_int8_many(segs, 0, 0, null) == _abi.CF_OK
+
+
+def test_lora_abi_validates_shapes_and_workspace():
+    lib = _abi.load()
+    f = ctypes.c_void_p(0x1000)
+    args = dict(m=128, k=256, n=256, r=16)
+    ws = lib.cf_lora_linear_workspace_bytes(args["m"], args["r"])
+    assert ws >= args["m"] * args["r"] * 2
+    call = lambda m, k, n, r, ws_bytes, wsp=f: lib.cf_lora_linear(  # noqa: E731
+        f, f, 1, f, 0, f, 0, f, m, k, n, r, 2.0, _abi.CF_DTYPE_BF16, wsp, ws_bytes, None)
+    assert call(128, 100, 256, 16, ws) == _abi.CF_ERR_UNSUPPORTED        # k % 64 != 0
+    assert call(128, 256, 250, 16, ws) == _abi.CF_ERR_UNSUPPORTED        # n % 16 != 0
+    assert call(128, 256, 256, 24, ws) == _abi.CF_ERR_UNSUPPORTED        # rank not 16/32/64
+    assert call(128, 256, 256, 16, ws - 16) == _abi.CF_ERR_WORKSPACE
+    assert call(128, 256, 256, 16, ws, None) == _abi.CF_ERR_WORKSPACE
+    assert call(-1, 256, 256, 16, ws) == _abi.CF_ERR_INVALID_ARGUMENT
+    assert lib.cf_lora_linear(None, f, 1, f, 0, f, 0, f, 128, 256, 256, 16, 2.0,
+                              _abi.CF_DTYPE_BF16, f, ws, None) == _abi.CF_ERR_INVALID_ARGUMENT
+    assert lib.cf_lora_linear(f, f, 1, f, 0, f, 0, f, 128, 256, 256, 16, 2.0,
+                              _abi.CF_DTYPE_F32, f, ws, None) == _abi.CF_ERR_UNSUPPORTED
+    misaligned = ctypes.c_void_p(0x1008)
+    assert lib.cf_lora_linear(misaligned, f, 1, f, 0, f, 0, f, 128, 256, 256, 16, 2.0,
+                              _abi.CF_DTYPE_BF16, f, ws, None) == _abi.CF_ERR_MISALIGNED
+    assert lib.cf_lora_linear(f, f, 1, f, 0, f, 0, f, 0, 256, 256, 16, 2.0,
+                              _abi.CF_DTYPE_BF16, f, ws, None) == _abi.CF_OK      # empty
+
+
+def test_dispatcher_schemas_match_the_reference():
+    # Byte-identical to reference cpp/src/bindings.cpp:344,352-353.
+    expected = {
+        "lora_linear": "cudaforge::lora_linear(Tensor x, Tensor w, Tensor a, Tensor b, float scale) -> Tensor",
+        "quantize_int8": "cudaforge::quantize_int8(Tensor input) -> Tensor[]",
+        "dequantize_int8": "cudaforge::dequantize_int8(Tensor quantised, Tensor scales) -> Tensor",
+    }
+    for name, schema in expected.items():
+        assert str(getattr(torch.ops.cudaforge, name).default._schema) == schema
+
+
+def test_cpu_tensors_fail_loudly():
+    with pytest.raises(RuntimeError, match="CUDA"):
+        cf.quantize_int8(torch.randn(128))
+    with pytest.raises((RuntimeError, NotImplementedError)):
+        torch.ops.cudaforge.quantize_int8(torch.randn(128))
+
+
+@pytest.mark.parametrize(
+    ("shapes", "message"),
+    [
+        ({"x": (4, 31), "w": (32, 16), "a": (32, 4), "b": (4, 16)}, "input features"),
+        ({"x": (4, 32), "w": (32, 16), "a": (31, 4), "b": (4, 16)}, "lora_a"),
+        ({"x": (4, 32), "w": (32, 16), "a": (32, 4), "b": (5, 16)}, "lora_b"),
+        ({"x": (4, 32), "w": (32, 16), "a": (32, 4), "b": (4, 15)}, "lora_b"),
+    ],
+)
+def test_lora_rejects_mismatched_shapes(shapes, message):
+    # Same cases and messages as the reference's tests/python/test_ops.py:141-161.
+    with pytest.raises(ValueError, match=message):
+        cf.lora_linear(torch.randn(*shapes["x"]), torch.randn(*shapes["w"]),
+                       torch.randn(*shapes["a"]), torch.randn(*shapes["b"]))
+
+
+def test_dequantize_rejects_a_wrong_scale_count():
+    with pytest.raises(ValueError, match="block scales"):
+        cf.dequantize_int8(torch.zeros(128, dtype=torch.int8), torch.ones(1))
+
+
+def test_lora_int8_rejects_wrong_scale_count():
+    with pytest.raises(ValueError, match="block scales"):
+        cf.lora_linear_int8(torch.randn(2, 64), torch.zeros(16, 64, dtype=torch.int8),
+                            torch.ones(3), torch.randn(64, 16), torch.randn(16, 16))
+
+
+def test_backend_report_is_truthful_without_a_gpu():
+    report = cf.backend_report()
+    assert report.extension_loaded
+    assert report.using_custom_kernels == torch.cuda.is_available()
+    assert "cuda_force_b200" in str(report)
+
+
+def test_autograd_inputs_are_rejected():
+    x = torch.randn(4, 64, requires_grad=True)
+    with pytest.raises(RuntimeError):
+        cf.quantize_int8(x)

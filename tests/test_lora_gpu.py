@@ -1,0 +1,176 @@
+"""Parity of the tcgen05 LoRA linears against the fp32 oracle.
+
+Tolerance: max|y - ref| / max|ref| <= 2e-2 with fp32
+accumulation, ref = the reference's formula (python/cudaforge/ops.py:178-185)
+evaluated in fp32 on the CPU from the same bf16/fp16 inputs. The kernel rounds
+P = scale * x A to the activation dtype before the up-projection and its output
+to the activation dtype, so typical errors are ~1e-3; the tests assert the
+stated bound and a tighter bound that catches a broken tile (5e-3).
+
+Covers every storage layout of w / a / b (reference [in, out] order and the
+nn.Linear transposes), ranks 16/32/64 plus padded small ranks, bf16 and fp16,
+ragged M / N / K, the W8 variant, and the reference's semantic tests
+(tests/python/test_ops.py:101-138: definition, zero-B, linearity in scale).
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import pytest
+import torch
+
+import cuda_force_b200 as cf
+from cuda_force_b200 import _abi
+from oracle import linear_ref
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-2
+TIGHT = 5e-3
+
+
+def make(m, k, n, r, dtype, seed=0, device="cuda"):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    x = torch.randn(m, k, generator=g).to(dtype)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(dtype)      # nn.Linear layout [out, in]
+    a = (torch.randn(k, r, generator=g) * 0.01).to(dtype)
+    b = (torch.randn(r, n, generator=g) * 0.01).to(dtype)
+    return x, w, a, b
+
+
+def as_layout(t: torch.Tensor, transposed: bool) -> torch.Tensor:
+    """The same logical matrix, stored contiguous (REF) or as a transposed view (T)."""
+    return t.t().contiguous().t() if transposed else t.contiguous()
+
+
+@pytest.mark.parametrize("w_t", [False, True])
+@pytest.mark.parametrize("a_t", [False, True])
+@pytest.mark.parametrize("b_t", [False, True])
+def test_every_layout(w_t, a_t, b_t, cuda_device):
+    x, w, a, b = make(256, 512, 384, 16, torch.bfloat16, seed=1)
+    dev = cuda_device
+    wk = as_layout(w.t().to(dev), w_t)   # logical [K, N]
+    ak = as_layout(a.to(dev), a_t)
+    bk = as_layout(b.to(dev), b_t)
+    y = cf.lora_linear(x.to(dev), wk, ak, bk, 2.0)
+    ref = linear_ref.lora_linear(x, w.t(), a, b, 2.0)
+    err = linear_ref.max_rel_error(y, ref)
+    assert err <= TIGHT, f"layout w_t={w_t} a_t={a_t} b_t={b_t}: {err}"
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("rank", [16, 32, 64, 4, 8, 2])
+def test_ranks_and_dtypes(dtype, rank, cuda_device):
+    x, w, a, b = make(384, 1024, 512, rank, dtype, seed=rank)
+    a = a * 10  # make the adapter visible next to the frozen path
+    b = b * 10
+    dev = cuda_device
+    y = cf.lora_linear(x.to(dev), w.to(dev).t(), a.to(dev), b.to(dev), 32.0 / rank)
+    ref = linear_ref.lora_linear(x, w.t(), a, b, 32.0 / rank)
+    assert y.dtype == dtype
+    assert linear_ref.max_rel_error(y, ref) <= TIGHT
+
+
+@pytest.mark.parametrize(("m", "k", "n"), [(1, 64, 256), (33, 128, 264), (200, 200, 96),
+                                           (129, 4160, 520), (1000, 256, 8)])
+def test_ragged_shapes(m, k, n, cuda_device):
+    x, w, a, b = make(m, k, n, 16, torch.bfloat16, seed=m)
+    dev = cuda_device
+    y = cf.lora_linear(x.to(dev), w.to(dev).t(), a.to(dev), b.to(dev), 2.0)
+    assert y.shape == (m, n)
+    assert linear_ref.max_rel_error(y, linear_ref.lora_linear(x, w.t(), a, b, 2.0)) <= TIGHT
+
+
+def test_adapter_path_alone(cuda_device):
+    # W = 0 isolates the adapter; linear in scale (reference test_ops.py:130-138).
+    x, w, a, b = make(256, 256, 256, 16, torch.bfloat16, seed=5)
+    dev = cuda_device
+    w0 = torch.zeros_like(w).to(dev)
+    y1 = cf.lora_linear(x.to(dev), w0.t(), a.to(dev), b.to(dev), 1.0).float()
+    y2 = cf.lora_linear(x.to(dev), w0.t(), a.to(dev), b.to(dev), 2.0).float()
+    ref1 = linear_ref.lora_linear(x, torch.zeros(256, 256), a, b, 1.0)
+    assert linear_ref.max_rel_error(y1, ref1) <= TOL
+    torch.testing.assert_close(y2, 2 * y1, rtol=2e-2, atol=1e-3)
+
+
+def test_zero_b_reduces_to_the_frozen_layer(cuda_device):
+    x, w, a, b = make(256, 512, 256, 16, torch.bfloat16, seed=6)
+    dev = cuda_device
+    y = cf.lora_linear(x.to(dev), w.to(dev).t(), a.to(dev), torch.zeros_like(b).to(dev), 2.0)
+    frozen = (x.float() @ w.float().t())
+    assert linear_ref.max_rel_error(y, frozen) <= TIGHT
+
+
+def test_int8_weight_matches_dequantised_composition(cuda_device):
+    x, w, a, b = make(256, 1024, 768, 16, torch.bfloat16, seed=7)
+    dev = cuda_device
+    codes, scales = cf.quantize_int8(w.to(dev))
+    y = cf.lora_linear_int8(x.to(dev), codes, scales, a.to(dev), b.to(dev), 2.0)
+    ref = linear_ref.lora_linear_int8(x, codes.cpu(), scales.cpu(), a, b, 2.0)
+    assert linear_ref.max_rel_error(y, ref) <= TIGHT
+    # and it equals the bf16 path fed with the dequantised weight, up to rounding
+    wdq = cf.dequantize_int8(codes, scales).to(torch.bfloat16)
+    y_bf16 = cf.lora_linear(x.to(dev), wdq.t(), a.to(dev), b.to(dev), 2.0)
+    assert linear_ref.max_rel_error(y, y_bf16) <= 1e-2
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize(("m", "rank", "a_t", "b_t"), [(32, 16, False, False), (300, 32, True, True),
+                                                       (64, 64, False, True)])
+def test_int8_variants(dtype, m, rank, a_t, b_t, cuda_device):
+    x, w, a, b = make(m, 512, 1024, rank, dtype, seed=m + rank)
+    dev = cuda_device
+    codes, scales = cf.quantize_int8(w.to(dev))
+    y = cf.lora_linear_int8(x.to(dev), codes, scales, as_layout(a.to(dev), a_t),
+                            as_layout(b.to(dev), b_t), 2.0)
+    ref = linear_ref.lora_linear_int8(x, codes.cpu(), scales.cpu(), a, b, 2.0)
+    assert linear_ref.max_rel_error(y, ref) <= TIGHT
+
+
+def test_through_the_c_abi(cuda_device):
+    m, k, n, r = 256, 512, 512, 16
+    x, w, a, b = (t.to(cuda_device) for t in make(m, k, n, r, torch.bfloat16, seed=8))
+    lib = _abi.load()
+    y = torch.empty(m, n, dtype=torch.bfloat16, device=cuda_device)
+    ws_bytes = lib.cf_lora_linear_workspace_bytes(m, r)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=cuda_device)
+    s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    _abi.check(lib.cf_lora_linear(p(x), p(w), _abi.CF_LAYOUT_T, p(a), _abi.CF_LAYOUT_REF, p(b),
+                                  _abi.CF_LAYOUT_REF, p(y), m, k, n, r, 2.0, _abi.CF_DTYPE_BF16,
+                                  p(ws), ws_bytes, s), "cf_lora_linear")
+    ref = linear_ref.lora_linear(x, w.t(), a, b, 2.0)
+    assert linear_ref.max_rel_error(y, ref) <= TIGHT
+    assert lib.cf_device_status() == _abi.CF_OK
+
+
+def sampled_rows_error(y, x, w_t, a, b, scale, rows=256, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    idx = torch.randperm(x.shape[0], generator=g)[:rows].to(x.device)
+    ref = linear_ref.lora_linear(x[idx], w_t, a, b, scale)
+    return linear_ref.max_rel_error(y[idx], ref)
+
+
+def test_baseline_config3_bf16_lora(cuda_device):
+    # x [8192, 4096] N(0,1); W [4096, 4096] N(0, 0.02); A, B N(0, 0.01); r 16, alpha 32.
+    g = torch.Generator(device=cuda_device).manual_seed(3)
+    x = torch.randn(8192, 4096, device=cuda_device, generator=g).to(torch.bfloat16)
+    w = (torch.randn(4096, 4096, device=cuda_device, generator=g) * 0.02).to(torch.bfloat16)
+    a = (torch.randn(4096, 16, device=cuda_device, generator=g) * 0.01).to(torch.bfloat16)
+    b = (torch.randn(16, 4096, device=cuda_device, generator=g) * 0.01).to(torch.bfloat16)
+    y = cf.lora_linear(x, w.t(), a, b, 2.0)
+    assert sampled_rows_error(y, x, w.t(), a, b, 2.0) <= TIGHT
+
+
+@pytest.mark.parametrize("m", [32, 4096])
+def test_baseline_config4_w8_lora(m, cuda_device):
+    g = torch.Generator(device=cuda_device).manual_seed(4)
+    x = torch.randn(m, 4096, device=cuda_device, generator=g).to(torch.bfloat16)
+    w = (torch.randn(11008, 4096, device=cuda_device, generator=g) * 0.02).to(torch.bfloat16)
+    a = (torch.randn(4096, 16, device=cuda_device, generator=g) * 0.01).to(torch.bfloat16)
+    b = (torch.randn(16, 11008, device=cuda_device, generator=g) * 0.01).to(torch.bfloat16)
+    codes, scales = cf.quantize_int8(w)
+    y = cf.lora_linear_int8(x, codes, scales, a, b, 2.0)
+    w_t = linear_ref.dequantized_weight_t(codes, scales)
+    assert sampled_rows_error(y, x, w_t, a, b, 2.0, rows=min(m, 256)) <= TIGHT
