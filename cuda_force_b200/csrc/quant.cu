@@ -8,27 +8,28 @@
 //   dequant = fl32(code * scale).
 //
 // Design (not a translation of the reference's one-thread-per-element kernel):
-//   * main path (quantize_tma_kernel): a persistent grid streams 32 KB tiles
-//     through a 5-stage shared-memory ring with bulk copies (TMA engine) and
-//     writes codes and scales back with bulk stores; tails, misaligned tensors
+//   * main path (quantize_tma_kernel): a persistent grid in which every warp
+//     streams 1024-element tiles through its own 3-stage shared-memory ring
+//     with bulk copies (TMA engine) and writes codes and scales back with bulk
+//     stores; tails, misaligned tensors
 //     and fake-quant use a register-streaming kernel whose lanes issue UNROLL
 //     independent 16-byte loads before touching any of them;
 //   * a 64-element block is spread over 16 lanes (f32) or 8 lanes (f16/bf16);
 //     the absmax is a shuffle-xor max over those lanes of |x| bit patterns as
 //     unsigned integers, which orders non-negative floats exactly and makes a
 //     NaN win, the same propagation as torch.amax;
-//   * codes: the exact quotient fl32(x / s) is only needed near a rounding
-//     boundary. Each element is first multiplied by r = rn(1/s); when the
-//     product is further than 2^-12 from a half-integer (true for all but ~1e-4
-//     of elements) its rint equals rint(fl32(x/s)) — |t - x/s| < 2^-15.9 for
-//     |x/s| <= 127 with s and r normal — otherwise the correctly rounded IEEE
-//     division decides. Bit-exact, at a fraction of the divider's issue cost;
+//   * codes: fl32(x / s) is formed without a divide, as q0 = x * r, a residual
+//     FMA and one correction FMA (r = fl32(1/s)); the half-to-even rounding is
+//     an add of 1.5 * 2^23 whose low bits are the code. Verified equal to the
+//     IEEE quotient for all bf16/fp16 (x, absmax) pairs on the CPU; blocks with
+//     NaN/inf or extreme scales fall back to the IEEE division;
 //   * codes are packed 4 or 8 per store; the register path writes them with
 //     streaming stores (st.global.cs).
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include "cf_common.cuh"
 #include "ptx.cuh"
@@ -123,22 +124,32 @@ __device__ __forceinline__ float block_scale(unsigned absmax_bits) {
   return s > 0.0f ? s : 1.0f;
 }
 
-// Whether the reciprocal shortcut is valid for this scale (s and 1/s normal).
-__device__ __forceinline__ bool fast_scale(float s) {
-  return s >= 0x1p-126f && s <= 0x1p126f;
-}
-
 __device__ __forceinline__ int clamp_code(int v) { return min(max(v, -127), 127); }
 
-// clamp(rint_half_even(fl32(x / s)), -127, 127), NaN -> 0 (cvt.rni of NaN is 0).
-__device__ __forceinline__ int quantise_one(float x, float s, float r, bool fast) {
-  if (fast) {
-    const float t = __fmul_rn(x, r);
-    const float n = rintf(t);
-    // 0.5 - 2^-12: the product is at least 2^-12 away from a half-integer.
-    if (fabsf(t - n) <= 0.499755859375f) return clamp_code(__float2int_rn(n));
-  }
-  return clamp_code(__float2int_rn(__fdiv_rn(x, s)));
+// Division-free code of one element. With r = fl32(1/s) (correctly rounded)
+// and s in [2^-100, 2^100]:
+//   q0 = fl(x * r);  e = fma(-q0, s, x) (exact residual);  q = fma(e, r, q0)
+// gives q = fl32(x / s) (Markstein's correction step); the code is then
+// rint_half_even(q), produced by adding 1.5 * 2^23, which leaves the integer in
+// the low bits of the sum (the code byte is read from there; |q| <= 127 needs
+// no clamp). tests/native/verify_quotient.c checks this against the IEEE
+// division for every bf16 and fp16 (x, absmax) pair and a large fp32 sample.
+__device__ __forceinline__ uint32_t code_bits_fast(float x, float s, float r) {
+  const float q0 = __fmul_rn(x, r);
+  const float e = __fmaf_rn(-q0, s, x);
+  const float q = __fmaf_rn(e, r, q0);
+  return __float_as_uint(__fadd_rn(q, 12582912.0f));  // 1.5 * 2^23
+}
+
+// Reference-exact code by IEEE division, for every other block.
+__device__ __forceinline__ uint32_t code_bits_exact(float x, float s) {
+  return static_cast<uint32_t>(clamp_code(__float2int_rn(__fdiv_rn(x, s))));
+}
+
+// Blocks on the division-free path: no NaN/inf in the block and a scale whose
+// residual arithmetic stays in the normal range.
+__device__ __forceinline__ bool quotient_path_ok(unsigned absmax_bits, float s) {
+  return absmax_bits < 0x7f800000u && s >= 0x1p-100f && s <= 0x1p100f;
 }
 
 __device__ __forceinline__ unsigned pack4(int a, int b, int c, int d) {
@@ -149,57 +160,6 @@ __device__ __forceinline__ unsigned pack4(int a, int b, int c, int d) {
 // ---------------------------------------------------------------------------
 // Quantisation core shared by every kernel.
 // ---------------------------------------------------------------------------
-// Per-block constants. `fast` selects the reciprocal path: the block holds no
-// NaN/inf and both s and 1/s are normal, so |x * r| <= 127 * (1 + 2^-22) and
-// no clamp is needed.
-struct BlockParams {
-  float s;
-  float r;
-  bool fast;
-};
-
-__device__ __forceinline__ BlockParams block_params(unsigned absmax_bits) {
-  BlockParams b;
-  b.s = block_scale(absmax_bits);
-  b.r = __frcp_rn(b.s);
-  b.fast = absmax_bits < 0x7f800000u && b.s >= 0x1p-126f && b.s <= 0x1p126f;
-  return b;
-}
-
-// Codes of 4 elements of one block, packed little-endian into a word.
-//
-// Fast path: m = fma(x, r, 1.5 * 2^23) rounds the exact product x * r to the
-// nearest integer (ties to even) in one instruction, leaving that integer in
-// the low bits of m's bit pattern (so the code byte is read directly); d, the
-// product's distance to that integer, is exact to 2^-24. When |d| is at most
-// 0.5 - 2^-12 the rounding of fl32(x / s) agrees, because
-// |x*r - x/s| <= 2^-17 and |fl32(x/s) - x/s| <= 2^-18 for |x/s| <= 127.
-// Otherwise (a near tie, about one element in 4000) or off the fast path, the
-// correctly rounded IEEE division decides.
-__device__ __forceinline__ uint32_t quantise4(const float (&x)[4], const BlockParams &b) {
-  constexpr float kRound = 12582912.0f;           // 1.5 * 2^23
-  constexpr float kTieGuard = 0.499755859375f;    // 0.5 - 2^-12
-  uint32_t mb[4];
-  unsigned slow = b.fast ? 0u : 0xfu;
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const float m = __fmaf_rn(x[e], b.r, kRound);
-    const float d = __fmaf_rn(x[e], b.r, -(m - kRound));
-    mb[e] = __float_as_uint(m);
-    slow |= (fabsf(d) > kTieGuard ? 1u : 0u) << e;
-  }
-  if (slow != 0u) {
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      if (slow & (1u << e)) {
-        mb[e] = static_cast<uint32_t>(clamp_code(__float2int_rn(__fdiv_rn(x[e], b.s))));
-      }
-    }
-  }
-  return __byte_perm(__byte_perm(mb[0], mb[1], 0x0040u), __byte_perm(mb[2], mb[3], 0x0040u),
-                     0x5410u);
-}
-
 // Absolute-value bit pattern maximum of a lane's 16-byte vector, as float bits.
 // Non-negative floats order like their bit patterns and NaN patterns sit above
 // +inf, so the maximum propagates NaN exactly as torch.amax does.
@@ -210,10 +170,22 @@ __device__ __forceinline__ unsigned vec_absmax_bits(const uint4 &v, float *) {
 }
 // bf16: max of the packed 16-bit magnitudes, two per instruction; the bf16
 // pattern shifted left by 16 is the float pattern.
+__device__ __forceinline__ __nv_bfloat162 as_bf162(uint32_t w) {
+  return *reinterpret_cast<__nv_bfloat162 *>(&w);
+}
+__device__ __forceinline__ uint32_t bf162_bits(__nv_bfloat162 h) {
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+// Packed |x| maximum of a 16-byte bf16 vector, two lanes per instruction;
+// __hmax2_nan returns NaN when either operand is NaN.
+__device__ __forceinline__ uint32_t vec_absmax_bf16x2(const uint4 &v) {
+  const __nv_bfloat162 a = __hmax2_nan(__habs2(as_bf162(v.x)), __habs2(as_bf162(v.y)));
+  const __nv_bfloat162 b = __hmax2_nan(__habs2(as_bf162(v.z)), __habs2(as_bf162(v.w)));
+  return bf162_bits(__hmax2_nan(a, b));
+}
+// bf16: the bf16 pattern shifted left by 16 is the float pattern.
 __device__ __forceinline__ unsigned vec_absmax_bits(const uint4 &v, __nv_bfloat16 *) {
-  unsigned m = __vmaxu2(v.x & 0x7fff7fffu, v.y & 0x7fff7fffu);
-  m = __vmaxu2(m, v.z & 0x7fff7fffu);
-  m = __vmaxu2(m, v.w & 0x7fff7fffu);
+  const unsigned m = vec_absmax_bf16x2(v);
   return max(m << 16, m & 0xffff0000u);
 }
 // fp16: same packed maximum on the half patterns, then widened to float exactly.
@@ -240,35 +212,36 @@ struct LaneQuant {
     for (int off = kLanesPerBlock / 2; off > 0; off >>= 1) {
       m = max(m, __shfl_xor_sync(0xffffffffu, m, off));
     }
-    const BlockParams b = block_params(m);
+    const float s = block_scale(m);
+    const float r = __frcp_rn(s);
+    const bool fast = quotient_path_ok(m, s);
     float f[kPerVec];
     if constexpr (kPerVec == 4) {
       unpack(v, f);
     } else {
       unpack(v, f, static_cast<T *>(nullptr));
     }
+    uint32_t mb[kPerVec];
+#pragma unroll
+    for (int e = 0; e < kPerVec; ++e) mb[e] = fast ? code_bits_fast(f[e], s, r) : code_bits_exact(f[e], s);
 #pragma unroll
     for (int w = 0; w < kWords; ++w) {
-      const float x4[4] = {f[4 * w], f[4 * w + 1], f[4 * w + 2], f[4 * w + 3]};
-      codes[w] = quantise4(x4, b);
+      codes[w] = __byte_perm(__byte_perm(mb[4 * w], mb[4 * w + 1], 0x0040u),
+                             __byte_perm(mb[4 * w + 2], mb[4 * w + 3], 0x0040u), 0x5410u);
     }
-    scale = b.s;
+    scale = s;
   }
 };
 
-__device__ __forceinline__ float rcp_approx(float s) {
-  float r;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(s));
-  return r;
-}
 
 // Shared-memory layout of the TMA kernel: 4 lanes per 64-element block, 16
 // elements (kChunks 16-byte chunks) per lane, 8 blocks per warp step.
 //
-// Lane 4b+i of a step owns chunks 4*((j + (b & 1)) % kChunks) + i (j = 0 ..
+// Lane 4b+i of a step owns chunks 4*((j + b/2) % kChunks) + i (j = 0 ..
 // kChunks-1) of block b. Within one load instruction j the 32 chunk indices
 // then cover every residue mod 8 exactly four times, so the 16-byte shared
-// loads are bank-conflict-free while each lane's chunks stay in one block.
+// loads are bank-conflict-free while each lane's chunks stay in one block; the
+// code stores (4 or 8 bytes per chunk) spread evenly over the banks too.
 template <typename T>
 struct Quad {
   static constexpr int kPerChunk = 16 / static_cast<int>(sizeof(T));  // elements per chunk
@@ -277,32 +250,52 @@ struct Quad {
 
   static __device__ __forceinline__ int chunk_of(int lane, int j) {
     const int b = lane >> 2;
-    return 4 * ((j + (b & 1)) % kChunks) + (lane & 3);
+    return 4 * ((j + (b >> 1)) % kChunks) + (lane & 3);
+  }
+
+  // Per-lane byte offsets inside a step, fixed for the whole kernel.
+  struct Offsets {
+    int in[kChunks];    // input chunk offsets (bytes)
+    int code[kChunks];  // code offsets (bytes = elements)
+    int block;          // block of this lane within the step
+  };
+
+  static __device__ __forceinline__ Offsets offsets(int lane) {
+    Offsets o;
+    o.block = lane >> 2;
+#pragma unroll
+    for (int j = 0; j < kChunks; ++j) {
+      const int elem = o.block * kQuantBlockSize + chunk_of(lane, j) * kPerChunk;
+      o.in[j] = elem * static_cast<int>(sizeof(T));
+      o.code[j] = elem;
+    }
+    return o;
   }
 
   // Quantises one warp step: reads from `src` (the step's 512 elements),
   // writes codes to `codes` (512 bytes) and 8 scales to `scales`.
   static __device__ __forceinline__ void step(const uint8_t *src, uint8_t *codes, float *scales,
-                                              int lane) {
-    const int b = lane >> 2;
+                                              const Offsets &o, int lane) {
     uint4 v[kChunks];
 #pragma unroll
-    for (int j = 0; j < kChunks; ++j) {
-      const int elem = b * kQuantBlockSize + chunk_of(lane, j) * kPerChunk;
-      v[j] = *reinterpret_cast<const uint4 *>(src + elem * static_cast<int>(sizeof(T)));
-    }
+    for (int j = 0; j < kChunks; ++j) v[j] = *reinterpret_cast<const uint4 *>(src + o.in[j]);
     unsigned m = 0u;
+    if constexpr (std::is_same_v<T, __nv_bfloat16>) {
+      uint32_t packed = vec_absmax_bf16x2(v[0]);
 #pragma unroll
-    for (int j = 0; j < kChunks; ++j) m = max(m, vec_absmax_bits(v[j], static_cast<T *>(nullptr)));
+      for (int j = 1; j < kChunks; ++j) {
+        packed = bf162_bits(__hmax2_nan(as_bf162(packed), as_bf162(vec_absmax_bf16x2(v[j]))));
+      }
+      m = max(packed << 16, packed & 0xffff0000u);
+    } else {
+#pragma unroll
+      for (int j = 0; j < kChunks; ++j) m = max(m, vec_absmax_bits(v[j], static_cast<T *>(nullptr)));
+    }
     m = max(m, __shfl_xor_sync(0xffffffffu, m, 2));
     m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
     const float s = block_scale(m);
-    // 1 ulp reciprocal: |x*r - x/s| <= 127 * 2^-23 < 2^-15.9, far inside the guard.
-    const bool fast = m < 0x7f800000u && s >= 0x1p-126f && s <= 0x1p126f;
-    const float r = rcp_approx(s);
-
-    constexpr float kRound = 12582912.0f;         // 1.5 * 2^23
-    constexpr float kTieGuard = 0.499755859375f;  // 0.5 - 2^-12
+    const bool fast = quotient_path_ok(m, s);
+    const float r = __frcp_rn(s);
     float f[16];
 #pragma unroll
     for (int j = 0; j < kChunks; ++j) {
@@ -316,24 +309,17 @@ struct Quad {
       for (int e = 0; e < kPerChunk; ++e) f[j * kPerChunk + e] = g[e];
     }
     uint32_t mb[16];
-    float worst = 0.0f;
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      const float mm = __fmaf_rn(f[e], r, kRound);
-      const float d = __fmaf_rn(f[e], r, -(mm - kRound));
-      mb[e] = __float_as_uint(mm);
-      worst = fmaxf(worst, fabsf(d));
-    }
-    if (!fast || !(worst <= kTieGuard)) {
+    for (int e = 0; e < 16; ++e) mb[e] = code_bits_fast(f[e], s, r);
+    if (__any_sync(0xffffffffu, !fast)) {
+      // Blocks holding NaN/inf or with extreme scales: IEEE division.
 #pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        mb[e] = static_cast<uint32_t>(clamp_code(__float2int_rn(__fdiv_rn(f[e], s))));
-      }
+      for (int e = 0; e < 16; ++e) mb[e] = fast ? mb[e] : code_bits_exact(f[e], s);
     }
 #pragma unroll
     for (int j = 0; j < kChunks; ++j) {
       const int e0 = j * kPerChunk;
-      uint8_t *dst = codes + b * kQuantBlockSize + chunk_of(lane, j) * kPerChunk;
+      uint8_t *dst = codes + o.code[j];
       const uint32_t w0 = __byte_perm(__byte_perm(mb[e0], mb[e0 + 1], 0x0040u),
                                       __byte_perm(mb[e0 + 2], mb[e0 + 3], 0x0040u), 0x5410u);
       if constexpr (kPerChunk == 4) {
@@ -344,7 +330,7 @@ struct Quad {
         *reinterpret_cast<uint2 *>(dst) = make_uint2(w0, w1);
       }
     }
-    if ((lane & 3) == 0) scales[b] = s;
+    if ((lane & 3) == 0) scales[o.block] = s;
   }
 };
 
@@ -446,15 +432,13 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
     for (int off = kWarp / 2; off > 0; off >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, off));
     const float s = block_scale(m);
-    const float r = __frcp_rn(s);
-    const bool fast = fast_scale(s);
     if (i0 < count) {
-      const int q = quantise_one(x0, s, r, fast);
+      const int q = static_cast<int8_t>(code_bits_exact(x0, s) & 0xffu);
       if constexpr (kFake) fake_out[i0] = __fmul_rn(static_cast<float>(q), s);
       else codes[i0] = static_cast<int8_t>(q);
     }
     if (i1 < count) {
-      const int q = quantise_one(x1, s, r, fast);
+      const int q = static_cast<int8_t>(code_bits_exact(x1, s) & 0xffu);
       if constexpr (kFake) fake_out[i1] = __fmul_rn(static_cast<float>(q), s);
       else codes[i1] = static_cast<int8_t>(q);
     }
@@ -477,55 +461,56 @@ struct GroupedArgs {
 // ---------------------------------------------------------------------------
 // TMA-staged quantiser (the main path).
 //
-// A "tile" is kBlocks blocks of 64 elements (32 KB of input), contiguous in
-// memory. Thread 0 streams tiles into a ring of
-// kStages shared-memory buffers with bulk copies (cp.async.bulk, completion on
-// an mbarrier), so each SM keeps (kStages - 1) tiles of loads in flight no
-// matter how many registers the arithmetic needs. Each warp quantises its share
-// of the tile from shared memory (4 lanes per block, conflict-free 16-byte
-// loads, two-step shuffle absmax) into a triple-buffered shared staging area, and thread 0 writes the tile's codes and
-// scales back with bulk stores. Tiles are dealt round-robin to a persistent grid
-// of one CTA per SM, across every segment of a grouped launch.
+// Every warp runs its own pipeline; there is no CTA-wide barrier. A warp tile
+// is 1024 contiguous elements (16 blocks). Lane 0 keeps kStages - 1 tiles of
+// input in flight with bulk copies (cp.async.bulk global -> shared, completion
+// on the warp's mbarriers); the warp quantises a landed tile in two 8-block
+// steps (Quad layout), stages 1 KB of codes and 64 B of scales in shared
+// memory, and lane 0 writes them back with bulk stores (shared -> global).
+// Warp tiles are dealt round-robin over a persistent grid of one CTA per SM,
+// across every segment of a grouped launch.
 // ---------------------------------------------------------------------------
 template <typename T>
 struct TmaQuantCfg {
-  static constexpr int kThreads = sizeof(T) == 4 ? 256 : 512;
-  static constexpr int kStages = 5;
-  static constexpr int kBlocks = sizeof(T) == 4 ? 128 : 256;  // quant blocks per tile (32 KB)
-  static constexpr int kTileElems = kBlocks * kQuantBlockSize;  // 8192 (f32) / 16384
+  static constexpr int kWarps = sizeof(T) == 4 ? 12 : 20;
+  static constexpr int kThreads = kWarps * kWarp;
+  static constexpr int kStages = 3;
+  static constexpr int kCodeBufs = 2;
+  static constexpr int kTileElems = 1024;                      // per warp tile
+  static constexpr int kBlocks = kTileElems / kQuantBlockSize;  // 16
   static constexpr int kInBytes = kTileElems * static_cast<int>(sizeof(T));
-  static constexpr int kWarpElems = kTileElems / (kThreads / kWarp);  // per warp
-  static constexpr int kCodeBufs = 3;
-  static constexpr size_t kSmemBytes = static_cast<size_t>(kStages) * kInBytes +
-                                       kCodeBufs * kTileElems + kCodeBufs * kBlocks * 4 +
-                                       kStages * 8 + 16;
+  // per warp: input ring, code staging, scale staging, barriers
+  static constexpr int kWarpBytes = kStages * kInBytes + kCodeBufs * kTileElems +
+                                    kCodeBufs * kBlocks * 4 + 64;
+  static constexpr size_t kSmemBytes = static_cast<size_t>(kWarps) * kWarpBytes;
 };
 
 template <typename T>
 __global__ void __launch_bounds__(TmaQuantCfg<T>::kThreads, 1)
     quantize_tma_kernel(const __grid_constant__ GroupedArgs args, unsigned *error_word) {
   using C = TmaQuantCfg<T>;
+  using Q = Quad<T>;
   extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t *in_buf = smem;
-  uint8_t *code_buf = smem + C::kStages * C::kInBytes;
+  const int lane = threadIdx.x & (kWarp - 1);
+  const int warp = threadIdx.x / kWarp;
+  uint8_t *mine = smem + warp * C::kWarpBytes;
+  uint8_t *in_buf = mine;
+  uint8_t *code_buf = in_buf + C::kStages * C::kInBytes;
   float *scale_buf = reinterpret_cast<float *>(code_buf + C::kCodeBufs * C::kTileElems);
   uint64_t *full = reinterpret_cast<uint64_t *>(scale_buf + C::kCodeBufs * C::kBlocks);
-  __shared__ int abort_flag;
 
-  const int tid = threadIdx.x;
   const int64_t total = args.unit_end[args.nseg - 1];
-  const int64_t first = blockIdx.x;
-  const int64_t step = gridDim.x;
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * C::kWarps + warp;
+  const int64_t step = static_cast<int64_t>(gridDim.x) * C::kWarps;
   const int64_t n_mine = first < total ? (total - first + step - 1) / step : 0;
 
-  if (tid == 0) {
+  if (lane == 0) {
     for (int s = 0; s < C::kStages; ++s) ptx::mbar_init(&full[s], 1);
     ptx::fence_mbar_init();
-    abort_flag = 0;
   }
-  __syncthreads();
+  __syncwarp();
 
-  int seg_p = 0;  // producer's segment cursor (thread 0 only)
+  int seg_p = 0;  // lane 0's segment cursor for loads
   auto issue_load = [&](int64_t j) {
     const int64_t tile = first + j * step;
     while (tile >= args.unit_end[seg_p]) ++seg_p;
@@ -535,21 +520,21 @@ __global__ void __launch_bounds__(TmaQuantCfg<T>::kThreads, 1)
     ptx::mbar_expect_tx(&full[s], C::kInBytes);
     ptx::bulk_load(in_buf + s * C::kInBytes, src, C::kInBytes, &full[s]);
   };
-
-  if (tid == 0) {
+  if (lane == 0) {
     for (int64_t j = 0; j < n_mine && j < C::kStages - 1; ++j) issue_load(j);
   }
 
+  const typename Q::Offsets offs = Q::offsets(lane);
   int seg_c = 0;
+  int64_t issued = n_mine < C::kStages - 1 ? n_mine : C::kStages - 1;
+  bool aborted = false;
   for (int64_t j = 0; j < n_mine; ++j) {
     const int s = static_cast<int>(j % C::kStages);
     const uint32_t parity = static_cast<uint32_t>((j / C::kStages) & 1);
-    const bool timed_out = !ptx::mbar_wait(&full[s], parity);
-    if (__syncthreads_or(timed_out)) {
-      if (tid == 0) {
-        atomicOr(error_word, kDevErrTimeout);
-        abort_flag = 1;
-      }
+    const bool ok = ptx::mbar_wait(&full[s], parity);
+    if (__any_sync(0xffffffffu, !ok)) {
+      if (lane == 0) atomicOr(error_word, kDevErrTimeout);
+      aborted = true;
       break;
     }
     const int64_t tile = first + j * step;
@@ -557,38 +542,35 @@ __global__ void __launch_bounds__(TmaQuantCfg<T>::kThreads, 1)
     const int64_t seg_begin = seg_c == 0 ? 0 : args.unit_end[seg_c - 1];
     const int64_t elem0 = (tile - seg_begin) * C::kTileElems;
 
-    // Each warp quantises a contiguous 1/kWarps of the tile in steps of 8
-    // blocks (Quad layout: 4 lanes per block, conflict-free 16-byte loads).
-    using Q = Quad<T>;
-    const int lane = tid & (kWarp - 1);
-    const int warp = tid / kWarp;
     const int cb = static_cast<int>(j % C::kCodeBufs);
     const uint8_t *src = in_buf + s * C::kInBytes;
     uint8_t *codes_out = code_buf + cb * C::kTileElems;
     float *scales_out = scale_buf + cb * C::kBlocks;
-#pragma unroll 2
-    for (int st = 0; st < C::kWarpElems / Q::kStepElems; ++st) {
-      const int e0 = warp * C::kWarpElems + st * Q::kStepElems;
+#pragma unroll
+    for (int st = 0; st < C::kTileElems / Q::kStepElems; ++st) {
+      const int e0 = st * Q::kStepElems;
       Q::step(src + e0 * static_cast<int>(sizeof(T)), codes_out + e0,
-              scales_out + e0 / kQuantBlockSize, lane);
+              scales_out + e0 / kQuantBlockSize, offs, lane);
     }
     ptx::fence_proxy_async_smem();
-    __syncthreads();
-    if (tid == 0) {
-      ptx::bulk_store(args.codes[seg_c] + elem0, code_buf + cb * C::kTileElems, C::kTileElems);
-      ptx::bulk_store(args.scales[seg_c] + elem0 / kQuantBlockSize, scale_buf + cb * C::kBlocks,
-                      C::kBlocks * 4);
+    __syncwarp();
+    if (lane == 0) {
+      ptx::bulk_store(args.codes[seg_c] + elem0, codes_out, C::kTileElems);
+      ptx::bulk_store(args.scales[seg_c] + elem0 / kQuantBlockSize, scales_out, C::kBlocks * 4);
       ptx::bulk_commit();
-      if (j + C::kStages - 1 < n_mine) issue_load(j + C::kStages - 1);
-      // The staging buffer written next iteration was last read by the store
-      // two iterations ago; at most one group (this one) may still be reading.
-      ptx::bulk_wait_read<1>();
+      // The next tile goes into the stage of tile j - 1, whose reads finished
+      // before the previous iteration's __syncwarp.
+      if (issued < n_mine) issue_load(issued++);
+      // The staging buffer written next was last read by the store of tile
+      // j + 1 - kCodeBufs: allow only the kCodeBufs - 1 newest stores pending.
+      ptx::bulk_wait_read<C::kCodeBufs - 1>();
     }
+    __syncwarp();
   }
-  if (tid == 0) {
+  if (lane == 0) {
     ptx::bulk_wait_all();
-    // On abort, drain loads still in flight (bounded) before the CTA exits.
-    if (abort_flag) {
+    if (aborted) {
+      // Let loads still in flight land (bounded) before the CTA's shared memory goes away.
       for (int s = 0; s < C::kStages; ++s) ptx::mbar_wait(&full[s], 0, 100000000ull);
     }
   }
@@ -691,7 +673,8 @@ int launch_tma_quant(const GroupedArgs &args, int64_t tiles, cudaStream_t stream
                                     static_cast<int>(C::kSmemBytes)));
   unsigned *err = device_error_word();
   if (err == nullptr) return record_cuda_error(cudaGetLastError());
-  const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(tiles, sm_count())));
+  const int64_t ctas = (tiles + C::kWarps - 1) / C::kWarps;
+  const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(ctas, sm_count())));
   quantize_tma_kernel<T><<<grid, C::kThreads, C::kSmemBytes, stream>>>(args, err);
   return check_launch();
 }
