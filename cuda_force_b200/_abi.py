@@ -57,6 +57,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_p, _p, _p, _p, _int, _p, _int, _p, _i64, _i64, _i64, _i64, ctypes.c_float, _int, _p,
          ctypes.c_size_t, _p],
     ),
+    "cf_lora_linear_noalloc": (
+        _int,
+        [_p, _p, _int, _p, _int, _p, _int, _p, _i64, _i64, _i64, _i64, ctypes.c_float, _int, _p],
+    ),
     "cf_status_string": (ctypes.c_char_p, [_int]),
     "cf_last_cuda_error": (_int, []),
     "cf_device_status": (_int, []),

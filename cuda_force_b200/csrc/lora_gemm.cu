@@ -621,7 +621,73 @@ int validate_and_run(const LinearArgs &L, cf_stream_t stream) {
 }  // namespace
 }  // namespace cfb
 
+// ---------------------------------------------------------------------------
+// Allocation-free variant of cf_lora_linear.
+//
+// Some callers cannot allocate device memory for the down-projection
+// workspace: a host whose device memory is reserved up front by another
+// allocator (a serving engine that hands all free HBM to its KV cache or its
+// own pool), a foreign-language host bound to this C ABI with no CUDA
+// allocator of its own, and latency-critical loops that must not pay
+// cudaMalloc's implicit device synchronisation per layer. For them the
+// workspace lives in this file-scope device array, which every GPU that loads
+// the library holds until the process exits.
+//
+// Limits and rules:
+//   * at most kNoAllocScratchBytes (4 MiB) of workspace: m * rank * 2 bytes,
+//     rounded up to 256 (m <= 131072 at rank 16, m <= 32768 at rank 64);
+//     larger calls return CF_ERR_WORKSPACE and launch nothing;
+//   * the array is shared by every call on a device and keeps the last call's
+//     contents. Nothing needs to start at zero: each call's down-projection
+//     overwrites the rows it reads. Calls whose kernels overlap on the GPU
+//     (different streams without ordering) race on it;
+//   * the first call on a device looks up the array's device address with
+//     cudaGetSymbolAddress (once per device, with that device current); make
+//     that first call before any stream capture.
+// ---------------------------------------------------------------------------
+namespace cfb {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t{4} << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::atomic<void *> g_noalloc_ptr[64];
+
+// Device address of g_noalloc_scratch on the current device (set up once per
+// device). In host code the array's name is only a host-side stand-in.
+int noalloc_scratch(void **out) {
+  int dev = 0;
+  CFB_TRY_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return CF_ERR_UNSUPPORTED;
+  void *ptr = g_noalloc_ptr[dev].load(std::memory_order_acquire);
+  if (ptr == nullptr) {
+    CFB_TRY_CUDA(cudaGetSymbolAddress(&ptr, g_noalloc_scratch));
+    g_noalloc_ptr[dev].store(ptr, std::memory_order_release);
+  }
+  *out = ptr;
+  return CF_OK;
+}
+
+}  // namespace
+}  // namespace cfb
+
 extern "C" {
+
+int cf_lora_linear_noalloc(const void *x, const void *w, int w_layout, const void *a,
+                           int a_layout, const void *b, int b_layout, void *y, int64_t m,
+                           int64_t k, int64_t n, int64_t rank, float scale, int dtype,
+                           cf_stream_t stream) {
+  if (m < 0 || rank < 0) return CF_ERR_INVALID_ARGUMENT;
+  const size_t need = cfb::workspace_bytes(m, rank);
+  if (need > cfb::kNoAllocScratchBytes) return CF_ERR_WORKSPACE;
+  void *scratch = nullptr;
+  if (m > 0 && n > 0) {
+    if (int st = cfb::noalloc_scratch(&scratch)) return st;
+  }
+  cfb::LinearArgs L{x, w, w_layout, nullptr, a, a_layout, b, b_layout, y, m, k, n, rank,
+                    scale, dtype, scratch, cfb::kNoAllocScratchBytes, false};
+  return cfb::validate_and_run(L, stream);
+}
 
 size_t cf_lora_linear_workspace_bytes(int64_t m, int64_t rank) {
   return cfb::workspace_bytes(m, rank);

@@ -138,6 +138,21 @@ CF_API int cf_lora_linear_int8(const void *x, const int8_t *w_codes, const float
                         int64_t m, int64_t k, int64_t n, int64_t rank, float scale, int dtype,
                         void *workspace, size_t workspace_bytes, cf_stream_t stream);
 
+/* Allocation-free form of cf_lora_linear, for callers that cannot allocate the
+ * workspace: hosts whose device memory is reserved up front by another
+ * allocator, foreign-language hosts without a CUDA allocator, and loops that
+ * must not pay cudaMalloc's device synchronisation. No counterpart in the
+ * reference. The workspace is a 4 MiB device array inside the library, held by
+ * every GPU that loads it until exit: m * rank * 2 bytes (rounded up to 256)
+ * must fit, else CF_ERR_WORKSPACE and nothing is launched. Calls on one device
+ * share the array; calls that overlap on the GPU race on it. The first call on
+ * a device looks up the array's address (make it before any stream capture).
+ * Same arguments and semantics as cf_lora_linear otherwise. */
+CF_API int cf_lora_linear_noalloc(const void *x, const void *w, int w_layout, const void *a,
+                                  int a_layout, const void *b, int b_layout, void *y, int64_t m,
+                                  int64_t k, int64_t n, int64_t rank, float scale, int dtype,
+                                  cf_stream_t stream);
+
 /* ---- status -------------------------------------------------------------- */
 
 /* Human-readable text for a cf_status value. */
