@@ -9,8 +9,9 @@
 // memory: q * s in fp32 exactly as the dequantiser does, then rounded to the
 // activation dtype for the MMA.
 //
-// Two launches per call, both of the same persistent warp-specialised kernel:
-//   1. down-projection  P = scale * x A  -> workspace [M, r] (bf16/f16), tile N = r;
+// Two launches per call:
+//   1. down-projection  P = scale * x A  -> workspace [M, r] (bf16/f16), split-K
+//      over a thread-block cluster (down_proj_kernel);
 //   2. main product     y = x W^T + P B  with the adapter folded into the MMA as
 //      r/16 extra K-steps at the end of every output tile (A operand = P tile,
 //      B operand = B slice), so the rank-r update costs no epilogue arithmetic.
@@ -354,6 +355,9 @@ __global__ void __launch_bounds__(GemmCfg<BN, kInt8>::kThreads, 1)
     // Lane l of a converter warp handles row (group * 8 + l / 4) and 16-code
     // chunk (l % 4) of the int8 tile; it writes 32 bytes (two 16-byte chunks)
     // of the 128B-swizzled bf16 row: logical chunk c sits at c ^ (row % 8).
+    // Block scales are read from global memory one k-block ahead (registers),
+    // so their latency hides behind the current k-block's conversion.
+    constexpr int kGroups = BN >= 64 ? BN / 8 / (kConvThreads / kWarp) : 1;  // rows per thread
     const int cw = warp - kConvWarp0;
     const int sub_row = lane / 4;
     const int chunk = lane % 4;
@@ -361,9 +365,21 @@ __global__ void __launch_bounds__(GemmCfg<BN, kInt8>::kThreads, 1)
     uint32_t phase = 0;
     for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x) {
       const int n0 = (tile % p.n_tiles_n) * BN;
+      const float *srow[kGroups];
+      float s_cur[kGroups], s_next[kGroups];
+#pragma unroll
+      for (int g = 0; g < kGroups; ++g) {
+        const int n = n0 + (cw + g * (kConvThreads / kWarp)) * 8 + sub_row;
+        srow[g] = n < p.N ? p.w_scales + static_cast<int64_t>(n) * p.kb_per_row : nullptr;
+        s_cur[g] = srow[g] != nullptr ? __ldg(srow[g]) : 0.0f;
+      }
       bool ok = true;
       for (int it = 0; it < num_iters; ++it) {
         if (it < p.num_kb) {
+#pragma unroll
+          for (int g = 0; g < kGroups; ++g) {
+            s_next[g] = (srow[g] != nullptr && it + 1 < p.num_kb) ? __ldg(srow[g] + it + 1) : 0.0f;
+          }
           const bool got = ptx::mbar_wait(&full[stage], phase);
           if (__any_sync(0xffffffffu, !got)) {
             if (lane == 0) record_timeout(p.err, abort_flag);
@@ -373,11 +389,9 @@ __global__ void __launch_bounds__(GemmCfg<BN, kInt8>::kThreads, 1)
           uint8_t *sb = smem + stage * C::kStageBytes + C::kABytes;
           const uint8_t *raw = sb + C::kBBytes;
 #pragma unroll
-          for (int g = cw; g < BN / 8; g += (kConvThreads / kWarp)) {
-            const int r = g * 8 + sub_row;
-            const int n = n0 + r;
-            const float s = n < p.N ? __ldg(p.w_scales + static_cast<int64_t>(n) * p.kb_per_row + it)
-                                    : 0.0f;
+          for (int g = 0; g < kGroups; ++g) {
+            const int r = (cw + g * (kConvThreads / kWarp)) * 8 + sub_row;
+            const float sc = s_cur[g];
             const uint4 codes = *reinterpret_cast<const uint4 *>(raw + r * kBK + chunk * 16);
             const uint32_t words[4] = {codes.x, codes.y, codes.z, codes.w};
             uint32_t outw[8];
@@ -389,7 +403,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, kInt8>::kThreads, 1)
               for (int b = 0; b < 4; ++b) {
                 // 2^23 + (q + 128) as a float, minus (2^23 + 128): exactly q.
                 const float biased = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7440u | b));
-                f[b] = __fmul_rn(biased - 8388736.0f, s);
+                f[b] = __fmul_rn(biased - 8388736.0f, sc);
               }
               outw[2 * wd] = kBf16 ? ptx::pack_bf16x2(f[0], f[1]) : ptx::pack_f16x2(f[0], f[1]);
               outw[2 * wd + 1] = kBf16 ? ptx::pack_bf16x2(f[2], f[3]) : ptx::pack_f16x2(f[2], f[3]);
@@ -403,6 +417,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, kInt8>::kThreads, 1)
           }
           ptx::fence_proxy_async_smem();
           ptx::mbar_arrive(&conv_full[stage]);
+#pragma unroll
+          for (int g = 0; g < kGroups; ++g) s_cur[g] = s_next[g];
         }
         if (++stage == C::kStages) {
           stage = 0;
@@ -415,6 +431,223 @@ __global__ void __launch_bounds__(GemmCfg<BN, kInt8>::kThreads, 1)
 
   ptx::tc_fence_before();
   __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Down-projection P = scale * x A with split-K across a thread-block cluster.
+//
+// One cluster per 128-row tile of x; its S CTAs take consecutive slices of K,
+// accumulate 128 x R partial sums in TMEM (tcgen05.mma, N = R), park them in
+// shared memory, and after a cluster barrier each CTA reduces 128/S rows across
+// the S partials through distributed shared memory, scales, rounds and stores
+// its rows of P. No global scratch, deterministic summation order, and small M
+// (decode) still spreads the x and A stream over S SMs.
+//   warp 0: TMA producer; warp 1: TMEM owner + MMA issuer; warps 2-5: epilogue.
+// ---------------------------------------------------------------------------
+template <int R>
+struct DownCfg {
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = R * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = 8;
+  static constexpr int kPartialBytes = kBM * R * 4;
+  static constexpr int kThreads = 192;
+  static constexpr int kTmemCols = R < 32 ? 32 : R;
+  static constexpr size_t kSmemBytes =
+      1024 + static_cast<size_t>(kStages) * kStageBytes + kPartialBytes + 256;
+};
+
+struct DownParams {
+  int M;
+  int num_kb;
+  int kb_per_split;
+  int splits;
+  int a_mn_major;  // A stored [K, r] (r contiguous)
+  float scale;
+  void *out;  // P [M, R] 16-bit
+  unsigned *err;
+};
+
+template <int R, bool kBf16>
+__global__ void __launch_bounds__(DownCfg<R>::kThreads, 1)
+    down_proj_kernel(const __grid_constant__ CUtensorMap tm_x,
+                     const __grid_constant__ CUtensorMap tm_a, const DownParams p) {
+  using C = DownCfg<R>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  float *partial = reinterpret_cast<float *>(smem + C::kStages * C::kStageBytes);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(partial + kBM * R);
+  uint64_t *full = bars;
+  uint64_t *empty = bars + C::kStages;
+  uint64_t *acc_full = bars + 2 * C::kStages;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
+  int *abort_flag = reinterpret_cast<int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / kWarp;
+  const int lane = threadIdx.x % kWarp;
+  const int rank = static_cast<int>(ptx::cluster_ctarank());
+  const int m0 = (blockIdx.x / p.splits) * kBM;
+  const int kb0 = rank * p.kb_per_split;
+  const int nkb = max(0, min(p.num_kb, kb0 + p.kb_per_split) - kb0);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      ptx::mbar_init(&full[s], 1);
+      ptx::mbar_init(&empty[s], 1);
+    }
+    ptx::mbar_init(acc_full, 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, C::kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t outstanding = 0, issue_parity = 0;
+      for (int i = 0; i < nkb; ++i) {
+        if (!ptx::mbar_wait(&empty[stage], phase ^ 1)) {
+          record_timeout(p.err, abort_flag);
+          break;
+        }
+        uint8_t *sa = smem + stage * C::kStageBytes;
+        const int k0 = (kb0 + i) * kBK;
+        ptx::mbar_expect_tx(&full[stage], C::kStageBytes);
+        ptx::tma_load_2d(sa, &tm_x, &full[stage], k0, m0);
+        if (p.a_mn_major) {
+          ptx::tma_load_2d(sa + C::kABytes, &tm_a, &full[stage], 0, k0);
+        } else {
+          ptx::tma_load_2d(sa + C::kABytes, &tm_a, &full[stage], k0, 0);
+        }
+        outstanding |= 1u << stage;
+        issue_parity = (issue_parity & ~(1u << stage)) | (phase << stage);
+        if (++stage == C::kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (aborted(abort_flag)) {
+        for (int s = 0; s < C::kStages; ++s) {
+          if (outstanding & (1u << s)) ptx::mbar_wait(&full[s], (issue_parity >> s) & 1u, 200000000ull);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && nkb > 0) {
+      const uint32_t idesc = ptx::make_idesc_f16(kBf16, kBM, R, false, p.a_mn_major != 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int i = 0; i < nkb; ++i) {
+        if (!ptx::mbar_wait(&full[stage], phase)) {
+          record_timeout(p.err, abort_flag);
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t sa = ptx::smem_addr(smem + stage * C::kStageBytes);
+        const uint32_t sb = sa + C::kABytes;
+        for (int ks = 0; ks < kBK / kUmmaK; ++ks) {
+          const uint64_t adesc = kmajor_desc(sa, 128, ks);
+          const uint64_t bdesc = p.a_mn_major ? mnmajor_desc(sb, R * 2, C::kBBytes, ks)
+                                              : kmajor_desc(sb, 128, ks);
+          ptx::mma_f16(tmem_base, adesc, bdesc, idesc, (i > 0 || ks > 0) ? 1u : 0u);
+        }
+        ptx::mma_commit(&empty[stage]);
+        if (++stage == C::kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      // Also retires everything issued when aborting, before TMEM is freed.
+      ptx::mma_commit(acc_full);
+      if (!ok) ptx::mbar_wait(acc_full, 0, 200000000ull);
+    }
+  } else {
+    // epilogue warps 2..5 cover the four TMEM lane quarters
+    const int quarter = warp % 4;
+    const int row = quarter * 32 + lane;
+    float *prow = partial + row * R;
+    bool have = nkb > 0;
+    if (have) {
+      const bool ok = ptx::mbar_wait(acc_full, 0);
+      if (__any_sync(0xffffffffu, !ok)) {
+        if (lane == 0) record_timeout(p.err, abort_flag);
+        have = false;
+      }
+    }
+    if (have) {
+      ptx::tc_fence_after();
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+#pragma unroll
+      for (int c = 0; c < (R + 31) / 32; ++c) {
+        uint32_t v[32];
+        if constexpr (R >= 32) {
+          ptx::tmem_ld_32x32b_x32(t_row + c * 32, v);
+        } else {
+          ptx::tmem_ld_32x32b_x16(t_row, v);
+        }
+        ptx::tmem_ld_wait();
+        constexpr int kCols = R >= 32 ? 32 : R;
+#pragma unroll
+        for (int e = 0; e < kCols; e += 4) {
+          *reinterpret_cast<float4 *>(prow + c * 32 + e) =
+              make_float4(__uint_as_float(v[e]), __uint_as_float(v[e + 1]),
+                          __uint_as_float(v[e + 2]), __uint_as_float(v[e + 3]));
+        }
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < R; e += 4) *reinterpret_cast<float4 *>(prow + e) = make_float4(0, 0, 0, 0);
+    }
+  }
+
+  // Partials of every CTA are in shared memory; reduce across the cluster.
+  ptx::tc_fence_before();
+  ptx::cluster_sync();
+  {
+    const int rows_per = kBM / p.splits;
+    const int r_begin = rank * rows_per;
+    const int items = rows_per * (R / 4);
+    const uint32_t base = ptx::smem_addr(partial);
+    for (int it = threadIdx.x; it < items; it += C::kThreads) {
+      const int row = r_begin + it / (R / 4);
+      const int c4 = (it % (R / 4)) * 4;
+      const uint32_t off = static_cast<uint32_t>((row * R + c4) * 4);
+      float4 acc = make_float4(0, 0, 0, 0);
+      for (int peer = 0; peer < p.splits; ++peer) {
+        const float4 v = ptx::ld_shared_cluster_f4(ptx::map_shared_rank(base + off, peer));
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      const int grow = m0 + row;
+      if (grow < p.M) {
+        const uint32_t lo = kBf16 ? ptx::pack_bf16x2(acc.x * p.scale, acc.y * p.scale)
+                                  : ptx::pack_f16x2(acc.x * p.scale, acc.y * p.scale);
+        const uint32_t hi = kBf16 ? ptx::pack_bf16x2(acc.z * p.scale, acc.w * p.scale)
+                                  : ptx::pack_f16x2(acc.z * p.scale, acc.w * p.scale);
+        *reinterpret_cast<uint2 *>(static_cast<uint16_t *>(p.out) + static_cast<int64_t>(grow) * R +
+                                   c4) = make_uint2(lo, hi);
+      }
+    }
+  }
+  // No CTA may leave while a peer can still read its shared memory.
+  ptx::cluster_sync();
   if (warp == 1) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem_base, C::kTmemCols);
@@ -508,33 +741,50 @@ struct LinearArgs {
   bool int8;
 };
 
-template <int BN, bool kBf16>
+template <int R, bool kBf16>
 int launch_down_projection(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
+  using C = DownCfg<R>;
   CUtensorMap tm_x, tm_a;
   if (int st = make_map(&tm_x, L.x, 2, L.k, L.m, kBK, kBM, true)) return st;
-  GemmParams p{};
+  DownParams p{};
   p.M = static_cast<int>(L.m);
-  p.N = BN;
-  p.K = static_cast<int>(L.k);
   p.num_kb = static_cast<int>((L.k + kBK - 1) / kBK);
-  p.rank = BN;
-  p.is_bf16 = kBf16;
-  p.out_scale = L.scale;
+  p.scale = L.scale;
   p.out = L.ws;
-  p.ldo = BN;
-  p.n_tiles_n = 1;
-  p.n_tiles = static_cast<int>((L.m + kBM - 1) / kBM);
   p.err = err;
   if (L.a_layout == CF_LAYOUT_REF) {
-    // a [K, r]: r contiguous -> MN-major B operand, one chunk of r columns.
-    if (int st = make_map(&tm_a, L.a, 2, BN, L.k, BN, kBK, true)) return st;
-    p.b_src = kBMNMajor;
+    // a [K, r]: r contiguous -> MN-major B operand, one swizzle row of r elements.
+    if (int st = make_map(&tm_a, L.a, 2, R, L.k, R, kBK, true)) return st;
+    p.a_mn_major = 1;
   } else {
     // a^T [r, K]: K contiguous -> K-major B operand.
-    if (int st = make_map(&tm_a, L.a, 2, L.k, BN, kBK, BN, true)) return st;
-    p.b_src = kBKMajor;
+    if (int st = make_map(&tm_a, L.a, 2, L.k, R, kBK, R, true)) return st;
+    p.a_mn_major = 0;
   }
-  return launch_gemm<BN, kBf16, false>(tm_x, tm_a, tm_x, tm_x, p, stream);
+  // Split K over up to 8 CTAs per row tile while the grid stays within one wave.
+  const int m_tiles = static_cast<int>((L.m + kBM - 1) / kBM);
+  int splits = 1;
+  while (splits < 8 && m_tiles * splits * 2 <= sm_count() && splits * 2 <= p.num_kb) splits *= 2;
+  p.splits = splits;
+  p.kb_per_split = (p.num_kb + splits - 1) / splits;
+
+  auto kernel = down_proj_kernel<R, kBf16>;
+  CFB_TRY_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(C::kSmemBytes)));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(m_tiles * splits));
+  cfg.blockDim = dim3(C::kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  CFB_TRY_CUDA(cudaLaunchKernelEx(&cfg, kernel, tm_x, tm_a, p));
+  return check_launch();
 }
 
 template <bool kBf16>
