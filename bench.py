@@ -203,7 +203,9 @@ class LlamaStackQuant:
     def __init__(self, dist: Dist, n_layers: int = LLAMA7B_LAYERS):
         self.dist = dist
         self.n_layers = n_layers
-        self.layers = [l for l in range(n_layers) if l % dist.world == dist.rank]
+        from cuda_force_b200.sharding import layer_shard
+
+        self.layers = layer_shard(n_layers, dist.rank, dist.world)
         self.elems_per_layer = sum(a * b for a, b in LLAMA7B_LAYER)
 
     def config(self) -> dict:
@@ -623,8 +625,128 @@ class W8Prefill(LoraLinear):
     int8 = True
 
 
+class W8ColumnSharded:
+    """column-sharded W8 + LoRA on a Llama-70B MLP shape + NCCL all-gather."""
+
+    name = "w8_lora_70b_colshard_16384x8192x28672"
+    unit = "TFLOP/s"
+    bound = "tensor"
+    scaling = "strong"
+    flush_l2 = False
+    m, k, n, r, alpha = 16384, 8192, 28672, 64, 128.0
+    chunks = 4
+    kernel = "w8_swap_kernel<256> + down_proj_kernel<64> per row chunk, NCCL all-gather overlapped"
+    dtype = "bf16 x int8->bf16 (fp32 acc)"
+    metric = ("W8+LoRA column-sharded linear TFLOP/s (x [16384,8192], W [28672,8192] int8, "
+              "r 64, all-gather of y)")
+
+    def __init__(self, dist: Dist, _layers: int = 0):
+        self.dist = dist
+
+    def flops(self) -> float:
+        return 2.0 * self.m * self.n * self.k + 2.0 * self.m * self.r * (self.k + self.n)
+
+    def config(self) -> dict:
+        g = self.dist.world
+        return {"workload": self.__doc__.strip(), "m": self.m, "k": self.k, "n": self.n,
+                "rank": self.r, "alpha": self.alpha, "weight": "block-64 int8 codes + fp32 scales",
+                "parallelism": f"column-sharded over {g} GPU(s): {self.n // g} output features "
+                               f"per rank, x and A replicated, y slices all-gathered over NCCL "
+                               f"in {self.chunks} row chunks overlapped with compute",
+                "output": "rank-major [G, rows, N/G] per chunk (no relayout copy)",
+                "values": "x N(0,1), W N(0,0.015), A and B N(0,0.01); W and B seeded per rank",
+                "l2": "inputs larger than L2 (x 268 MB, W codes 235 MB / G)"}
+
+    def setup(self) -> None:
+        import cuda_force_b200 as cf
+        from cuda_force_b200.sharding import column_slice
+
+        dev = self.dist.device
+        g = torch.Generator(device=dev).manual_seed(5)
+        self.x = torch.randn(self.m, self.k, device=dev, generator=g).to(torch.bfloat16)
+        self.a = (torch.randn(self.k, self.r, device=dev, generator=g) * 0.01).to(torch.bfloat16)
+        cols = column_slice(self.n, self.dist.rank, self.dist.world)
+        width = cols.stop - cols.start
+        gw = torch.Generator(device=dev).manual_seed(7 + self.dist.rank)
+        w = (torch.randn(width, self.k, device=dev, generator=gw) * 0.015).to(torch.bfloat16)
+        self.codes, self.scales = cf.quantize_int8(w)
+        del w
+        self.b = (torch.randn(self.r, width, device=dev, generator=gw) * 0.01).to(torch.bfloat16)
+        self.scale = self.alpha / self.r
+        self.work_per_step = self.flops() / self.dist.world
+        self.launches_per_step = 2 * (self.chunks if self.dist.world > 1 else 1)
+        self.last = None
+
+    def step(self, stream) -> None:
+        from cuda_force_b200.sharding import sharded_lora_linear_int8
+
+        group = self.dist.pg.group.WORLD if self.dist.pg is not None else None
+        self.last = sharded_lora_linear_int8(self.x, self.codes, self.scales, self.a, self.b,
+                                             self.scale, group=group, chunks=self.chunks)
+
+    def verify(self) -> None:
+        from oracle import linear_ref
+
+        torch.cuda.synchronize(self.dist.device)
+        w_t = linear_ref.dequantized_weight_t(self.codes, self.scales)
+        rows = torch.randperm(self.m, generator=torch.Generator().manual_seed(0))[:64].tolist()
+        rows.sort()
+        chunk_rows = -(-self.m // (self.chunks if self.dist.world > 1 else 1))
+        got = torch.stack([self.last[r // chunk_rows][self.dist.rank, r % chunk_rows]
+                           for r in rows])
+        ref = linear_ref.lora_linear(self.x[rows], w_t, self.a, self.b, self.scale)
+        err = linear_ref.max_rel_error(got, ref)
+        assert err <= 2e-2, f"{self.name}: max relative error {err}"
+
+    def e2e(self, steps: int) -> dict:
+        dev = self.dist.device
+        hx = self.x.cpu().pin_memory()
+        hy = torch.empty(self.dist.world * self.m * self.codes.shape[0],
+                         dtype=torch.bfloat16).pin_memory()
+
+        def one():
+            from cuda_force_b200.sharding import sharded_lora_linear_int8
+
+            x = hx.to(dev, non_blocking=True)
+            group = self.dist.pg.group.WORLD if self.dist.pg is not None else None
+            parts = sharded_lora_linear_int8(x, self.codes, self.scales, self.a, self.b,
+                                             self.scale, group=group, chunks=self.chunks)
+            off = 0
+            for part in parts:
+                n = part.numel()
+                hy[off:off + n].copy_(part.reshape(-1), non_blocking=True)
+                off += n
+
+        return timed_e2e(self, one, steps, hx.numel() * 2, hy.numel() * 2,
+                         "cuda_force_b200.sharding.sharded_lora_linear_int8 "
+                         "(weights resident, x in, gathered y out)")
+
+    def cpu_sample(self):
+        from oracle import build_ref
+
+        rows = 256
+        have_ref = build_ref.load()
+        x = self.x[:rows].float().cpu()
+        a, b = self.a.float().cpu(), self.b.float().cpu()
+        codes, scales = self.codes.cpu(), self.scales.cpu()
+        width = codes.shape[0]
+
+        def fn():
+            wt = (torch.ops.cudaforge_ref.dequantize_int8(codes, scales) if have_ref
+                  else codes.float()).reshape(width, self.k).t()
+            if have_ref:
+                torch.ops.cudaforge_ref.lora_linear(x, wt, a, b, self.scale)
+            else:
+                x @ wt + self.scale * ((x @ a) @ b)
+
+        work = (2.0 * rows * width * self.k + 2.0 * rows * self.r * (self.k + width))
+        return fn, work, "reference" if have_ref else "port", (
+            f"{rows} rows x this rank's {width} output features in fp32 through the reference's "
+            f"CPU dequantize_int8 + lora_linear (W dequantised every call)")
+
+
 WORKLOADS = {w.name: w for w in (LlamaStackQuant, Config1Quant, Config1Dequant, LoraLinear,
-                                W8Decode, W8Prefill)}
+                                W8Decode, W8Prefill, W8ColumnSharded)}
 
 
 # ---------------------------------------------------------------------------
