@@ -40,6 +40,7 @@ import torch
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
+COMM_MODE = "fused"  # config 5 all-gather: "fused" (peer stores) or "nccl"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 BYTES_PER_ELEM_BF16_QUANT = 2 + 1 + 4 / 64
 
@@ -651,9 +652,12 @@ class W8ColumnSharded:
         return {"workload": self.__doc__.strip(), "m": self.m, "k": self.k, "n": self.n,
                 "rank": self.r, "alpha": self.alpha, "weight": "block-64 int8 codes + fp32 scales",
                 "parallelism": f"column-sharded over {g} GPU(s): {self.n // g} output features "
-                               f"per rank, x and A replicated, y slices all-gathered over NCCL "
-                               f"in {self.chunks} row chunks overlapped with compute",
-                "output": "rank-major [G, rows, N/G] per chunk (no relayout copy)",
+                               f"per rank, x and A replicated; all-gather of y "
+                               + ("fused into the GEMM epilogue (peer stores into every rank's "
+                                  "symmetric-memory y)" if COMM_MODE == "fused" and g > 1 else
+                                  f"by NCCL in {self.chunks} row chunks on a side stream"),
+                "output": ("y [M, N] on every rank" if COMM_MODE == "fused" and g > 1 else
+                           "rank-major [G, rows, N/G] per chunk (no relayout copy)"),
                 "values": "x N(0,1), W N(0,0.015), A and B N(0,0.01); W and B seeded per rank",
                 "l2": "inputs larger than L2 (x 268 MB, W codes 235 MB / G)"}
 
@@ -674,12 +678,24 @@ class W8ColumnSharded:
         self.b = (torch.randn(self.r, width, device=dev, generator=gw) * 0.01).to(torch.bfloat16)
         self.scale = self.alpha / self.r
         self.work_per_step = self.flops() / self.dist.world
-        self.launches_per_step = 2 * (self.chunks if self.dist.world > 1 else 1)
         self.last = None
+        self.fused = None
+        if self.dist.world > 1 and COMM_MODE == "fused":
+            from cuda_force_b200.sharding import FusedGatherLinear
+
+            self.fused = FusedGatherLinear(self.m, self.n, torch.bfloat16, dev)
+            self.kernel = ("w8_swap_kernel<256> with the all-gather fused into the epilogue "
+                           "(peer stores over NVLink) + down_proj_kernel<64>")
+            self.launches_per_step = 2
+        else:
+            self.launches_per_step = 2 * (self.chunks if self.dist.world > 1 else 1)
 
     def step(self, stream) -> None:
         from cuda_force_b200.sharding import sharded_lora_linear_int8
 
+        if self.fused is not None:
+            self.last = self.fused(self.x, self.codes, self.scales, self.a, self.b, self.scale)
+            return
         group = self.dist.pg.group.WORLD if self.dist.pg is not None else None
         self.last = sharded_lora_linear_int8(self.x, self.codes, self.scales, self.a, self.b,
                                              self.scale, group=group, chunks=self.chunks)
@@ -691,9 +707,15 @@ class W8ColumnSharded:
         w_t = linear_ref.dequantized_weight_t(self.codes, self.scales)
         rows = torch.randperm(self.m, generator=torch.Generator().manual_seed(0))[:64].tolist()
         rows.sort()
-        chunk_rows = -(-self.m // (self.chunks if self.dist.world > 1 else 1))
-        got = torch.stack([self.last[r // chunk_rows][self.dist.rank, r % chunk_rows]
-                           for r in rows])
+        if self.fused is not None:
+            width = self.codes.shape[0]
+            got = self.last[rows][:, self.dist.rank * width:(self.dist.rank + 1) * width]
+            peer = (self.dist.rank + 1) % self.dist.world
+            assert torch.isfinite(self.last[:, peer * width:(peer + 1) * width].float()).all()
+        else:
+            chunk_rows = -(-self.m // (self.chunks if self.dist.world > 1 else 1))
+            got = torch.stack([self.last[r // chunk_rows][self.dist.rank, r % chunk_rows]
+                               for r in rows])
         ref = linear_ref.lora_linear(self.x[rows], w_t, self.a, self.b, self.scale)
         err = linear_ref.max_rel_error(got, ref)
         assert err <= 2e-2, f"{self.name}: max relative error {err}"
@@ -709,8 +731,11 @@ class W8ColumnSharded:
 
             x = hx.to(dev, non_blocking=True)
             group = self.dist.pg.group.WORLD if self.dist.pg is not None else None
-            parts = sharded_lora_linear_int8(x, self.codes, self.scales, self.a, self.b,
-                                             self.scale, group=group, chunks=self.chunks)
+            if self.fused is not None:
+                parts = [self.fused(x, self.codes, self.scales, self.a, self.b, self.scale)]
+            else:
+                parts = sharded_lora_linear_int8(x, self.codes, self.scales, self.a, self.b,
+                                                 self.scale, group=group, chunks=self.chunks)
             off = 0
             for part in parts:
                 n = part.numel()
@@ -911,7 +936,11 @@ def main() -> None:
                         help="stack depth (default 32 = BASELINE config 2; smaller only "
                              "for profiling captures)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--comm", choices=["fused", "nccl"], default="fused",
+                        help="config 5 all-gather: fused into the kernel or NCCL")
     args = parser.parse_args()
+    global COMM_MODE
+    COMM_MODE = args.comm
     if args.warmup < 3:
         parser.error("--warmup must be >= 3")
 

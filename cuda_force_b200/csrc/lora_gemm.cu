@@ -674,15 +674,17 @@ __global__ void __launch_bounds__(DownCfg<R>::kThreads, 1)
 //   warp 0 TMA producer, warp 1 TMEM owner + MMA issuer, warps 4-7 epilogue,
 //   warps 8-15 converters.
 // ---------------------------------------------------------------------------
-template <int BT>
+template <int BT, bool kStaged>
 struct W8Cfg {
   static constexpr int kABytes = kBM * kBK * 2;   // converted W tile / adapter B^T tile
   static constexpr int kXBytes = BT * kBK * 2;    // x tile / P tile
   static constexpr int kRawBytes = kBM * kBK;     // int8 codes
   static constexpr int kStageBytes = kABytes + kXBytes + kRawBytes;
-  static constexpr int kStages = BT <= 32 ? 3 : 4;
+  // Pipeline depth: 4 when shared memory allows; the staged epilogue's
+  // 8 KB transpose tile costs one stage at BT = 256.
+  static constexpr int kStages = (BT > 32 && kStaged) || BT <= 32 ? 3 : 4;
   static constexpr bool kSplit = BT <= 32;
-  static constexpr int kPartialBytes = kSplit ? kBM * BT * 4 : 0;
+  static constexpr int kPartialBytes = kSplit ? kBM * BT * 4 : (kStaged ? kBM * 32 * 2 : 0);
   static constexpr int kThreads = 512;
   static constexpr int kMinBlocks = BT <= 32 ? 2 : 1;
   static constexpr int kTmemCols = 2 * BT <= 32 ? 32 : 2 * BT;
@@ -690,6 +692,8 @@ struct W8Cfg {
       1024 + static_cast<size_t>(kStages) * kStageBytes + kPartialBytes + 256;
   static_assert(kStageBytes % 1024 == 0, "stage alignment");
 };
+
+constexpr int kMaxOuts = 8;
 
 struct W8Params {
   int M;             // tokens
@@ -702,24 +706,28 @@ struct W8Params {
   int extra_b_mn;    // B stored [rank, N] (N contiguous)
   const float *w_scales;
   int kb_per_row;
-  void *out;         // y [M, ldo]
-  int ldo;
+  void *out;         // y [M, ldo] (split path)
+  int ldo;           // row stride of every destination (elements)
+  int out_col0;      // first column of this call's features in the destination
+  int n_outs;        // destinations written by the transposing epilogue
+  void *outs[kMaxOuts];
   int n_tiles_w;
   int n_tiles;
   unsigned *err;
 };
 
-template <int BT, bool kBf16>
-__global__ void __launch_bounds__(W8Cfg<BT>::kThreads, W8Cfg<BT>::kMinBlocks)
+template <int BT, bool kBf16, bool kStaged>
+__global__ void __launch_bounds__(W8Cfg<BT, kStaged>::kThreads, W8Cfg<BT, kStaged>::kMinBlocks)
     w8_swap_kernel(const __grid_constant__ CUtensorMap tm_x,
                    const __grid_constant__ CUtensorMap tm_codes,
                    const __grid_constant__ CUtensorMap tm_p,
                    const __grid_constant__ CUtensorMap tm_bt, const W8Params p) {
-  using C = W8Cfg<BT>;
+  using C = W8Cfg<BT, kStaged>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   float *partial = reinterpret_cast<float *>(smem + C::kStages * C::kStageBytes);
+  uint8_t *staging = smem + C::kStages * C::kStageBytes;  // (no split) transpose tile
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kStages * C::kStageBytes +
                                                 C::kPartialBytes);
   uint64_t *full = bars;
@@ -914,14 +922,44 @@ __global__ void __launch_bounds__(W8Cfg<BT>::kThreads, W8Cfg<BT>::kMinBlocks)
             continue;
           }
         }
-        if (n < p.N) {
+        if constexpr (!C::kSplit && kStaged) {
+          // Transpose through shared memory: feature-major accumulator rows
+          // become token rows of 128 features (256 contiguous bytes), written
+          // with 16-byte stores to every destination (this GPU's y and, for
+          // the fused all-gather, each peer's y over NVLink).
+          uint16_t *stg = reinterpret_cast<uint16_t *>(staging);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float f = __uint_as_float(v[j]);
+            const uint32_t h = kBf16 ? ptx::pack_bf16x2(f, 0.0f) : ptx::pack_f16x2(f, 0.0f);
+            stg[j * kBM + row] = static_cast<uint16_t>(h & 0xffffu);
+          }
+          ptx::named_bar_sync(1, 4 * kWarp);
+          const int et = threadIdx.x - kEpiWarp0 * kWarp;  // 0..127
+#pragma unroll
+          for (int pass = 0; pass < 4; ++pass) {
+            const int idx = pass * 4 * kWarp + et;
+            const int j = idx / 16;
+            const int seg = idx % 16;
+            const int t = t0 + c * 32 + j;
+            const int col = w0 + seg * 8;
+            if (t < p.M && col < p.N) {
+              const uint4 val = *reinterpret_cast<const uint4 *>(stg + j * kBM + seg * 8);
+              const int64_t off = static_cast<int64_t>(t) * p.ldo + p.out_col0 + col;
+              for (int d = 0; d < p.n_outs; ++d) {
+                *reinterpret_cast<uint4 *>(static_cast<uint16_t *>(p.outs[d]) + off) = val;
+              }
+            }
+          }
+          ptx::named_bar_sync(1, 4 * kWarp);
+        } else if (n < p.N) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const int t = t0 + c * 32 + j;
             if (t < p.M) {
               const float f = __uint_as_float(v[j]);
               const uint32_t h = kBf16 ? ptx::pack_bf16x2(f, 0.0f) : ptx::pack_f16x2(f, 0.0f);
-              out[static_cast<int64_t>(t) * p.ldo + n] = static_cast<uint16_t>(h & 0xffffu);
+              out[static_cast<int64_t>(t) * p.ldo + p.out_col0 + n] = static_cast<uint16_t>(h & 0xffffu);
             }
           }
         }
@@ -1039,7 +1077,8 @@ __global__ void __launch_bounds__(W8Cfg<BT>::kThreads, W8Cfg<BT>::kMinBlocks)
             if (t < p.M) {
               const uint32_t h = kBf16 ? ptx::pack_bf16x2(vals[j], 0.0f)
                                        : ptx::pack_f16x2(vals[j], 0.0f);
-              out[static_cast<int64_t>(t) * p.ldo + n] = static_cast<uint16_t>(h & 0xffffu);
+              out[static_cast<int64_t>(t) * p.ldo + p.out_col0 + n] =
+                  static_cast<uint16_t>(h & 0xffffu);
             }
           }
         }
@@ -1141,6 +1180,12 @@ struct LinearArgs {
   void *ws;
   size_t ws_bytes;
   bool int8;
+  // Fused all-gather (W8 only): every destination receives this call's
+  // features at columns [col0, col0 + n) of a [m, ldy] matrix.
+  int n_dest = 0;
+  void *const *dest = nullptr;
+  int64_t ldy = 0;
+  int64_t col0 = 0;
 };
 
 template <int R, bool kBf16>
@@ -1189,9 +1234,9 @@ int launch_down_projection(const LinearArgs &L, unsigned *err, cudaStream_t stre
   return check_launch();
 }
 
-template <int BT, bool kBf16>
+template <int BT, bool kBf16, bool kStaged>
 int launch_w8_swap(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
-  using C = W8Cfg<BT>;
+  using C = W8Cfg<BT, kStaged>;
   const int r = static_cast<int>(L.r);
   CUtensorMap tm_x, tm_codes, tm_p, tm_bt;
   int st = CF_OK;
@@ -1216,7 +1261,17 @@ int launch_w8_swap(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
   p.w_scales = L.w_scales;
   p.kb_per_row = static_cast<int>(L.k / kBK);
   p.out = L.y;
-  p.ldo = static_cast<int>(L.n);
+  if (L.n_dest > 0) {
+    p.ldo = static_cast<int>(L.ldy);
+    p.out_col0 = static_cast<int>(L.col0);
+    p.n_outs = L.n_dest;
+    for (int d = 0; d < L.n_dest; ++d) p.outs[d] = L.dest[d];
+  } else {
+    p.ldo = static_cast<int>(L.n);
+    p.out_col0 = 0;
+    p.n_outs = 1;
+    p.outs[0] = L.y;
+  }
   p.n_tiles_w = static_cast<int>((L.n + kBM - 1) / kBM);
   p.n_tiles = p.n_tiles_w * static_cast<int>((L.m + BT - 1) / BT);
   p.err = err;
@@ -1234,7 +1289,7 @@ int launch_w8_swap(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
   p.splits = splits;
   p.kb_per_split = (p.num_kb + splits - 1) / splits;
 
-  auto kernel = w8_swap_kernel<BT, kBf16>;
+  auto kernel = w8_swap_kernel<BT, kBf16, kStaged>;
   CFB_TRY_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(C::kSmemBytes)));
   cudaLaunchConfig_t cfg = {};
@@ -1266,8 +1321,9 @@ int run_linear(const LinearArgs &L, cudaStream_t stream) {
   }
   if (st != CF_OK) return st;
   if (L.int8) {
-    return L.m <= 128 ? launch_w8_swap<32, kBf16>(L, err, stream)
-                      : launch_w8_swap<256, kBf16>(L, err, stream);
+    if (L.n_dest > 0) return launch_w8_swap<256, kBf16, true>(L, err, stream);
+    return L.m <= 128 ? launch_w8_swap<32, kBf16, false>(L, err, stream)
+                      : launch_w8_swap<256, kBf16, false>(L, err, stream);
   }
 
   constexpr int BN = 256;
@@ -1429,6 +1485,29 @@ int cf_lora_linear_int8(const void *x, const int8_t *w_codes, const float *w_sca
                         void *workspace, size_t workspace_bytes, cf_stream_t stream) {
   cfb::LinearArgs L{x, w_codes, CF_LAYOUT_T, w_scales, a, a_layout, b, b_layout, y, m, k, n,
                     rank, scale, dtype, workspace, workspace_bytes, true};
+  if (w_scales != nullptr && !cfb::aligned_to(w_scales, 4)) return CF_ERR_MISALIGNED;
+  return cfb::validate_and_run(L, stream);
+}
+
+int cf_lora_linear_int8_allgather(const void *x, const int8_t *w_codes, const float *w_scales,
+                                  const void *a, int a_layout, const void *b, int b_layout,
+                                  int n_dest, void *const *y_dest, int64_t ldy, int64_t col0,
+                                  int64_t m, int64_t k, int64_t n, int64_t rank, float scale,
+                                  int dtype, void *workspace, size_t workspace_bytes,
+                                  cf_stream_t stream) {
+  if (n_dest < 1 || n_dest > cfb::kMaxOuts || y_dest == nullptr) return CF_ERR_INVALID_ARGUMENT;
+  for (int d = 0; d < n_dest; ++d) {
+    if (y_dest[d] == nullptr) return CF_ERR_INVALID_ARGUMENT;
+    if (!cfb::aligned_to(y_dest[d], 16)) return CF_ERR_MISALIGNED;
+  }
+  if (ldy <= 0 || col0 < 0 || col0 + n > ldy) return CF_ERR_INVALID_ARGUMENT;
+  if (ldy % 8 != 0 || col0 % 8 != 0 || ldy > INT32_MAX) return CF_ERR_UNSUPPORTED;
+  cfb::LinearArgs L{x, w_codes, CF_LAYOUT_T, w_scales, a, a_layout, b, b_layout, y_dest[0], m, k,
+                    n, rank, scale, dtype, workspace, workspace_bytes, true};
+  L.n_dest = n_dest;
+  L.dest = y_dest;
+  L.ldy = ldy;
+  L.col0 = col0;
   if (w_scales != nullptr && !cfb::aligned_to(w_scales, 4)) return CF_ERR_MISALIGNED;
   return cfb::validate_and_run(L, stream);
 }

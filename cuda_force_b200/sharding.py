@@ -97,3 +97,56 @@ def sharded_lora_linear_int8(
     if on_cuda:
         torch.cuda.current_stream(x.device).wait_stream(comm)
     return result
+
+
+class FusedGatherLinear:
+    """Column-sharded W8 + LoRA with the all-gather fused into the kernel.
+
+    The output y [M, N] is a symmetric-memory buffer (one per GPU, mapped into
+    every rank); each rank's kernel writes its own columns into all G copies
+    over NVLink as its tiles complete (``cf_lora_linear_int8_allgather``), so
+    the exchange overlaps the GEMM tile by tile and no relayout is needed.
+    A device-side barrier after the launch orders the ranks before y is read.
+    """
+
+    def __init__(self, m: int, n: int, dtype: torch.dtype, device: torch.device,
+                 group: dist.ProcessGroup | None = None):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self.group = group if group is not None else dist.group.WORLD
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        self.y = symm_mem.empty(m, n, dtype=dtype, device=device)
+        self.handle = symm_mem.rendezvous(self.y, self.group.group_name)
+        peers = [self.handle.get_buffer(r, (m, n), dtype) for r in range(self.world)]
+        self._peers = peers  # keep the views alive
+        import ctypes
+
+        self._dest = (ctypes.c_void_p * self.world)(*[t.data_ptr() for t in peers])
+        self.m, self.n = m, n
+
+    def __call__(self, x, w_codes, w_scales, lora_a, lora_b, scale: float) -> torch.Tensor:
+        import ctypes
+
+        from cuda_force_b200 import _abi
+
+        lib = _abi.load()
+        width, k = w_codes.shape
+        m = x.shape[0]
+        r = lora_a.shape[1]
+        rp = 16 if r <= 16 else 32 if r <= 32 else 64
+        if rp != r:
+            raise ValueError("pad the adapter rank to 16, 32 or 64 first")
+        a_layout = _abi.CF_LAYOUT_REF if lora_a.is_contiguous() else _abi.CF_LAYOUT_T
+        b_layout = _abi.CF_LAYOUT_REF if lora_b.is_contiguous() else _abi.CF_LAYOUT_T
+        ws_bytes = lib.cf_lora_linear_workspace_bytes(m, r)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
+        dtype = _abi.CF_DTYPE_BF16 if x.dtype == torch.bfloat16 else _abi.CF_DTYPE_F16
+        stream = ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)
+        p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+        _abi.check(lib.cf_lora_linear_int8_allgather(
+            p(x), p(w_codes), p(w_scales), p(lora_a), a_layout, p(lora_b), b_layout,
+            self.world, self._dest, self.n, self.rank * width, m, k, width, r, float(scale),
+            dtype, p(ws), ws_bytes, stream), "cf_lora_linear_int8_allgather")
+        self.handle.barrier()
+        return self.y
