@@ -52,14 +52,19 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
                : "memory");
 }
 
+// Upper bound (ns) a waiting thread may be suspended inside one try_wait; the
+// hardware wakes it as soon as the phase completes, so waiting warps stop
+// competing for issue slots without adding latency.
+constexpr uint32_t kSuspendHintNs = 1000000u;
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(addr), "r"(parity)
+      : "r"(addr), "r"(parity), "r"(kSuspendHintNs)
       : "memory");
   return ok != 0;
 }
