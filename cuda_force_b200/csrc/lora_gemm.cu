@@ -1096,364 +1096,6 @@ __global__ void __launch_bounds__(W8Cfg<BT, kStaged>::kThreads, W8Cfg<BT, kStage
 }
 
 // ---------------------------------------------------------------------------
-// W8 + LoRA, swap-AB, prefill shapes (256-token tiles), with the conversion
-// decoupled from the input stream.
-//
-// Two rings: an input ring (x tile 32 KB + a 16 KB slot holding the int8 code
-// tile, or the adapter's B^T tile for the adapter K-steps) kIn deep, and a
-// 2-deep ring of converted 128 x 64 bf16/f16 weight tiles (the MMA's A
-// operand). TMA runs kIn - 1 k-blocks ahead regardless of conversion, the
-// converters run one slot ahead of the MMA. Every iteration flows through the
-// same roles: for the adapter iteration the converters copy the B^T tile into
-// the A slot unchanged. Persistent over tiles, double-buffered TMEM
-// accumulators; the epilogue is the scalar one or, with kStaged, the shared-
-// memory transpose that can write several destinations (fused all-gather).
-// ---------------------------------------------------------------------------
-template <bool kStaged>
-struct W8PipeCfg {
-  static constexpr int BT = 256;
-  static constexpr int kXBytes = BT * kBK * 2;       // 32 KB
-  static constexpr int kRBytes = kBM * 128;          // 16 KB: codes (8 KB) or B^T tile
-  static constexpr int kInBytes = kXBytes + kRBytes;
-  static constexpr int kIn = 3;
-  static constexpr int kConv = 4;
-  static constexpr int kConvWarps = 16;
-  static constexpr int kABytes = kBM * kBK * 2;      // 16 KB
-  static constexpr int kStagingBytes = kStaged ? kBM * 32 * 2 : 0;
-  static constexpr int kThreads = (kConvWarp0 + kConvWarps) * kWarp;  // 768
-  static constexpr int kTmemCols = 512;
-  static constexpr size_t kSmemBytes = 1024 + static_cast<size_t>(kIn) * kInBytes +
-                                       kConv * kABytes + kStagingBytes + 256;
-};
-
-// Position in a ring of N slots: slot index and the parity of its current use.
-template <int N>
-struct Ring {
-  int slot = 0;
-  uint32_t phase = 0;
-  __device__ __forceinline__ void advance() {
-    if (++slot == N) {
-      slot = 0;
-      phase ^= 1u;
-    }
-  }
-};
-
-template <bool kBf16, bool kStaged>
-__global__ void __launch_bounds__(W8PipeCfg<kStaged>::kThreads, 1)
-    w8_pipe_kernel(const __grid_constant__ CUtensorMap tm_x,
-                   const __grid_constant__ CUtensorMap tm_codes,
-                   const __grid_constant__ CUtensorMap tm_p,
-                   const __grid_constant__ CUtensorMap tm_bt, const W8Params p) {
-  using C = W8PipeCfg<kStaged>;
-  constexpr int BT = C::BT;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint8_t *in_ring = smem;
-  uint8_t *conv_ring = smem + C::kIn * C::kInBytes;
-  uint8_t *staging = conv_ring + C::kConv * C::kABytes;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(staging + C::kStagingBytes);
-  uint64_t *in_full = bars;
-  uint64_t *in_empty = bars + C::kIn;
-  uint64_t *conv_full = bars + 2 * C::kIn;
-  uint64_t *conv_empty = conv_full + C::kConv;
-  uint64_t *tmem_full = conv_empty + C::kConv;
-  uint64_t *tmem_empty = tmem_full + 2;
-  uint64_t *drain = tmem_empty + 2;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
-  int *abort_flag = reinterpret_cast<int *>(tmem_slot + 1);
-
-  constexpr int kConvWarps = C::kConvWarps;
-  const int warp = threadIdx.x / kWarp;
-  const int lane = threadIdx.x % kWarp;
-  const bool has_extra = p.extra_ksteps > 0;
-  const int num_iters = p.num_kb + (has_extra ? 1 : 0);
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < C::kIn; ++s) {
-      ptx::mbar_init(&in_full[s], 1);
-      ptx::mbar_init(&in_empty[s], 1 + kConvWarps);
-    }
-    for (int c = 0; c < C::kConv; ++c) {
-      ptx::mbar_init(&conv_full[c], kConvWarps);
-      ptx::mbar_init(&conv_empty[c], 1);
-    }
-    for (int a = 0; a < 2; ++a) {
-      ptx::mbar_init(&tmem_full[a], 1);
-      ptx::mbar_init(&tmem_empty[a], 4 * kWarp);
-    }
-    ptx::mbar_init(drain, 1);
-    *abort_flag = 0;
-    ptx::fence_mbar_init();
-  }
-  if (warp == 1) {
-    ptx::tmem_alloc(tmem_slot, C::kTmemCols);
-    ptx::tmem_relinquish();
-  }
-  ptx::tc_fence_before();
-  __syncthreads();
-  ptx::tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-
-  if (warp == 0) {
-    // ------------------------------------------------------------------ producer
-    if (lane == 0) {
-      uint32_t outstanding = 0, issue_parity = 0;
-      Ring<C::kIn> in;
-      for (int tile = blockIdx.x; tile < p.n_tiles && !aborted(abort_flag); tile += gridDim.x) {
-        const int w0 = (tile % p.n_tiles_w) * kBM;
-        const int t0 = (tile / p.n_tiles_w) * BT;
-        for (int it = 0; it < num_iters; ++it, in.advance()) {
-          const int s = in.slot;
-          const uint32_t ph = in.phase;
-          if (!ptx::mbar_wait(&in_empty[s], ph ^ 1)) {
-            record_timeout(p.err, abort_flag);
-            break;
-          }
-          uint8_t *sx = in_ring + s * C::kInBytes;
-          uint8_t *sr = sx + C::kXBytes;
-          if (it < p.num_kb) {
-            const int k0 = it * kBK;
-            ptx::mbar_expect_tx(&in_full[s], C::kXBytes + kBM * kBK);
-            ptx::tma_load_2d(sx, &tm_x, &in_full[s], k0, t0);
-            ptx::tma_load_2d(sr, &tm_codes, &in_full[s], k0, w0);
-          } else {
-            ptx::mbar_expect_tx(&in_full[s], (kBM + BT) * p.rank * 2);
-            if (p.extra_b_mn) {
-              for (int c = 0; c < kBM / 64; ++c) {
-                ptx::tma_load_2d(sr + c * (p.rank * 128), &tm_bt, &in_full[s], w0 + c * 64, 0);
-              }
-            } else {
-              ptx::tma_load_2d(sr, &tm_bt, &in_full[s], 0, w0);
-            }
-            ptx::tma_load_2d(sx, &tm_p, &in_full[s], 0, t0);
-          }
-          outstanding |= 1u << s;
-          issue_parity = (issue_parity & ~(1u << s)) | (ph << s);
-        }
-      }
-      if (aborted(abort_flag)) {
-        for (int s = 0; s < C::kIn; ++s) {
-          if (outstanding & (1u << s)) ptx::mbar_wait(&in_full[s], (issue_parity >> s) & 1u, 200000000ull);
-        }
-      }
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc_main = ptx::make_idesc_f16(kBf16, kBM, BT, false, false);
-      const uint32_t idesc_extra = ptx::make_idesc_f16(kBf16, kBM, BT, p.extra_b_mn != 0, false);
-      Ring<C::kIn> in;
-      Ring<C::kConv> cv;
-      int local = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; tile < p.n_tiles && ok && !aborted(abort_flag);
-           tile += gridDim.x, ++local) {
-        const int acc = local & 1;
-        const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
-        if (!ptx::mbar_wait(&tmem_empty[acc], acc_phase ^ 1)) {
-          record_timeout(p.err, abort_flag);
-          break;
-        }
-        ptx::tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BT;
-        for (int it = 0; it < num_iters; ++it, in.advance(), cv.advance()) {
-          const int s = in.slot;
-          const int c = cv.slot;
-          if (!ptx::mbar_wait(&conv_full[c], cv.phase) || !ptx::mbar_wait(&in_full[s], in.phase)) {
-            record_timeout(p.err, abort_flag);
-            ok = false;
-            break;
-          }
-          ptx::tc_fence_after();
-          const uint32_t sa = ptx::smem_addr(conv_ring + c * C::kABytes);
-          const uint32_t sx = ptx::smem_addr(in_ring + s * C::kInBytes);
-          if (it < p.num_kb) {
-            for (int ks = 0; ks < kBK / kUmmaK; ++ks) {
-              ptx::mma_f16(d_tmem, kmajor_desc(sa, 128, ks), kmajor_desc(sx, 128, ks), idesc_main,
-                           (it > 0 || ks > 0) ? 1u : 0u);
-            }
-          } else {
-            const int row_bytes = p.rank * 2;
-            for (int ks = 0; ks < p.extra_ksteps; ++ks) {
-              const uint64_t adesc = p.extra_b_mn ? mnmajor_desc(sa, 128, p.rank * 128, ks)
-                                                  : kmajor_desc(sa, row_bytes, ks);
-              ptx::mma_f16(d_tmem, adesc, kmajor_desc(sx, row_bytes, ks), idesc_extra,
-                           (it > 0 || ks > 0) ? 1u : 0u);
-            }
-          }
-          ptx::mma_commit(&in_empty[s]);
-          ptx::mma_commit(&conv_empty[c]);
-        }
-        if (!ok) break;
-        ptx::mma_commit(&tmem_full[acc]);
-      }
-      if (aborted(abort_flag)) {
-        ptx::mma_commit(drain);
-        ptx::mbar_wait(drain, 0, 200000000ull);
-      }
-    }
-  } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) {
-    // ------------------------------------------------------------------ epilogue
-    const int quarter = warp % 4;
-    const int row = quarter * 32 + lane;
-    int local = 0;
-    for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x, ++local) {
-      const int acc = local & 1;
-      const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
-      const int w0 = (tile % p.n_tiles_w) * kBM;
-      const int t0 = (tile / p.n_tiles_w) * BT;
-      const bool ok = ptx::mbar_wait(&tmem_full[acc], acc_phase);
-      if (__any_sync(0xffffffffu, !ok)) {
-        if (lane == 0) record_timeout(p.err, abort_flag);
-        break;
-      }
-      ptx::tc_fence_after();
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BT;
-      const int n = w0 + row;
-#pragma unroll 1
-      for (int c = 0; c < BT / 32; ++c) {
-        uint32_t v[32];
-        ptx::tmem_ld_32x32b_x32(t_row + c * 32, v);
-        ptx::tmem_ld_wait();
-        if constexpr (kStaged) {
-          uint16_t *stg = reinterpret_cast<uint16_t *>(staging);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float f = __uint_as_float(v[j]);
-            const uint32_t h = kBf16 ? ptx::pack_bf16x2(f, 0.0f) : ptx::pack_f16x2(f, 0.0f);
-            stg[j * kBM + row] = static_cast<uint16_t>(h & 0xffffu);
-          }
-          ptx::named_bar_sync(1, 4 * kWarp);
-          const int et = threadIdx.x - kEpiWarp0 * kWarp;
-#pragma unroll
-          for (int pass = 0; pass < 4; ++pass) {
-            const int idx = pass * 4 * kWarp + et;
-            const int j = idx / 16;
-            const int seg = idx % 16;
-            const int t = t0 + c * 32 + j;
-            const int col = w0 + seg * 8;
-            if (t < p.M && col < p.N) {
-              const uint4 val = *reinterpret_cast<const uint4 *>(stg + j * kBM + seg * 8);
-              const int64_t off = static_cast<int64_t>(t) * p.ldo + p.out_col0 + col;
-              for (int d = 0; d < p.n_outs; ++d) {
-                *reinterpret_cast<uint4 *>(static_cast<uint16_t *>(p.outs[d]) + off) = val;
-              }
-            }
-          }
-          ptx::named_bar_sync(1, 4 * kWarp);
-        } else if (n < p.N) {
-          uint16_t *out = static_cast<uint16_t *>(p.outs[0]);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int t = t0 + c * 32 + j;
-            if (t < p.M) {
-              const float f = __uint_as_float(v[j]);
-              const uint32_t h = kBf16 ? ptx::pack_bf16x2(f, 0.0f) : ptx::pack_f16x2(f, 0.0f);
-              out[static_cast<int64_t>(t) * p.ldo + p.out_col0 + n] =
-                  static_cast<uint16_t>(h & 0xffffu);
-            }
-          }
-        }
-      }
-      ptx::tc_fence_before();
-      ptx::mbar_arrive(&tmem_empty[acc]);
-    }
-  } else if (warp >= kConvWarp0) {
-    // ------------------------------------------------------------------ converters
-    constexpr int kGroups = kBM / 8 / kConvWarps;  // 1
-    const int cw = warp - kConvWarp0;
-    const int sub_row = lane / 4;
-    const int chunk = lane % 4;
-    Ring<C::kIn> in;
-    Ring<C::kConv> cv;
-    bool ok = true;
-    for (int tile = blockIdx.x; tile < p.n_tiles && ok; tile += gridDim.x) {
-      const int w0 = (tile % p.n_tiles_w) * kBM;
-      const float *srow[kGroups];
-      float s_cur[kGroups], s_next[kGroups];
-#pragma unroll
-      for (int g = 0; g < kGroups; ++g) {
-        const int n = w0 + (cw + g * kConvWarps) * 8 + sub_row;
-        srow[g] = n < p.N ? p.w_scales + static_cast<int64_t>(n) * p.kb_per_row : nullptr;
-        s_cur[g] = srow[g] != nullptr ? __ldg(srow[g]) : 0.0f;
-      }
-      for (int it = 0; it < num_iters; ++it, in.advance(), cv.advance()) {
-        const int s = in.slot;
-        const int c = cv.slot;
-        const bool main_kb = it < p.num_kb;
-        if (main_kb) {
-#pragma unroll
-          for (int g = 0; g < kGroups; ++g) {
-            s_next[g] = (srow[g] != nullptr && it + 1 < p.num_kb) ? __ldg(srow[g] + it + 1) : 0.0f;
-          }
-        }
-        const bool got = ptx::mbar_wait(&in_full[s], in.phase) &&
-                         ptx::mbar_wait(&conv_empty[c], cv.phase ^ 1u);
-        if (__any_sync(0xffffffffu, !got)) {
-          if (lane == 0) record_timeout(p.err, abort_flag);
-          ok = false;
-          break;
-        }
-        const uint8_t *sr = in_ring + s * C::kInBytes + C::kXBytes;
-        uint8_t *sa = conv_ring + c * C::kABytes;
-        if (main_kb) {
-#pragma unroll
-          for (int g = 0; g < kGroups; ++g) {
-            const int r = (cw + g * kConvWarps) * 8 + sub_row;
-            const float sc = s_cur[g];
-            const uint4 codes = *reinterpret_cast<const uint4 *>(sr + r * kBK + chunk * 16);
-            const uint32_t words[4] = {codes.x, codes.y, codes.z, codes.w};
-            uint32_t outw[8];
-#pragma unroll
-            for (int wd = 0; wd < 4; ++wd) {
-              const uint32_t u = words[wd] ^ 0x80808080u;
-              float f[4];
-#pragma unroll
-              for (int b = 0; b < 4; ++b) {
-                const float biased = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7440u | b));
-                f[b] = __fmul_rn(biased - 8388736.0f, sc);
-              }
-              outw[2 * wd] = kBf16 ? ptx::pack_bf16x2(f[0], f[1]) : ptx::pack_f16x2(f[0], f[1]);
-              outw[2 * wd + 1] = kBf16 ? ptx::pack_bf16x2(f[2], f[3]) : ptx::pack_f16x2(f[2], f[3]);
-            }
-            uint8_t *dst_row = sa + r * 128;
-            const int sw = r & 7;
-            *reinterpret_cast<uint4 *>(dst_row + (((2 * chunk) ^ sw) << 4)) =
-                make_uint4(outw[0], outw[1], outw[2], outw[3]);
-            *reinterpret_cast<uint4 *>(dst_row + (((2 * chunk + 1) ^ sw) << 4)) =
-                make_uint4(outw[4], outw[5], outw[6], outw[7]);
-          }
-#pragma unroll
-          for (int g = 0; g < kGroups; ++g) s_cur[g] = s_next[g];
-        } else {
-          // Adapter B^T tile (already in MMA layout): copy it into the A slot.
-          const int bytes = kBM * p.rank * 2;
-          const int tid = threadIdx.x - kConvWarp0 * kWarp;
-          for (int off = tid * 16; off < bytes; off += kConvWarps * kWarp * 16) {
-            *reinterpret_cast<uint4 *>(sa + off) = *reinterpret_cast<const uint4 *>(sr + off);
-          }
-        }
-        ptx::fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          ptx::mbar_arrive(&conv_full[c]);
-          ptx::mbar_arrive(&in_empty[s]);
-        }
-      }
-    }
-  }
-
-  ptx::tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    ptx::tc_fence_after();
-    ptx::tmem_dealloc(tmem_base, C::kTmemCols);
-  }
-}
-
-// ---------------------------------------------------------------------------
 // Host side: tensor maps and launches.
 // ---------------------------------------------------------------------------
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
@@ -1647,18 +1289,6 @@ int launch_w8_swap(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
   p.splits = splits;
   p.kb_per_split = (p.num_kb + splits - 1) / splits;
 
-  if constexpr (BT == 256 && kStaged) {
-    // Prefill shapes: the decoupled-ring kernel, persistent, no cluster.
-    using PC = W8PipeCfg<kStaged>;
-    auto pk = w8_pipe_kernel<kBf16, kStaged>;
-    CFB_TRY_CUDA(cudaFuncSetAttribute(pk, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(PC::kSmemBytes)));
-    p.splits = 1;
-    p.kb_per_split = p.num_kb;
-    const int grid = std::max(1, std::min(p.n_tiles, sm_count()));
-    pk<<<grid, PC::kThreads, PC::kSmemBytes, stream>>>(tm_x, tm_codes, tm_p, tm_bt, p);
-    return check_launch();
-  }
   auto kernel = w8_swap_kernel<BT, kBf16, kStaged>;
   CFB_TRY_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(C::kSmemBytes)));
