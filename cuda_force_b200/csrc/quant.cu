@@ -472,11 +472,12 @@ struct GroupedArgs {
 // ---------------------------------------------------------------------------
 template <typename T>
 struct TmaQuantCfg {
-  static constexpr int kWarps = sizeof(T) == 4 ? 12 : 20;
+  static constexpr int kWarps = 20;
   static constexpr int kThreads = kWarps * kWarp;
-  static constexpr int kStages = 3;
+  static constexpr int kStages = sizeof(T) == 4 ? 4 : 3;
   static constexpr int kCodeBufs = 2;
-  static constexpr int kTileElems = 1024;                      // per warp tile
+  // per warp tile: 2 KB of input for every dtype (512 fp32 / 1024 16-bit elements)
+  static constexpr int kTileElems = 2048 / static_cast<int>(sizeof(T));
   static constexpr int kBlocks = kTileElems / kQuantBlockSize;  // 16
   static constexpr int kInBytes = kTileElems * static_cast<int>(sizeof(T));
   // per warp: input ring, code staging, scale staging, barriers
@@ -510,13 +511,15 @@ __global__ void __launch_bounds__(TmaQuantCfg<T>::kThreads, 1)
   }
   __syncwarp();
 
-  int seg_p = 0;  // lane 0's segment cursor for loads
+  int seg_p = 0;    // lane 0's segment cursor for loads
+  int p_stage = 0;  // lane 0's next load stage (loads are issued in tile order)
   auto issue_load = [&](int64_t j) {
     const int64_t tile = first + j * step;
     while (tile >= args.unit_end[seg_p]) ++seg_p;
     const int64_t seg_begin = seg_p == 0 ? 0 : args.unit_end[seg_p - 1];
     const T *src = static_cast<const T *>(args.input[seg_p]) + (tile - seg_begin) * C::kTileElems;
-    const int s = static_cast<int>(j % C::kStages);
+    const int s = p_stage;
+    p_stage = p_stage + 1 == C::kStages ? 0 : p_stage + 1;
     ptx::mbar_expect_tx(&full[s], C::kInBytes);
     ptx::bulk_load(in_buf + s * C::kInBytes, src, C::kInBytes, &full[s]);
   };
@@ -528,9 +531,9 @@ __global__ void __launch_bounds__(TmaQuantCfg<T>::kThreads, 1)
   int seg_c = 0;
   int64_t issued = n_mine < C::kStages - 1 ? n_mine : C::kStages - 1;
   bool aborted = false;
+  int s = 0, cb = 0;
+  uint32_t parity = 0;
   for (int64_t j = 0; j < n_mine; ++j) {
-    const int s = static_cast<int>(j % C::kStages);
-    const uint32_t parity = static_cast<uint32_t>((j / C::kStages) & 1);
     const bool ok = ptx::mbar_wait(&full[s], parity);
     if (__any_sync(0xffffffffu, !ok)) {
       if (lane == 0) atomicOr(error_word, kDevErrTimeout);
@@ -542,7 +545,6 @@ __global__ void __launch_bounds__(TmaQuantCfg<T>::kThreads, 1)
     const int64_t seg_begin = seg_c == 0 ? 0 : args.unit_end[seg_c - 1];
     const int64_t elem0 = (tile - seg_begin) * C::kTileElems;
 
-    const int cb = static_cast<int>(j % C::kCodeBufs);
     const uint8_t *src = in_buf + s * C::kInBytes;
     uint8_t *codes_out = code_buf + cb * C::kTileElems;
     float *scales_out = scale_buf + cb * C::kBlocks;
@@ -566,6 +568,11 @@ __global__ void __launch_bounds__(TmaQuantCfg<T>::kThreads, 1)
       ptx::bulk_wait_read<C::kCodeBufs - 1>();
     }
     __syncwarp();
+    if (++s == C::kStages) {
+      s = 0;
+      parity ^= 1u;
+    }
+    cb = cb + 1 == C::kCodeBufs ? 0 : cb + 1;
   }
   if (lane == 0) {
     ptx::bulk_wait_all();
