@@ -40,6 +40,7 @@ import torch
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
+CONFIG1_ROWS = 4096  # rows of 4096 fp32 for the config 1 workloads (--elements)
 COMM_MODE = "fused"  # config 5 all-gather: "fused" (peer stores) or "nccl"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 BYTES_PER_ELEM_BF16_QUANT = 2 + 1 + 4 / 64
@@ -354,13 +355,16 @@ class Config1Quant:
     def __init__(self, dist: Dist, _layers: int = 0):
         self.dist = dist
         op = "dequantise" if self.dequant else "quantise"
-        self.metric = f"INT8 block {op} GB/s (fp32 4096x4096)"
+        self.rows = CONFIG1_ROWS
+        self.metric = f"INT8 block {op} GB/s (fp32 {self.rows}x4096)"
         self.dtype = "int8->f32" if self.dequant else "f32->int8"
         self.kernel = "dequantize_vec_kernel" if self.dequant else "quantize_tma_kernel<f32>"
 
     def config(self) -> dict:
-        return {"workload": f"BASELINE config 1: fp32 [4096,4096] N(0,1) block-64 "
-                            f"{'dequantise' if self.dequant else 'quantise'}",
+        return {"workload": (f"BASELINE config 1: fp32 [4096,4096] N(0,1) block-64 "
+                             f"{'dequantise' if self.dequant else 'quantise'}")
+                if self.rows == 4096 else
+                f"config 1 kernel at [{self.rows},4096] fp32 (size study, not a BASELINE config)",
                 "block": 64, "bytes_per_element": 4 + 1 + 4 / 64,
                 "l2": "flushed between steps (256 MiB write outside the timed events)",
                 "parallelism": f"{self.dist.world} independent replica(s)"}
@@ -371,10 +375,10 @@ class Config1Quant:
         dev = self.dist.device
         self.lib = _abi.load()
         g = torch.Generator(device=dev).manual_seed(1)
-        self.x = torch.randn(4096, 4096, device=dev, generator=g)
-        self.codes = torch.empty(4096, 4096, dtype=torch.int8, device=dev)
-        self.scales = torch.empty(4096 * 64, device=dev)
-        self.out = torch.empty(4096, 4096, device=dev)
+        self.x = torch.randn(self.rows, 4096, device=dev, generator=g)
+        self.codes = torch.empty(self.rows, 4096, dtype=torch.int8, device=dev)
+        self.scales = torch.empty(self.rows * 64, device=dev)
+        self.out = torch.empty(self.rows, 4096, device=dev)
         _abi.check(self.lib.cf_quantize_int8(self.x.data_ptr(), 0, self.codes.data_ptr(),
                                              self.scales.data_ptr(), self.x.numel(), None), "q")
         self.work_per_step = (4 + 1 + 4 / 64) * self.x.numel()
@@ -394,11 +398,12 @@ class Config1Quant:
     def verify(self) -> None:
         from oracle import quant_ref
 
-        rc, rs = quant_ref.quantize(self.x.cpu().numpy())
-        assert (self.codes.cpu().numpy().reshape(-1) == rc).all(), "codes differ from oracle"
+        rows = min(self.rows, 4096)  # a bounded prefix on very large size studies
+        rc, rs = quant_ref.quantize(self.x[:rows].cpu().numpy())
+        assert (self.codes[:rows].cpu().numpy().reshape(-1) == rc).all(), "codes differ"
         if self.dequant:
             ref = quant_ref.dequantize(rc, rs)
-            assert (self.out.cpu().numpy().reshape(-1) == ref).all(), "dequant differs"
+            assert (self.out[:rows].cpu().numpy().reshape(-1) == ref).all(), "dequant differs"
 
     def e2e(self, steps: int) -> dict:
         import cuda_force_b200 as cf
@@ -406,11 +411,11 @@ class Config1Quant:
         dev = self.dist.device
         if self.dequant:
             h_in = [self.codes.cpu().pin_memory(), self.scales.cpu().pin_memory()]
-            h_out = torch.empty(4096, 4096).pin_memory()
+            h_out = torch.empty(self.rows, 4096).pin_memory()
         else:
             h_in = [self.x.cpu().pin_memory()]
-            h_out = [torch.empty(4096, 4096, dtype=torch.int8).pin_memory(),
-                     torch.empty(4096 * 64).pin_memory()]
+            h_out = [torch.empty(self.rows, 4096, dtype=torch.int8).pin_memory(),
+                     torch.empty(self.rows * 64).pin_memory()]
 
         def one():
             d = [t.to(dev, non_blocking=True) for t in h_in]
@@ -936,11 +941,17 @@ def main() -> None:
                         help="stack depth (default 32 = BASELINE config 2; smaller only "
                              "for profiling captures)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--elements", type=int, default=0,
+                        help="config 1 workloads: tensor size (default 4096*4096)")
     parser.add_argument("--comm", choices=["fused", "nccl"], default="fused",
                         help="config 5 all-gather: fused into the kernel or NCCL")
     args = parser.parse_args()
-    global COMM_MODE
+    global COMM_MODE, CONFIG1_ROWS
     COMM_MODE = args.comm
+    if args.elements:
+        if args.elements % 4096:
+            parser.error("--elements must be a multiple of 4096")
+        CONFIG1_ROWS = args.elements // 4096
     if args.warmup < 3:
         parser.error("--warmup must be >= 3")
 
