@@ -1010,17 +1010,20 @@ __global__ void __launch_bounds__(W8Cfg<BT, kStaged>::kThreads, W8Cfg<BT, kStage
             const uint4 codes = *reinterpret_cast<const uint4 *>(raw + r * kBK + chunk * 16);
             const uint32_t words[4] = {codes.x, codes.y, codes.z, codes.w};
             uint32_t outw[8];
+            const uint64_t sc2 = ptx::splat_f32x2(sc);
 #pragma unroll
             for (int wd = 0; wd < 4; ++wd) {
               const uint32_t u = words[wd] ^ 0x80808080u;
-              float f[4];
 #pragma unroll
-              for (int b = 0; b < 4; ++b) {
-                const float biased = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7440u | b));
-                f[b] = __fmul_rn(biased - 8388736.0f, sc);
+              for (int h = 0; h < 2; ++h) {
+                // 2^23 + (q + 128) as floats, then (that - (2^23 + 128)) * s for
+                // two codes per packed f32x2 add and multiply: exactly q * s.
+                const uint32_t b0 = __byte_perm(u, 0x4B000000u, 0x7440u | (2 * h));
+                const uint32_t b1 = __byte_perm(u, 0x4B000000u, 0x7440u | (2 * h + 1));
+                float lo, hi;
+                ptx::dequant_pair(b0, b1, sc2, lo, hi);
+                outw[2 * wd + h] = kBf16 ? ptx::pack_bf16x2(lo, hi) : ptx::pack_f16x2(lo, hi);
               }
-              outw[2 * wd] = kBf16 ? ptx::pack_bf16x2(f[0], f[1]) : ptx::pack_f16x2(f[0], f[1]);
-              outw[2 * wd + 1] = kBf16 ? ptx::pack_bf16x2(f[2], f[3]) : ptx::pack_f16x2(f[2], f[3]);
             }
             uint8_t *dst_row = sa + r * 128;
             const int sw = r & 7;

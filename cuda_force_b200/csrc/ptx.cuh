@@ -275,6 +275,29 @@ __host__ __device__ constexpr uint32_t make_idesc_f16(bool bf16, int m, int n, b
          ((static_cast<uint32_t>(n) >> 3) << 17) | ((static_cast<uint32_t>(m) >> 4) << 24);
 }
 
+// Both lanes of a packed f32x2 set to v.
+__device__ __forceinline__ uint64_t splat_f32x2(float v) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %1};" : "=l"(r) : "r"(__float_as_uint(v)));
+  return r;
+}
+
+// (b - (2^23 + 128)) * s for two biased-code floats b0, b1 with packed f32x2
+// arithmetic (IEEE round-to-nearest per lane, as the scalar FADD/FMUL).
+__device__ __forceinline__ void dequant_pair(uint32_t b0, uint32_t b1, uint64_t s2, float &lo,
+                                             float &hi) {
+  uint32_t r0, r1;
+  asm("{\n\t.reg .b64 t;\n\t"
+      "mov.b64 t, {%2, %3};\n\t"
+      "add.rn.f32x2 t, t, %4;\n\t"
+      "mul.rn.f32x2 t, t, %5;\n\t"
+      "mov.b64 {%0, %1}, t;\n\t}"
+      : "=r"(r0), "=r"(r1)
+      : "r"(b0), "r"(b1), "l"(0xCB000080CB000080ull), "l"(s2));
+  lo = __uint_as_float(r0);
+  hi = __uint_as_float(r1);
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
