@@ -143,11 +143,11 @@ __global__ void __launch_bounds__(GemmCfg<BN, kInt8>::kThreads, 1)
     for (int s = 0; s < C::kStages; ++s) {
       ptx::mbar_init(&full[s], 1);
       ptx::mbar_init(&empty[s], 1);
-      ptx::mbar_init(&conv_full[s], kConvThreads);
+      ptx::mbar_init(&conv_full[s], kConvThreads / kWarp);
     }
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(&tmem_full[a], 1);
-      ptx::mbar_init(&tmem_empty[a], 4 * kWarp);
+      ptx::mbar_init(&tmem_empty[a], 4);
     }
     ptx::mbar_init(drain, 1);
     *abort_flag = 0;
@@ -308,7 +308,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, kInt8>::kThreads, 1)
     for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x, ++local) {
       const int acc = local & 1;
       const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
-      const bool ok = ptx::mbar_wait(&tmem_full[acc], acc_phase);
+      const bool ok = ptx::warp_wait(&tmem_full[acc], acc_phase);
       if (__any_sync(0xffffffffu, !ok)) {
         if (lane == 0) record_timeout(p.err, abort_flag);
         break;
@@ -348,7 +348,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, kInt8>::kThreads, 1)
         }
       }
       ptx::tc_fence_before();
-      ptx::mbar_arrive(&tmem_empty[acc]);
+      ptx::warp_arrive(&tmem_empty[acc]);
     }
   } else if (kInt8 && warp >= kConvWarp0) {
     // ------------------------------------------------------------------ converters
@@ -416,7 +416,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, kInt8>::kThreads, 1)
                 make_uint4(outw[4], outw[5], outw[6], outw[7]);
           }
           ptx::fence_proxy_async_smem();
-          ptx::mbar_arrive(&conv_full[stage]);
+          ptx::warp_arrive(&conv_full[stage]);
 #pragma unroll
           for (int g = 0; g < kGroups; ++g) s_cur[g] = s_next[g];
         }
@@ -754,11 +754,11 @@ __global__ void __launch_bounds__(W8Cfg<BT, kStaged>::kThreads, W8Cfg<BT, kStage
     for (int s = 0; s < C::kStages; ++s) {
       ptx::mbar_init(&full[s], 1);
       ptx::mbar_init(&empty[s], 1);
-      ptx::mbar_init(&conv_full[s], kConvThreads);
+      ptx::mbar_init(&conv_full[s], kConvThreads / kWarp);
     }
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(&tmem_full[a], 1);
-      ptx::mbar_init(&tmem_empty[a], 4 * kWarp);
+      ptx::mbar_init(&tmem_empty[a], 4);
     }
     ptx::mbar_init(drain, 1);
     *abort_flag = 0;
@@ -890,7 +890,7 @@ __global__ void __launch_bounds__(W8Cfg<BT, kStaged>::kThreads, W8Cfg<BT, kStage
       const int row = quarter * 32 + lane;  // output feature within the tile
       bool have = num_iters > 0;
       if (have) {
-        const bool ok = ptx::mbar_wait(&tmem_full[acc], acc_phase);
+        const bool ok = ptx::warp_wait(&tmem_full[acc], acc_phase);
         if (__any_sync(0xffffffffu, !ok)) {
           if (lane == 0) record_timeout(p.err, abort_flag);
           have = false;
@@ -965,7 +965,7 @@ __global__ void __launch_bounds__(W8Cfg<BT, kStaged>::kThreads, W8Cfg<BT, kStage
         }
       }
       ptx::tc_fence_before();
-      ptx::mbar_arrive(&tmem_empty[acc]);
+      ptx::warp_arrive(&tmem_empty[acc]);
     }
   } else if (warp >= kConvWarp0) {
     // ------------------------------------------------------------------ converters
@@ -1033,7 +1033,7 @@ __global__ void __launch_bounds__(W8Cfg<BT, kStaged>::kThreads, W8Cfg<BT, kStage
                 make_uint4(outw[4], outw[5], outw[6], outw[7]);
           }
           ptx::fence_proxy_async_smem();
-          ptx::mbar_arrive(&conv_full[stage]);
+          ptx::warp_arrive(&conv_full[stage]);
 #pragma unroll
           for (int g = 0; g < kGroups; ++g) s_cur[g] = s_next[g];
         }

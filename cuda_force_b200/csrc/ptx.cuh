@@ -83,6 +83,23 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
   }
 }
 
+// Warp-level wait: lane 0 polls the barrier, the result is broadcast and the
+// warp synchronises, which carries the acquired ordering to every lane.
+__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity,
+                                          uint64_t limit_ns = 2000000000ull) {
+  bool ok = true;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, limit_ns);
+  ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+  __syncwarp();
+  return ok;
+}
+
+// Warp-level arrive: one arrival per warp once every lane got here.
+__device__ __forceinline__ void warp_arrive(uint64_t *bar) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
+}
+
 // ---- TMA ----------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar,
                                             int32_t c0, int32_t c1) {
