@@ -1099,6 +1099,300 @@ __global__ void __launch_bounds__(W8Cfg<BT, kStaged>::kThreads, W8Cfg<BT, kStage
 }
 
 // ---------------------------------------------------------------------------
+// W8 + LoRA, swap-AB with 512-token tiles (prefill).
+//
+// Each converted 128 x 32 weight tile feeds two N = 256 MMAs (tokens
+// [t0, t0+256) and [t0+256, t0+512)), so every int8 code is converted once per
+// 512 tokens instead of once per 256 — half the conversion work per FLOP of
+// w8_swap_kernel<256>. The 128 x 512 fp32 accumulator takes all 512 TMEM
+// columns (single buffer); k-blocks are 32 wide (64-byte swizzled rows) so the
+// ring stays 5 stages deep. The adapter runs as rank/16 extra iterations of
+// one K = 16 step each (A = 16 columns of B^T, B = 16 columns of P).
+// ---------------------------------------------------------------------------
+struct W8WideCfg {
+  static constexpr int BT = 512;
+  static constexpr int kBKw = 32;                      // k-block width (elements)
+  static constexpr int kRowBytes = kBKw * 2;           // 64 -> 64-byte swizzle
+  static constexpr int kABytes = kBM * kRowBytes;      // 8 KB
+  static constexpr int kXHalf = 256 * kRowBytes;       // 16 KB
+  static constexpr int kXBytes = 2 * kXHalf;           // 32 KB
+  static constexpr int kRawBytes = kBM * kBKw;         // 4 KB
+  static constexpr int kStageBytes = kABytes + kXBytes + kRawBytes;  // 44 KB
+  static constexpr int kStages = 5;
+  static constexpr int kThreads = 512;
+  static constexpr int kTmemCols = 512;
+  static constexpr size_t kSmemBytes =
+      1024 + static_cast<size_t>(kStages) * kStageBytes + 256;
+  static_assert(kStageBytes % 1024 == 0, "stage alignment");
+};
+
+template <bool kBf16>
+__global__ void __launch_bounds__(W8WideCfg::kThreads, 1)
+    w8_wide_kernel(const __grid_constant__ CUtensorMap tm_x,
+                   const __grid_constant__ CUtensorMap tm_codes,
+                   const __grid_constant__ CUtensorMap tm_p,
+                   const __grid_constant__ CUtensorMap tm_bt, const W8Params p) {
+  using C = W8WideCfg;
+  constexpr int BT = C::BT;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kStages * C::kStageBytes);
+  uint64_t *full = bars;
+  uint64_t *empty = bars + C::kStages;
+  uint64_t *conv_full = bars + 2 * C::kStages;
+  uint64_t *tmem_full = bars + 3 * C::kStages;
+  uint64_t *tmem_empty = tmem_full + 1;
+  uint64_t *drain = tmem_empty + 1;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  int *abort_flag = reinterpret_cast<int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / kWarp;
+  const int lane = threadIdx.x % kWarp;
+  const int n_extra = p.extra_ksteps;  // one K = 16 iteration per 16 adapter columns
+  const int num_iters = p.num_kb + n_extra;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      ptx::mbar_init(&full[s], 1);
+      ptx::mbar_init(&empty[s], 1);
+      ptx::mbar_init(&conv_full[s], kConvThreads / kWarp);
+    }
+    ptx::mbar_init(tmem_full, 1);
+    ptx::mbar_init(tmem_empty, 4);
+    ptx::mbar_init(drain, 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, C::kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t outstanding = 0, issue_parity = 0;
+      for (int tile = blockIdx.x; tile < p.n_tiles && !aborted(abort_flag); tile += gridDim.x) {
+        const int w0 = (tile % p.n_tiles_w) * kBM;
+        const int t0 = (tile / p.n_tiles_w) * BT;
+        for (int it = 0; it < num_iters; ++it) {
+          if (!ptx::mbar_wait(&empty[stage], phase ^ 1)) {
+            record_timeout(p.err, abort_flag);
+            break;
+          }
+          uint8_t *sa = smem + stage * C::kStageBytes;
+          uint8_t *sx = sa + C::kABytes;
+          if (it < p.num_kb) {
+            const int k0 = it * C::kBKw;
+            ptx::mbar_expect_tx(&full[stage], C::kXBytes + C::kRawBytes);
+            ptx::tma_load_2d(sx, &tm_x, &full[stage], k0, t0);
+            ptx::tma_load_2d(sx + C::kXHalf, &tm_x, &full[stage], k0, t0 + 256);
+            ptx::tma_load_2d(sx + C::kXBytes, &tm_codes, &full[stage], k0, w0);
+          } else {
+            const int j0 = (it - p.num_kb) * kUmmaK;  // adapter columns [j0, j0 + 16)
+            ptx::mbar_expect_tx(&full[stage], (kBM + BT) * kUmmaK * 2);
+            if (p.extra_b_mn) {
+              for (int c = 0; c < kBM / 64; ++c) {
+                ptx::tma_load_2d(sa + c * (kUmmaK * 128), &tm_bt, &full[stage], w0 + c * 64, j0);
+              }
+            } else {
+              ptx::tma_load_2d(sa, &tm_bt, &full[stage], j0, w0);
+            }
+            ptx::tma_load_2d(sx, &tm_p, &full[stage], j0, t0);
+            ptx::tma_load_2d(sx + C::kXHalf, &tm_p, &full[stage], j0, t0 + 256);
+          }
+          outstanding |= 1u << stage;
+          issue_parity = (issue_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (aborted(abort_flag)) {
+        for (int s = 0; s < C::kStages; ++s) {
+          if (outstanding & (1u << s)) ptx::mbar_wait(&full[s], (issue_parity >> s) & 1u, 200000000ull);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc_main = ptx::make_idesc_f16(kBf16, kBM, 256, false, false);
+      const uint32_t idesc_extra = ptx::make_idesc_f16(kBf16, kBM, 256, p.extra_b_mn != 0, false);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t conv_parity = 0;
+      int local = 0;
+      for (int tile = blockIdx.x; tile < p.n_tiles && !aborted(abort_flag);
+           tile += gridDim.x, ++local) {
+        if (!ptx::mbar_wait(tmem_empty, static_cast<uint32_t>(local & 1) ^ 1u)) {
+          record_timeout(p.err, abort_flag);
+          break;
+        }
+        ptx::tc_fence_after();
+        bool ok = true;
+        for (int it = 0; it < num_iters; ++it) {
+          const bool main_kb = it < p.num_kb;
+          const uint32_t want = main_kb ? (conv_parity >> stage) & 1u : phase;
+          if (main_kb) conv_parity ^= 1u << stage;
+          if (!ptx::mbar_wait(main_kb ? &conv_full[stage] : &full[stage], want)) {
+            record_timeout(p.err, abort_flag);
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint32_t sa = ptx::smem_addr(smem + stage * C::kStageBytes);
+          const uint32_t sx = sa + C::kABytes;
+          if (main_kb) {
+            for (int ks = 0; ks < C::kBKw / kUmmaK; ++ks) {
+              const uint64_t adesc = kmajor_desc(sa, C::kRowBytes, ks);
+              for (int h = 0; h < 2; ++h) {
+                ptx::mma_f16(tmem_base + h * 256, adesc,
+                             kmajor_desc(sx + h * C::kXHalf, C::kRowBytes, ks), idesc_main,
+                             (it > 0 || ks > 0) ? 1u : 0u);
+              }
+            }
+          } else {
+            const uint64_t adesc = p.extra_b_mn ? mnmajor_desc(sa, 128, kUmmaK * 128, 0)
+                                                : kmajor_desc(sa, kUmmaK * 2, 0);
+            for (int h = 0; h < 2; ++h) {
+              ptx::mma_f16(tmem_base + h * 256, adesc,
+                           kmajor_desc(sx + h * C::kXHalf, kUmmaK * 2, 0), idesc_extra,
+                           it > 0 ? 1u : 0u);
+            }
+          }
+          ptx::mma_commit(&empty[stage]);
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        ptx::mma_commit(tmem_full);
+      }
+      if (aborted(abort_flag)) {
+        ptx::mma_commit(drain);
+        ptx::mbar_wait(drain, 0, 200000000ull);
+      }
+    }
+  } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) {
+    // ------------------------------------------------------------------ epilogue
+    const int quarter = warp % 4;
+    const int row = quarter * 32 + lane;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x, ++local) {
+      const int w0 = (tile % p.n_tiles_w) * kBM;
+      const int t0 = (tile / p.n_tiles_w) * BT;
+      const bool ok = ptx::warp_wait(tmem_full, static_cast<uint32_t>(local & 1));
+      if (!ok) {
+        if (lane == 0) record_timeout(p.err, abort_flag);
+        break;
+      }
+      ptx::tc_fence_after();
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+      const int n = w0 + row;
+      uint16_t *out = static_cast<uint16_t *>(p.outs[0]);
+#pragma unroll 1
+      for (int c = 0; c < BT / 32; ++c) {
+        uint32_t v[32];
+        ptx::tmem_ld_32x32b_x32(t_row + c * 32, v);
+        ptx::tmem_ld_wait();
+        if (n < p.N) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int t = t0 + c * 32 + j;
+            if (t < p.M) {
+              const float f = __uint_as_float(v[j]);
+              const uint32_t h = kBf16 ? ptx::pack_bf16x2(f, 0.0f) : ptx::pack_f16x2(f, 0.0f);
+              out[static_cast<int64_t>(t) * p.ldo + p.out_col0 + n] =
+                  static_cast<uint16_t>(h & 0xffffu);
+            }
+          }
+        }
+      }
+      ptx::tc_fence_before();
+      ptx::warp_arrive(tmem_empty);
+    }
+  } else if (warp >= kConvWarp0) {
+    // ------------------------------------------------------------------ converters
+    // Lane l of converter warp cw: row cw * 16 + l / 2, 16-code half l % 2 of
+    // the 32-code row; writes 32 bytes of the 64-byte swizzled bf16 row
+    // (logical 16-byte chunk c sits at c ^ ((row >> 1) & 3)).
+    const int cw = warp - kConvWarp0;
+    const int r = cw * 16 + lane / 2;
+    const int half = lane & 1;
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x) {
+      const int w0 = (tile % p.n_tiles_w) * kBM;
+      const int n = w0 + r;
+      const float *srow = n < p.N ? p.w_scales + static_cast<int64_t>(n) * p.kb_per_row : nullptr;
+      float s_cur = srow != nullptr ? __ldg(srow) : 0.0f;
+      bool ok = true;
+      for (int it = 0; it < num_iters; ++it) {
+        if (it < p.num_kb) {
+          const float s_next =
+              (srow != nullptr && it + 1 < p.num_kb) ? __ldg(srow + (it + 1) / 2) : 0.0f;
+          const bool got = ptx::mbar_wait(&full[stage], phase);
+          if (__any_sync(0xffffffffu, !got)) {
+            if (lane == 0) record_timeout(p.err, abort_flag);
+            ok = false;
+            break;
+          }
+          uint8_t *sa = smem + stage * C::kStageBytes;
+          const uint8_t *raw = sa + C::kABytes + C::kXBytes;
+          const uint4 codes = *reinterpret_cast<const uint4 *>(raw + r * C::kBKw + half * 16);
+          const uint32_t words[4] = {codes.x, codes.y, codes.z, codes.w};
+          const uint64_t sc2 = ptx::splat_f32x2(s_cur);
+          uint32_t outw[8];
+#pragma unroll
+          for (int wd = 0; wd < 4; ++wd) {
+            const uint32_t u = words[wd] ^ 0x80808080u;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const uint32_t b0 = __byte_perm(u, 0x4B000000u, 0x7440u | (2 * h));
+              const uint32_t b1 = __byte_perm(u, 0x4B000000u, 0x7440u | (2 * h + 1));
+              float lo, hi;
+              ptx::dequant_pair(b0, b1, sc2, lo, hi);
+              outw[2 * wd + h] = kBf16 ? ptx::pack_bf16x2(lo, hi) : ptx::pack_f16x2(lo, hi);
+            }
+          }
+          uint8_t *dst_row = sa + r * C::kRowBytes;
+          const int sw = (r >> 1) & 3;
+          *reinterpret_cast<uint4 *>(dst_row + (((2 * half) ^ sw) << 4)) =
+              make_uint4(outw[0], outw[1], outw[2], outw[3]);
+          *reinterpret_cast<uint4 *>(dst_row + (((2 * half + 1) ^ sw) << 4)) =
+              make_uint4(outw[4], outw[5], outw[6], outw[7]);
+          ptx::fence_proxy_async_smem();
+          ptx::warp_arrive(&conv_full[stage]);
+          s_cur = s_next;
+        }
+        if (++stage == C::kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!ok) break;
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side: tensor maps and launches.
 // ---------------------------------------------------------------------------
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
@@ -1313,6 +1607,48 @@ int launch_w8_swap(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
 }
 
 template <bool kBf16>
+int launch_w8_wide(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
+  using C = W8WideCfg;
+  const int r = static_cast<int>(L.r);
+  CUtensorMap tm_x, tm_codes, tm_p, tm_bt;
+  int st = CF_OK;
+  if ((st = make_map(&tm_x, L.x, 2, L.k, L.m, C::kBKw, 256, true))) return st;
+  if ((st = make_map(&tm_codes, L.w, 1, L.k, L.n, C::kBKw, kBM, false))) return st;
+  if ((st = make_map(&tm_p, L.ws, 2, r, L.m, kUmmaK, 256, true))) return st;
+  W8Params p{};
+  if (L.b_layout == CF_LAYOUT_REF) {
+    if ((st = make_map(&tm_bt, L.b, 2, L.n, r, 64, kUmmaK, true))) return st;
+    p.extra_b_mn = 1;
+  } else {
+    if ((st = make_map(&tm_bt, L.b, 2, r, L.n, kUmmaK, kBM, true))) return st;
+    p.extra_b_mn = 0;
+  }
+  p.M = static_cast<int>(L.m);
+  p.N = static_cast<int>(L.n);
+  p.num_kb = static_cast<int>(L.k / C::kBKw);
+  p.extra_ksteps = r / kUmmaK;
+  p.rank = r;
+  p.w_scales = L.w_scales;
+  p.kb_per_row = static_cast<int>(L.k / kBK);
+  p.splits = 1;
+  p.kb_per_split = p.num_kb;
+  p.out = L.y;
+  p.ldo = static_cast<int>(L.n);
+  p.out_col0 = 0;
+  p.n_outs = 1;
+  p.outs[0] = L.y;
+  p.n_tiles_w = static_cast<int>((L.n + kBM - 1) / kBM);
+  p.n_tiles = p.n_tiles_w * static_cast<int>((L.m + C::BT - 1) / C::BT);
+  p.err = err;
+  auto kernel = w8_wide_kernel<kBf16>;
+  CFB_TRY_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(C::kSmemBytes)));
+  const int grid = std::max(1, std::min(p.n_tiles, sm_count()));
+  kernel<<<grid, C::kThreads, C::kSmemBytes, stream>>>(tm_x, tm_codes, tm_p, tm_bt, p);
+  return check_launch();
+}
+
+template <bool kBf16>
 int run_linear(const LinearArgs &L, cudaStream_t stream) {
   unsigned *err = device_error_word();
   if (err == nullptr) return record_cuda_error(cudaGetLastError());
@@ -1325,7 +1661,7 @@ int run_linear(const LinearArgs &L, cudaStream_t stream) {
   if (st != CF_OK) return st;
   if (L.int8) {
     if (L.m <= 128 && L.n_dest == 0) return launch_w8_swap<32, kBf16, false>(L, err, stream);
-    if (L.n_dest == 0) return launch_w8_swap<256, kBf16, false>(L, err, stream);
+    if (L.n_dest == 0) return launch_w8_wide<kBf16>(L, err, stream);
     return launch_w8_swap<256, kBf16, true>(L, err, stream);
   }
 
