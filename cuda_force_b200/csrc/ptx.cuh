@@ -52,12 +52,24 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
                : "memory");
 }
 
-// Upper bound (ns) a waiting thread may be suspended inside one try_wait; the
-// hardware wakes it as soon as the phase completes, so waiting warps stop
-// competing for issue slots without adding latency.
+// Upper bound (ns) a waiting thread may be suspended inside one try_wait.
+// Waits suspend by default: the suspension frees issue slots for the warps
+// doing work (measured faster for every kernel here than polling).
 constexpr uint32_t kSuspendHintNs = 1000000u;
 
 __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(addr), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint32_t addr, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
@@ -73,14 +85,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
 // Waits that legitimately last long (a whole tile's mainloop) are far shorter
 // than the limit; a false return means a protocol failure, never slowness.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
-                                          uint64_t limit_ns = 2000000000ull) {
+                                          uint64_t limit_ns = 2000000000ull, bool idle = true) {
   const uint32_t addr = smem_addr(bar);
   if (mbar_try_wait(addr, parity)) return true;
   const uint64_t start = global_timer_ns();
   for (uint32_t i = 0;; ++i) {
-    if (mbar_try_wait(addr, parity)) return true;
+    if (idle ? mbar_try_wait_suspend(addr, parity) : mbar_try_wait(addr, parity)) return true;
     if ((i & 255u) == 255u && global_timer_ns() - start > limit_ns) return false;
   }
+}
+
+// Same as mbar_wait (suspending); names waits that last whole tiles.
+__device__ __forceinline__ bool mbar_wait_idle(uint64_t *bar, uint32_t parity) {
+  return mbar_wait(bar, parity, 2000000000ull, true);
 }
 
 // Warp-level wait: lane 0 polls the barrier, the result is broadcast and the
@@ -88,7 +105,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
 __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity,
                                           uint64_t limit_ns = 2000000000ull) {
   bool ok = true;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, limit_ns);
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, limit_ns, true);
   ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
   __syncwarp();
   return ok;

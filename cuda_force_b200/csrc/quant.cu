@@ -534,7 +534,7 @@ __global__ void __launch_bounds__(TmaQuantCfg<T>::kThreads, 1)
   int s = 0, cb = 0;
   uint32_t parity = 0;
   for (int64_t j = 0; j < n_mine; ++j) {
-    const bool ok = ptx::mbar_wait(&full[s], parity);
+    const bool ok = ptx::mbar_wait_idle(&full[s], parity);
     if (__any_sync(0xffffffffu, !ok)) {
       if (lane == 0) atomicOr(error_word, kDevErrTimeout);
       aborted = true;
