@@ -419,6 +419,13 @@ __global__ void __launch_bounds__(GemmCfg<BN, kInt8>::kThreads, 1)
           ptx::warp_arrive(&conv_full[stage]);
 #pragma unroll
           for (int g = 0; g < kGroups; ++g) s_cur[g] = s_next[g];
+        } else if (!ptx::mbar_wait(&full[stage], phase)) {
+          // Adapter stages are not converted, but waiting for them keeps this
+          // warp within one phase of every stage's barrier (a parity wait
+          // cannot tell phase u from phase u - 2).
+          if (lane == 0) record_timeout(p.err, abort_flag);
+          ok = false;
+          break;
         }
         if (++stage == C::kStages) {
           stage = 0;
@@ -1036,6 +1043,13 @@ __global__ void __launch_bounds__(W8Cfg<BT, kStaged>::kThreads, W8Cfg<BT, kStage
           ptx::warp_arrive(&conv_full[stage]);
 #pragma unroll
           for (int g = 0; g < kGroups; ++g) s_cur[g] = s_next[g];
+        } else if (!ptx::mbar_wait(&full[stage], phase)) {
+          // Adapter stages are not converted, but waiting for them keeps this
+          // warp within one phase of every stage's barrier (a parity wait
+          // cannot tell phase u from phase u - 2).
+          if (lane == 0) record_timeout(p.err, abort_flag);
+          ok = false;
+          break;
         }
         if (++stage == C::kStages) {
           stage = 0;
@@ -1109,6 +1123,7 @@ __global__ void __launch_bounds__(W8Cfg<BT, kStaged>::kThreads, W8Cfg<BT, kStage
 // ring stays 5 stages deep. The adapter runs as rank/16 extra iterations of
 // one K = 16 step each (A = 16 columns of B^T, B = 16 columns of P).
 // ---------------------------------------------------------------------------
+template <bool kTmaStore>
 struct W8WideCfg {
   static constexpr int BT = 512;
   static constexpr int kBKw = 32;                      // k-block width (elements)
@@ -1118,26 +1133,36 @@ struct W8WideCfg {
   static constexpr int kXBytes = 2 * kXHalf;           // 32 KB
   static constexpr int kRawBytes = kBM * kBKw;         // 4 KB
   static constexpr int kStageBytes = kABytes + kXBytes + kRawBytes;  // 44 KB
-  static constexpr int kStages = 5;
+  static constexpr int kStages = kTmaStore ? 4 : 5;
+  static constexpr int kSlabBytes = 32 * kBM * 2;      // 32 tokens x 128 features, 8 KB
+  static constexpr int kStagingBytes = kTmaStore ? 2 * kSlabBytes : 0;
   static constexpr int kThreads = 512;
   static constexpr int kTmemCols = 512;
   static constexpr size_t kSmemBytes =
-      1024 + static_cast<size_t>(kStages) * kStageBytes + 256;
+      1024 + static_cast<size_t>(kStages) * kStageBytes + kStagingBytes + 256;
   static_assert(kStageBytes % 1024 == 0, "stage alignment");
 };
 
-template <bool kBf16>
-__global__ void __launch_bounds__(W8WideCfg::kThreads, 1)
+// Output tensor maps of the TMA-store epilogue: one per destination, each a
+// [M, ldy] 16-bit matrix with 32 x 128 boxes.
+struct OutMaps {
+  CUtensorMap map[kMaxOuts];
+};
+
+template <bool kBf16, bool kTmaStore>
+__global__ void __launch_bounds__(W8WideCfg<kTmaStore>::kThreads, 1)
     w8_wide_kernel(const __grid_constant__ CUtensorMap tm_x,
                    const __grid_constant__ CUtensorMap tm_codes,
                    const __grid_constant__ CUtensorMap tm_p,
-                   const __grid_constant__ CUtensorMap tm_bt, const W8Params p) {
-  using C = W8WideCfg;
+                   const __grid_constant__ CUtensorMap tm_bt,
+                   const __grid_constant__ OutMaps out_maps, const W8Params p) {
+  using C = W8WideCfg<kTmaStore>;
   constexpr int BT = C::BT;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kStages * C::kStageBytes);
+  uint8_t *staging = smem + C::kStages * C::kStageBytes;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(staging + C::kStagingBytes);
   uint64_t *full = bars;
   uint64_t *empty = bars + C::kStages;
   uint64_t *conv_full = bars + 2 * C::kStages;
@@ -1287,6 +1312,7 @@ __global__ void __launch_bounds__(W8WideCfg::kThreads, 1)
     // ------------------------------------------------------------------ epilogue
     const int quarter = warp % 4;
     const int row = quarter * 32 + lane;
+    uint32_t slab = 0;
     int local = 0;
     for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x, ++local) {
       const int w0 = (tile % p.n_tiles_w) * kBM;
@@ -1305,7 +1331,30 @@ __global__ void __launch_bounds__(W8WideCfg::kThreads, 1)
         uint32_t v[32];
         ptx::tmem_ld_32x32b_x32(t_row + c * 32, v);
         ptx::tmem_ld_wait();
-        if (n < p.N) {
+        if constexpr (kTmaStore) {
+          // Stage a 32-token x 128-feature slab (token-major, 256-byte rows)
+          // and let the TMA engine store it to every destination; the slab
+          // buffer is double-buffered against the stores still reading it.
+          const bool elected = threadIdx.x == kEpiWarp0 * kWarp;
+          if (elected) ptx::bulk_wait_read<1>();
+          ptx::named_bar_sync(1, 4 * kWarp);
+          uint16_t *stg = reinterpret_cast<uint16_t *>(staging + (slab & 1) * C::kSlabBytes);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float f = __uint_as_float(v[j]);
+            const uint32_t h = kBf16 ? ptx::pack_bf16x2(f, 0.0f) : ptx::pack_f16x2(f, 0.0f);
+            stg[j * kBM + row] = static_cast<uint16_t>(h & 0xffffu);
+          }
+          ptx::fence_proxy_async_smem();
+          ptx::named_bar_sync(1, 4 * kWarp);
+          if (elected) {
+            for (int d = 0; d < p.n_outs; ++d) {
+              ptx::tma_store_2d(&out_maps.map[d], stg, p.out_col0 + w0, t0 + c * 32);
+            }
+            ptx::bulk_commit();
+          }
+          ++slab;
+        } else if (n < p.N) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const int t = t0 + c * 32 + j;
@@ -1320,6 +1369,10 @@ __global__ void __launch_bounds__(W8WideCfg::kThreads, 1)
       }
       ptx::tc_fence_before();
       ptx::warp_arrive(tmem_empty);
+    }
+    if constexpr (kTmaStore) {
+      // Stores must finish reading shared memory before the CTA exits.
+      if (threadIdx.x == kEpiWarp0 * kWarp) ptx::bulk_wait_all();
     }
   } else if (warp >= kConvWarp0) {
     // ------------------------------------------------------------------ converters
@@ -1374,6 +1427,13 @@ __global__ void __launch_bounds__(W8WideCfg::kThreads, 1)
           ptx::fence_proxy_async_smem();
           ptx::warp_arrive(&conv_full[stage]);
           s_cur = s_next;
+        } else if (!ptx::mbar_wait(&full[stage], phase)) {
+          // Adapter stages are not converted, but waiting for them keeps this
+          // warp within one phase of every stage's barrier (a parity wait
+          // cannot tell phase u from phase u - 2).
+          if (lane == 0) record_timeout(p.err, abort_flag);
+          ok = false;
+          break;
         }
         if (++stage == C::kStages) {
           stage = 0;
@@ -1606,9 +1666,9 @@ int launch_w8_swap(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
   return check_launch();
 }
 
-template <bool kBf16>
+template <bool kBf16, bool kTmaStore>
 int launch_w8_wide(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
-  using C = W8WideCfg;
+  using C = W8WideCfg<kTmaStore>;
   const int r = static_cast<int>(L.r);
   CUtensorMap tm_x, tm_codes, tm_p, tm_bt;
   int st = CF_OK;
@@ -1633,18 +1693,32 @@ int launch_w8_wide(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
   p.splits = 1;
   p.kb_per_split = p.num_kb;
   p.out = L.y;
-  p.ldo = static_cast<int>(L.n);
-  p.out_col0 = 0;
-  p.n_outs = 1;
-  p.outs[0] = L.y;
+  OutMaps out_maps;
+  std::memset(&out_maps, 0, sizeof(out_maps));
+  if (L.n_dest > 0) {
+    p.ldo = static_cast<int>(L.ldy);
+    p.out_col0 = static_cast<int>(L.col0);
+    p.n_outs = L.n_dest;
+    for (int d = 0; d < L.n_dest; ++d) p.outs[d] = L.dest[d];
+  } else {
+    p.ldo = static_cast<int>(L.n);
+    p.out_col0 = 0;
+    p.n_outs = 1;
+    p.outs[0] = L.y;
+  }
+  if (kTmaStore) {
+    for (int d = 0; d < p.n_outs; ++d) {
+      if ((st = make_map(&out_maps.map[d], p.outs[d], 2, p.ldo, L.m, kBM, 32, false))) return st;
+    }
+  }
   p.n_tiles_w = static_cast<int>((L.n + kBM - 1) / kBM);
   p.n_tiles = p.n_tiles_w * static_cast<int>((L.m + C::BT - 1) / C::BT);
   p.err = err;
-  auto kernel = w8_wide_kernel<kBf16>;
+  auto kernel = w8_wide_kernel<kBf16, kTmaStore>;
   CFB_TRY_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(C::kSmemBytes)));
   const int grid = std::max(1, std::min(p.n_tiles, sm_count()));
-  kernel<<<grid, C::kThreads, C::kSmemBytes, stream>>>(tm_x, tm_codes, tm_p, tm_bt, p);
+  kernel<<<grid, C::kThreads, C::kSmemBytes, stream>>>(tm_x, tm_codes, tm_p, tm_bt, out_maps, p);
   return check_launch();
 }
 
@@ -1661,8 +1735,7 @@ int run_linear(const LinearArgs &L, cudaStream_t stream) {
   if (st != CF_OK) return st;
   if (L.int8) {
     if (L.m <= 128 && L.n_dest == 0) return launch_w8_swap<32, kBf16, false>(L, err, stream);
-    if (L.n_dest == 0) return launch_w8_wide<kBf16>(L, err, stream);
-    return launch_w8_swap<256, kBf16, true>(L, err, stream);
+    return launch_w8_wide<kBf16, true>(L, err, stream);
   }
 
   constexpr int BN = 256;
@@ -1840,7 +1913,7 @@ int cf_lora_linear_int8_allgather(const void *x, const int8_t *w_codes, const fl
     if (!cfb::aligned_to(y_dest[d], 16)) return CF_ERR_MISALIGNED;
   }
   if (ldy <= 0 || col0 < 0 || col0 + n > ldy) return CF_ERR_INVALID_ARGUMENT;
-  if (ldy % 8 != 0 || col0 % 8 != 0 || ldy > INT32_MAX) return CF_ERR_UNSUPPORTED;
+  if (ldy % 8 != 0 || col0 % 8 != 0 || ldy > INT32_MAX || n % 128 != 0) return CF_ERR_UNSUPPORTED;
   cfb::LinearArgs L{x, w_codes, CF_LAYOUT_T, w_scales, a, a_layout, b, b_layout, y_dest[0], m, k,
                     n, rank, scale, dtype, workspace, workspace_bytes, true};
   L.n_dest = n_dest;

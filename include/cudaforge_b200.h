@@ -144,7 +144,8 @@ CF_API int cf_lora_linear_int8(const void *x, const int8_t *w_codes, const float
  * into every destination y_dest[0 .. n_dest-1]: each a [m, ldy] row-major
  * matrix, typically the same buffer on each GPU of a tensor-parallel group
  * mapped into this process (peer / symmetric memory over NVLink). 1 <= n_dest
- * <= 8, ldy and col0 multiples of 8, destinations 16-byte aligned. The caller
+ * <= 8, n a multiple of 128, ldy and col0 multiples of 8, destinations 16-byte
+ * aligned. The caller
  * orders the ranks (a barrier after the calls) before reading a destination.
  * No counterpart in the reference, which has no multi-GPU linear; it replaces
  * the compute-then-all-gather pair of the column-sharded configuration. */

@@ -174,3 +174,19 @@ def test_baseline_config4_w8_lora(m, cuda_device):
     y = cf.lora_linear_int8(x, codes, scales, a, b, 2.0)
     w_t = linear_ref.dequantized_weight_t(codes, scales)
     assert sampled_rows_error(y, x, w_t, a, b, 2.0, rows=min(m, 256)) <= TIGHT
+
+
+@pytest.mark.parametrize("rank", [16, 32, 64])
+def test_w8_many_tiles_per_cta(rank, cuda_device):
+    # Several 512-token tiles per CTA with rank/16 adapter k-steps each: the
+    # converter warps must stay in phase with stages that carry adapter tiles.
+    g = torch.Generator(device=cuda_device).manual_seed(50 + rank)
+    m, k, n = 4096, 2048, 8192
+    x = torch.randn(m, k, device=cuda_device, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, device=cuda_device, generator=g) * 0.015).to(torch.bfloat16)
+    a = (torch.randn(k, rank, device=cuda_device, generator=g) * 0.01).to(torch.bfloat16)
+    b = (torch.randn(rank, n, device=cuda_device, generator=g) * 0.01).to(torch.bfloat16)
+    codes, scales = cf.quantize_int8(w)
+    y = cf.lora_linear_int8(x, codes, scales, a, b, 2.0)
+    w_t = linear_ref.dequantized_weight_t(codes, scales)
+    assert sampled_rows_error(y, x, w_t, a, b, 2.0, rows=1024) <= TIGHT
