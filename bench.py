@@ -41,7 +41,7 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 CONFIG1_ROWS = 4096  # rows of 4096 fp32 for the config 1 workloads (--elements)
-COMM_MODE = "fused"  # config 5 all-gather: "fused" (peer stores) or "nccl"
+COMM_MODE = "fused"  # config 5 all-gather: "fused" (peer stores), "ce" (copy engines) or "nccl"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 BYTES_PER_ELEM_BF16_QUANT = 2 + 1 + 4 / 64
 
@@ -641,7 +641,7 @@ class W8ColumnSharded:
     flush_l2 = False
     m, k, n, r, alpha = 16384, 8192, 28672, 64, 128.0
     chunks = 4
-    kernel = "w8_swap_kernel<256> + down_proj_kernel<64> per row chunk, NCCL all-gather overlapped"
+    kernel = "w8_wide_kernel + down_proj_kernel<64> per row chunk, NCCL all-gather overlapped"
     dtype = "bf16 x int8->bf16 (fp32 acc)"
     metric = ("W8+LoRA column-sharded linear TFLOP/s (x [16384,8192], W [28672,8192] int8, "
               "r 64, all-gather of y)")
@@ -658,10 +658,13 @@ class W8ColumnSharded:
                 "rank": self.r, "alpha": self.alpha, "weight": "block-64 int8 codes + fp32 scales",
                 "parallelism": f"column-sharded over {g} GPU(s): {self.n // g} output features "
                                f"per rank, x and A replicated; all-gather of y "
-                               + ("fused into the GEMM epilogue (peer stores into every rank's "
+                               + ("fused into the GEMM epilogue (TMA stores into every rank's "
                                   "symmetric-memory y)" if COMM_MODE == "fused" and g > 1 else
+                                  "by the copy engines, one stream per peer, each row group "
+                                  "pushed as soon as the kernel's counter says it is done "
+                                  "(symmetric-memory y)" if COMM_MODE == "ce" and g > 1 else
                                   f"by NCCL in {self.chunks} row chunks on a side stream"),
-                "output": ("y [M, N] on every rank" if COMM_MODE == "fused" and g > 1 else
+                "output": ("y [M, N] on every rank" if COMM_MODE != "nccl" and g > 1 else
                            "rank-major [G, rows, N/G] per chunk (no relayout copy)"),
                 "values": "x N(0,1), W N(0,0.015), A and B N(0,0.01); W and B seeded per rank",
                 "l2": "inputs larger than L2 (x 268 MB, W codes 235 MB / G)"}
@@ -685,12 +688,16 @@ class W8ColumnSharded:
         self.work_per_step = self.flops() / self.dist.world
         self.last = None
         self.fused = None
-        if self.dist.world > 1 and COMM_MODE == "fused":
+        if self.dist.world > 1 and COMM_MODE in ("fused", "ce"):
             from cuda_force_b200.sharding import FusedGatherLinear
 
-            self.fused = FusedGatherLinear(self.m, self.n, torch.bfloat16, dev)
-            self.kernel = ("w8_swap_kernel<256> with the all-gather fused into the epilogue "
-                           "(peer stores over NVLink) + down_proj_kernel<64>")
+            mode = "ce" if COMM_MODE == "ce" else "kernel"
+            self.fused = FusedGatherLinear(self.m, self.n, torch.bfloat16, dev, mode=mode)
+            self.kernel = ("w8_wide_kernel with the all-gather fused into the epilogue "
+                           "(TMA stores to every rank over NVLink) + down_proj_kernel<64>"
+                           if mode == "kernel" else
+                           "w8_wide_kernel (local y + row-group counters) + down_proj_kernel<64>; "
+                           "copy engines push finished row groups to the peers")
             self.launches_per_step = 2
         else:
             self.launches_per_step = 2 * (self.chunks if self.dist.world > 1 else 1)
@@ -943,8 +950,9 @@ def main() -> None:
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--elements", type=int, default=0,
                         help="config 1 workloads: tensor size (default 4096*4096)")
-    parser.add_argument("--comm", choices=["fused", "nccl"], default="fused",
-                        help="config 5 all-gather: fused into the kernel or NCCL")
+    parser.add_argument("--comm", choices=["fused", "ce", "nccl"], default="fused",
+                        help="config 5 all-gather: fused into the kernel, on the copy "
+                             "engines behind per-row-group counters, or NCCL")
     args = parser.parse_args()
     global COMM_MODE, CONFIG1_ROWS
     COMM_MODE = args.comm

@@ -35,6 +35,7 @@
 #include <algorithm>
 #include <atomic>
 #include <cstring>
+#include <mutex>
 
 #include "cf_common.cuh"
 #include "ptx.cuh"
@@ -721,6 +722,11 @@ struct W8Params {
   int n_tiles_w;
   int n_tiles;
   unsigned *err;
+  // Row-group completion counters (wide kernel, copy-engine all-gather):
+  // after a tile's stores have landed, done[row_block / rb_per_group] += 1.
+  unsigned *done;
+  int rb_per_group;
+  int n_groups;
 };
 
 template <int BT, bool kBf16, bool kStaged>
@@ -1369,6 +1375,16 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore>::kThreads, 1)
       }
       ptx::tc_fence_before();
       ptx::warp_arrive(tmem_empty);
+      if constexpr (kTmaStore) {
+        if (p.done != nullptr && threadIdx.x == kEpiWarp0 * kWarp) {
+          // Publish the tile: its stores have completed (not just read
+          // shared memory) before the group counter moves.
+          ptx::bulk_wait_all();
+          ptx::fence_proxy_async_global();
+          __threadfence();
+          atomicAdd(p.done + (t0 / BT) / p.rb_per_group, 1u);
+        }
+      }
     }
     if constexpr (kTmaStore) {
       // Stores must finish reading shared memory before the CTA exits.
@@ -1449,6 +1465,12 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore>::kThreads, 1)
   if (warp == 1) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+  if (p.done != nullptr && threadIdx.x == 0 && aborted(abort_flag)) {
+    // This CTA gave up on some tiles: push every counter past its target so
+    // that copies waiting on them are released (the error word says the
+    // output is invalid).
+    for (int g = 0; g < p.n_groups; ++g) atomicAdd(p.done + g, 1u << 24);
   }
 }
 
@@ -1543,6 +1565,10 @@ struct LinearArgs {
   void *const *dest = nullptr;
   int64_t ldy = 0;
   int64_t col0 = 0;
+  // Row-group completion counters for a copy-engine all-gather (wide kernel).
+  unsigned *done = nullptr;
+  int rb_per_group = 1;
+  int n_groups = 0;
 };
 
 template <int R, bool kBf16>
@@ -1714,6 +1740,9 @@ int launch_w8_wide(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
   p.n_tiles_w = static_cast<int>((L.n + kBM - 1) / kBM);
   p.n_tiles = p.n_tiles_w * static_cast<int>((L.m + C::BT - 1) / C::BT);
   p.err = err;
+  p.done = kTmaStore ? L.done : nullptr;
+  p.rb_per_group = L.rb_per_group;
+  p.n_groups = L.n_groups;
   auto kernel = w8_wide_kernel<kBf16, kTmaStore>;
   CFB_TRY_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(C::kSmemBytes)));
@@ -1925,3 +1954,160 @@ int cf_lora_linear_int8_allgather(const void *x, const int8_t *w_codes, const fl
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Column-sharded W8 linear with the all-gather on the copy engines.
+//
+// The wide kernel stores this rank's columns into the local destination only
+// and, as each tile's stores land, bumps the counter of its row group (at
+// most kCeGroups groups of whole 512-token row blocks). One copy stream per
+// peer waits on each group's counter with a stream wait-value operation and
+// then copies that group's [rows, n] block into the peer's destination with a
+// 2-D memcpy, so NVLink traffic runs on the copy engines while the SMs keep
+// computing the next row groups. The SMs' tile loop never waits for a peer.
+// ---------------------------------------------------------------------------
+namespace cfb {
+namespace {
+
+constexpr int kCeGroups = 16;
+constexpr size_t kCeCounterBytes = 256;  // kCeGroups 32-bit counters, padded
+static_assert(kCeGroups * sizeof(unsigned) <= kCeCounterBytes, "counter area");
+
+using StreamWaitValue32Fn = CUresult (*)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
+
+StreamWaitValue32Fn wait_value_fn() {
+  static std::atomic<StreamWaitValue32Fn> cached{nullptr};
+  StreamWaitValue32Fn fn = cached.load(std::memory_order_acquire);
+  if (fn != nullptr) return fn;
+  void *sym = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint("cuStreamWaitValue32", &sym, cudaEnableDefault, &q) !=
+          cudaSuccess ||
+      q != cudaDriverEntryPointSuccess || sym == nullptr) {
+    return nullptr;
+  }
+  fn = reinterpret_cast<StreamWaitValue32Fn>(sym);
+  cached.store(fn, std::memory_order_release);
+  return fn;
+}
+
+// Copy streams and events of one device, created on first use and kept for
+// the life of the process. Calls on one device serialise their enqueueing on
+// `mu` (the streams and events are shared).
+struct CopyLanes {
+  std::mutex mu;
+  bool ready = false;
+  cudaStream_t streams[kMaxOuts] = {};
+  cudaEvent_t start = nullptr;
+  cudaEvent_t finished[kMaxOuts] = {};
+};
+
+CopyLanes g_copy_lanes[64];
+
+int copy_lanes(CopyLanes **out) {
+  int dev = 0;
+  CFB_TRY_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return CF_ERR_UNSUPPORTED;
+  CopyLanes &lanes = g_copy_lanes[dev];
+  std::lock_guard<std::mutex> lock(lanes.mu);
+  if (!lanes.ready) {
+    int lo = 0, hi = 0;
+    CFB_TRY_CUDA(cudaDeviceGetStreamPriorityRange(&lo, &hi));
+    for (int d = 0; d < kMaxOuts; ++d) {
+      CFB_TRY_CUDA(cudaStreamCreateWithPriority(&lanes.streams[d], cudaStreamNonBlocking, hi));
+      CFB_TRY_CUDA(cudaEventCreateWithFlags(&lanes.finished[d], cudaEventDisableTiming));
+    }
+    CFB_TRY_CUDA(cudaEventCreateWithFlags(&lanes.start, cudaEventDisableTiming));
+    lanes.ready = true;
+  }
+  *out = &lanes;
+  return CF_OK;
+}
+
+}  // namespace
+}  // namespace cfb
+
+size_t cf_lora_linear_int8_allgather_ce_workspace_bytes(int64_t m, int64_t rank) {
+  if (m <= 0 || rank <= 0) return 0;
+  return cfb::workspace_bytes(m, rank) + cfb::kCeCounterBytes;
+}
+
+int cf_lora_linear_int8_allgather_ce(const void *x, const int8_t *w_codes, const float *w_scales,
+                                     const void *a, int a_layout, const void *b, int b_layout,
+                                     int n_dest, void *const *y_dest, int self_dest, int64_t ldy,
+                                     int64_t col0, int64_t m, int64_t k, int64_t n, int64_t rank,
+                                     float scale, int dtype, void *workspace,
+                                     size_t workspace_bytes, cf_stream_t stream) {
+  using namespace cfb;
+  if (n_dest < 1 || n_dest > kMaxOuts || y_dest == nullptr) return CF_ERR_INVALID_ARGUMENT;
+  if (self_dest < 0 || self_dest >= n_dest) return CF_ERR_INVALID_ARGUMENT;
+  for (int d = 0; d < n_dest; ++d) {
+    if (y_dest[d] == nullptr) return CF_ERR_INVALID_ARGUMENT;
+    if (!aligned_to(y_dest[d], 16)) return CF_ERR_MISALIGNED;
+  }
+  if (m < 0 || n < 0) return CF_ERR_INVALID_ARGUMENT;
+  if (ldy <= 0 || col0 < 0 || col0 + n > ldy) return CF_ERR_INVALID_ARGUMENT;
+  if (ldy % 8 != 0 || col0 % 8 != 0 || ldy > INT32_MAX || n % 128 != 0) return CF_ERR_UNSUPPORTED;
+  if (w_scales != nullptr && !aligned_to(w_scales, 4)) return CF_ERR_MISALIGNED;
+  if (m == 0 || n == 0) return CF_OK;
+  const size_t lin = cfb::workspace_bytes(m, rank);
+  if (workspace == nullptr || workspace_bytes < lin + kCeCounterBytes) return CF_ERR_WORKSPACE;
+  constexpr int kRowBlock = W8WideCfg<true>::BT;
+  const int64_t n_rb = (m + kRowBlock - 1) / kRowBlock;
+  const int rb_per_group = static_cast<int>((n_rb + kCeGroups - 1) / kCeGroups);
+  const int n_groups = static_cast<int>((n_rb + rb_per_group - 1) / rb_per_group);
+  const int64_t tiles_w = n / kBM;
+  if (tiles_w * rb_per_group >= (1 << 24)) return CF_ERR_UNSUPPORTED;
+  StreamWaitValue32Fn wait_value = wait_value_fn();
+  if (wait_value == nullptr) return CF_ERR_UNSUPPORTED;
+  CopyLanes *lanes = nullptr;
+  if (int st = copy_lanes(&lanes)) return st;
+
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  unsigned *done = reinterpret_cast<unsigned *>(static_cast<uint8_t *>(workspace) + lin);
+  std::lock_guard<std::mutex> lock(lanes->mu);
+  CFB_TRY_CUDA(cudaMemsetAsync(done, 0, kCeCounterBytes, s));
+  CFB_TRY_CUDA(cudaEventRecord(lanes->start, s));
+  LinearArgs L{x, w_codes, CF_LAYOUT_T, w_scales, a, a_layout, b, b_layout, y_dest[self_dest], m,
+               k, n, rank, scale, dtype, workspace, lin, true};
+  L.n_dest = 1;
+  L.dest = y_dest + self_dest;
+  L.ldy = ldy;
+  L.col0 = col0;
+  L.done = done;
+  L.rb_per_group = rb_per_group;
+  L.n_groups = n_groups;
+  // Only enqueue waits once the kernel that releases them has launched.
+  if (int st = validate_and_run(L, stream)) return st;
+
+  const size_t pitch = static_cast<size_t>(ldy) * 2;
+  const size_t width = static_cast<size_t>(n) * 2;
+  for (int d = 0; d < n_dest; ++d) {
+    if (d != self_dest) CFB_TRY_CUDA(cudaStreamWaitEvent(lanes->streams[d], lanes->start, 0));
+  }
+  for (int g = 0; g < n_groups; ++g) {
+    const int64_t rb0 = static_cast<int64_t>(g) * rb_per_group;
+    const int64_t rb1 = std::min<int64_t>(n_rb, rb0 + rb_per_group);
+    const int64_t r0 = rb0 * kRowBlock;
+    const int64_t r1 = std::min<int64_t>(m, rb1 * kRowBlock);
+    const auto target = static_cast<cuuint32_t>(tiles_w * (rb1 - rb0));
+    const size_t off = static_cast<size_t>(r0) * pitch + static_cast<size_t>(col0) * 2;
+    const auto *src = static_cast<const uint8_t *>(y_dest[self_dest]) + off;
+    for (int d = 0; d < n_dest; ++d) {
+      if (d == self_dest) continue;
+      const CUresult cr =
+          wait_value(reinterpret_cast<CUstream>(lanes->streams[d]),
+                     reinterpret_cast<CUdeviceptr>(done + g), target, CU_STREAM_WAIT_VALUE_GEQ);
+      if (cr != CUDA_SUCCESS) return record_cuda_error(cudaErrorNotSupported);
+      CFB_TRY_CUDA(cudaMemcpy2DAsync(static_cast<uint8_t *>(y_dest[d]) + off, pitch, src, pitch,
+                                     width, static_cast<size_t>(r1 - r0),
+                                     cudaMemcpyDeviceToDevice, lanes->streams[d]));
+    }
+  }
+  for (int d = 0; d < n_dest; ++d) {
+    if (d == self_dest) continue;
+    CFB_TRY_CUDA(cudaEventRecord(lanes->finished[d], lanes->streams[d]));
+    CFB_TRY_CUDA(cudaStreamWaitEvent(s, lanes->finished[d], 0));
+  }
+  return CF_OK;
+}

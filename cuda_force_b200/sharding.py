@@ -107,10 +107,18 @@ class FusedGatherLinear:
     over NVLink as its tiles complete (``cf_lora_linear_int8_allgather``), so
     the exchange overlaps the GEMM tile by tile and no relayout is needed.
     A device-side barrier after the launch orders the ranks before y is read.
+
+    ``mode="ce"`` moves the exchange to the copy engines
+    (``cf_lora_linear_int8_allgather_ce``): the kernel writes only the local
+    copy of y and counts finished tiles per row group, and one copy stream per
+    peer pushes each finished group over NVLink while the SMs compute the next.
     """
 
     def __init__(self, m: int, n: int, dtype: torch.dtype, device: torch.device,
-                 group: dist.ProcessGroup | None = None):
+                 group: dist.ProcessGroup | None = None, mode: str = "kernel"):
+        if mode not in ("kernel", "ce"):
+            raise ValueError(f"unknown exchange mode {mode!r}")
+        self.mode = mode
         import torch.distributed._symmetric_memory as symm_mem
 
         self.group = group if group is not None else dist.group.WORLD
@@ -139,14 +147,22 @@ class FusedGatherLinear:
             raise ValueError("pad the adapter rank to 16, 32 or 64 first")
         a_layout = _abi.CF_LAYOUT_REF if lora_a.is_contiguous() else _abi.CF_LAYOUT_T
         b_layout = _abi.CF_LAYOUT_REF if lora_b.is_contiguous() else _abi.CF_LAYOUT_T
-        ws_bytes = lib.cf_lora_linear_workspace_bytes(m, r)
-        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
         dtype = _abi.CF_DTYPE_BF16 if x.dtype == torch.bfloat16 else _abi.CF_DTYPE_F16
         stream = ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)
         p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
-        _abi.check(lib.cf_lora_linear_int8_allgather(
-            p(x), p(w_codes), p(w_scales), p(lora_a), a_layout, p(lora_b), b_layout,
-            self.world, self._dest, self.n, self.rank * width, m, k, width, r, float(scale),
-            dtype, p(ws), ws_bytes, stream), "cf_lora_linear_int8_allgather")
+        if self.mode == "ce":
+            ws_bytes = lib.cf_lora_linear_int8_allgather_ce_workspace_bytes(m, r)
+            ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
+            _abi.check(lib.cf_lora_linear_int8_allgather_ce(
+                p(x), p(w_codes), p(w_scales), p(lora_a), a_layout, p(lora_b), b_layout,
+                self.world, self._dest, self.rank, self.n, self.rank * width, m, k, width, r,
+                float(scale), dtype, p(ws), ws_bytes, stream), "cf_lora_linear_int8_allgather_ce")
+        else:
+            ws_bytes = lib.cf_lora_linear_workspace_bytes(m, r)
+            ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
+            _abi.check(lib.cf_lora_linear_int8_allgather(
+                p(x), p(w_codes), p(w_scales), p(lora_a), a_layout, p(lora_b), b_layout,
+                self.world, self._dest, self.n, self.rank * width, m, k, width, r, float(scale),
+                dtype, p(ws), ws_bytes, stream), "cf_lora_linear_int8_allgather")
         self.handle.barrier()
         return self.y

@@ -157,6 +157,31 @@ CF_API int cf_lora_linear_int8_allgather(const void *x, const int8_t *w_codes,
                                          float scale, int dtype, void *workspace,
                                          size_t workspace_bytes, cf_stream_t stream);
 
+/* Workspace bytes of cf_lora_linear_int8_allgather_ce: the down-projection
+ * workspace of cf_lora_linear_workspace_bytes plus 256 bytes of row-group
+ * counters. */
+CF_API size_t cf_lora_linear_int8_allgather_ce_workspace_bytes(int64_t m, int64_t rank);
+
+/* Column-sharded W8 linear with the output all-gather on the copy engines.
+ * Same product, destinations and argument rules as
+ * cf_lora_linear_int8_allgather, plus self_dest, the index in y_dest of this
+ * GPU's own destination. The kernel writes only y_dest[self_dest] and counts
+ * finished tiles per row group (up to 16 groups of 512-row blocks); one copy
+ * stream per other destination waits on each group's count (a stream
+ * wait-value operation) and copies that group's [rows, n] block into its
+ * destination while later groups are still being computed. The copies join
+ * `stream` before the call returns its work, so later work on `stream` sees
+ * every destination written. Calls on one device serialise their enqueueing.
+ * No counterpart in the reference (see cf_lora_linear_int8_allgather). */
+CF_API int cf_lora_linear_int8_allgather_ce(const void *x, const int8_t *w_codes,
+                                            const float *w_scales, const void *a, int a_layout,
+                                            const void *b, int b_layout, int n_dest,
+                                            void *const *y_dest, int self_dest, int64_t ldy,
+                                            int64_t col0, int64_t m, int64_t k, int64_t n,
+                                            int64_t rank, float scale, int dtype,
+                                            void *workspace, size_t workspace_bytes,
+                                            cf_stream_t stream);
+
 /* Allocation-free form of cf_lora_linear, for callers that cannot allocate the
  * workspace: hosts whose device memory is reserved up front by another
  * allocator, foreign-language hosts without a CUDA allocator, and loops that

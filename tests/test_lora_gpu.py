@@ -190,3 +190,63 @@ def test_w8_many_tiles_per_cta(rank, cuda_device):
     y = cf.lora_linear_int8(x, codes, scales, a, b, 2.0)
     w_t = linear_ref.dequantized_weight_t(codes, scales)
     assert sampled_rows_error(y, x, w_t, a, b, 2.0, rows=1024) <= TIGHT
+
+
+def _w8_case(m, k, n, rank, device, seed):
+    g = torch.Generator(device=device).manual_seed(seed)
+    x = torch.randn(m, k, device=device, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, device=device, generator=g) * 0.015).to(torch.bfloat16)
+    a = (torch.randn(k, rank, device=device, generator=g) * 0.01).to(torch.bfloat16)
+    b = (torch.randn(rank, n, device=device, generator=g) * 0.01).to(torch.bfloat16)
+    codes, scales = cf.quantize_int8(w)
+    return x, codes, scales, a, b
+
+
+@pytest.mark.parametrize("mode", ["kernel", "ce"])
+@pytest.mark.parametrize(("m", "rank"), [(1536, 64), (700, 16), (5000, 32)])
+def test_multi_destination_entry_points(mode, m, rank, cuda_device):
+    # Three destinations on one GPU stand in for three ranks' copies of y; this
+    # call owns columns [col0, col0 + n) of each [m, ldy] destination.
+    k, n, ldy, col0 = 1024, 1024, 3072, 1024
+    x, codes, scales, a, b = _w8_case(m, k, n, rank, cuda_device, seed=m + rank)
+    dests = [torch.full((m, ldy), 7.0, dtype=torch.bfloat16, device=cuda_device) for _ in range(3)]
+    ptrs = (ctypes.c_void_p * 3)(*[t.data_ptr() for t in dests])
+    lib = _abi.load()
+    s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    if mode == "ce":
+        ws_bytes = lib.cf_lora_linear_int8_allgather_ce_workspace_bytes(m, rank)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=cuda_device)
+        _abi.check(lib.cf_lora_linear_int8_allgather_ce(
+            p(x), p(codes), p(scales), p(a), _abi.CF_LAYOUT_REF, p(b), _abi.CF_LAYOUT_REF, 3, ptrs,
+            1, ldy, col0, m, k, n, rank, 2.0, _abi.CF_DTYPE_BF16, p(ws), ws_bytes, s),
+            "cf_lora_linear_int8_allgather_ce")
+    else:
+        ws_bytes = lib.cf_lora_linear_workspace_bytes(m, rank)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=cuda_device)
+        _abi.check(lib.cf_lora_linear_int8_allgather(
+            p(x), p(codes), p(scales), p(a), _abi.CF_LAYOUT_REF, p(b), _abi.CF_LAYOUT_REF, 3, ptrs,
+            ldy, col0, m, k, n, rank, 2.0, _abi.CF_DTYPE_BF16, p(ws), ws_bytes, s),
+            "cf_lora_linear_int8_allgather")
+    torch.cuda.synchronize()
+    assert lib.cf_device_status() == _abi.CF_OK
+    y = cf.lora_linear_int8(x, codes, scales, a, b, 2.0)
+    for d in dests:
+        assert torch.equal(d[:, col0:col0 + n], y)
+        assert (d[:, :col0] == 7.0).all() and (d[:, col0 + n:] == 7.0).all()
+    w_t = linear_ref.dequantized_weight_t(codes, scales)
+    assert sampled_rows_error(y, x, w_t, a, b, 2.0, rows=256) <= TIGHT
+
+
+def test_copy_engine_entry_point_rejects_bad_arguments(cuda_device):
+    lib = _abi.load()
+    dest = torch.empty(512, 256, dtype=torch.bfloat16, device=cuda_device)
+    ptrs = (ctypes.c_void_p * 1)(dest.data_ptr())
+    z = ctypes.c_void_p(dest.data_ptr())
+    ws = ctypes.c_void_p(dest.data_ptr())
+    args = (z, z, z, z, 0, z, 0, 1, ptrs)
+    tail = (256, 0, 512, 512, 128, 16, 1.0, _abi.CF_DTYPE_BF16, ws, 16, None)
+    # self_dest outside [0, n_dest)
+    assert lib.cf_lora_linear_int8_allgather_ce(*args, 1, *tail) == _abi.CF_ERR_INVALID_ARGUMENT
+    # workspace smaller than the counters need
+    assert lib.cf_lora_linear_int8_allgather_ce(*args, 0, *tail) == _abi.CF_ERR_WORKSPACE
