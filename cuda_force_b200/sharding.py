@@ -104,8 +104,10 @@ class FusedGatherLinear:
 
     The output y [M, N] is a symmetric-memory buffer (one per GPU, mapped into
     every rank); each rank's kernel writes its own columns into all G copies
-    over NVLink as its tiles complete (``cf_lora_linear_int8_allgather``), so
-    the exchange overlaps the GEMM tile by tile and no relayout is needed.
+    over NVLink as its tiles complete (``cf_lora_linear_int8_allgather``: the
+    epilogue stores the local copy, a forwarding warp pushes each finished tile
+    to the peers), so the exchange overlaps the GEMM tile by tile and no
+    relayout is needed.
     A device-side barrier after the launch orders the ranks before y is read.
 
     ``mode="ce"`` moves the exchange to the copy engines
@@ -162,7 +164,7 @@ class FusedGatherLinear:
             ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
             _abi.check(lib.cf_lora_linear_int8_allgather(
                 p(x), p(w_codes), p(w_scales), p(lora_a), a_layout, p(lora_b), b_layout,
-                self.world, self._dest, self.n, self.rank * width, m, k, width, r, float(scale),
-                dtype, p(ws), ws_bytes, stream), "cf_lora_linear_int8_allgather")
+                self.world, self._dest, self.rank, self.n, self.rank * width, m, k, width, r,
+                float(scale), dtype, p(ws), ws_bytes, stream), "cf_lora_linear_int8_allgather")
         self.handle.barrier()
         return self.y

@@ -138,21 +138,25 @@ CF_API int cf_lora_linear_int8(const void *x, const int8_t *w_codes, const float
                         int64_t m, int64_t k, int64_t n, int64_t rank, float scale, int dtype,
                         void *workspace, size_t workspace_bytes, cf_stream_t stream);
 
-/* Column-sharded W8 linear with the output all-gather fused into the epilogue.
+/* Column-sharded W8 linear with the output all-gather fused into the kernel.
  * This rank computes output features [col0, col0 + n) (its rows of the int8
- * weight, w_codes [n, k], and its columns of b) and writes them, row by row,
- * into every destination y_dest[0 .. n_dest-1]: each a [m, ldy] row-major
- * matrix, typically the same buffer on each GPU of a tensor-parallel group
- * mapped into this process (peer / symmetric memory over NVLink). 1 <= n_dest
- * <= 8, n a multiple of 128, ldy and col0 multiples of 8, destinations 16-byte
- * aligned. The caller
- * orders the ranks (a barrier after the calls) before reading a destination.
+ * weight, w_codes [n, k], and its columns of b) and writes them into every
+ * destination y_dest[0 .. n_dest-1]: each a [m, ldy] row-major matrix,
+ * typically the same buffer on each GPU of a tensor-parallel group mapped into
+ * this process (peer / symmetric memory over NVLink). y_dest[self_dest] is
+ * this GPU's own copy: the epilogue stores each finished tile there, and a
+ * forwarding warp of the same kernel streams it from there to the other
+ * destinations while later tiles compute. 1 <= n_dest <= 8, 0 <= self_dest <
+ * n_dest, n a multiple of 128, ldy and col0 multiples of 8, destinations
+ * 16-byte aligned. The caller orders the ranks (a barrier after the calls)
+ * before reading a destination.
  * No counterpart in the reference, which has no multi-GPU linear; it replaces
  * the compute-then-all-gather pair of the column-sharded configuration. */
 CF_API int cf_lora_linear_int8_allgather(const void *x, const int8_t *w_codes,
                                          const float *w_scales, const void *a, int a_layout,
                                          const void *b, int b_layout, int n_dest,
-                                         void *const *y_dest, int64_t ldy, int64_t col0,
+                                         void *const *y_dest, int self_dest, int64_t ldy,
+                                         int64_t col0,
                                          int64_t m, int64_t k, int64_t n, int64_t rank,
                                          float scale, int dtype, void *workspace,
                                          size_t workspace_bytes, cf_stream_t stream);

@@ -226,7 +226,7 @@ def test_multi_destination_entry_points(mode, m, rank, cuda_device):
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=cuda_device)
         _abi.check(lib.cf_lora_linear_int8_allgather(
             p(x), p(codes), p(scales), p(a), _abi.CF_LAYOUT_REF, p(b), _abi.CF_LAYOUT_REF, 3, ptrs,
-            ldy, col0, m, k, n, rank, 2.0, _abi.CF_DTYPE_BF16, p(ws), ws_bytes, s),
+            1, ldy, col0, m, k, n, rank, 2.0, _abi.CF_DTYPE_BF16, p(ws), ws_bytes, s),
             "cf_lora_linear_int8_allgather")
     torch.cuda.synchronize()
     assert lib.cf_device_status() == _abi.CF_OK
