@@ -718,7 +718,7 @@ struct W8Params {
   int ldo;           // row stride of every destination (elements)
   int out_col0;      // first column of this call's features in the destination
   int n_outs;        // destinations written by the transposing epilogue
-  int self_out;      // wide kernel: the destination on this GPU (the others are forwarded)
+  int self_out;      // wide kernel: index of the destination on this GPU (stored first)
   void *outs[kMaxOuts];
   int n_tiles_w;
   int n_tiles;
@@ -1142,8 +1142,7 @@ struct W8WideCfg {
   static constexpr int kStageBytes = kABytes + kXBytes + kRawBytes;  // 44 KB
   static constexpr int kStages = kTmaStore ? 4 : 5;
   static constexpr int kSlabBytes = 32 * kBM * 2;      // 32 tokens x 128 features, 8 KB
-  // Epilogue slabs [0, 2) and the forwarder's ring [2, 4).
-  static constexpr int kStagingBytes = kTmaStore ? 4 * kSlabBytes : 0;
+  static constexpr int kStagingBytes = kTmaStore ? 2 * kSlabBytes : 0;
   static constexpr int kThreads = 512;
   static constexpr int kTmemCols = 512;
   static constexpr size_t kSmemBytes =
@@ -1177,17 +1176,13 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore>::kThreads, 1)
   uint64_t *tmem_full = bars + 3 * C::kStages;
   uint64_t *tmem_empty = tmem_full + 1;
   uint64_t *drain = tmem_empty + 1;
-  uint64_t *stored = drain + 1;      // [2] epilogue -> forwarder: tile landed in the local y
-  uint64_t *forwarded = stored + 2;  // [2] forwarder -> epilogue: tile slot free again
-  uint64_t *fwd_full = forwarded + 2;  // [2] forwarder ring: slab loaded
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(fwd_full + 2);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
   int *abort_flag = reinterpret_cast<int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x / kWarp;
   const int lane = threadIdx.x % kWarp;
   const int n_extra = p.extra_ksteps;  // one K = 16 iteration per 16 adapter columns
   const int num_iters = p.num_kb + n_extra;
-  const bool forward = kTmaStore && p.n_outs > 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
@@ -1198,11 +1193,6 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore>::kThreads, 1)
     ptx::mbar_init(tmem_full, 1);
     ptx::mbar_init(tmem_empty, 4);
     ptx::mbar_init(drain, 1);
-    for (int i = 0; i < 2; ++i) {
-      ptx::mbar_init(&stored[i], 1);
-      ptx::mbar_init(&forwarded[i], 1);
-      ptx::mbar_init(&fwd_full[i], 1);
-    }
     *abort_flag = 0;
     ptx::fence_mbar_init();
   }
@@ -1365,7 +1355,11 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore>::kThreads, 1)
           ptx::fence_proxy_async_smem();
           ptx::named_bar_sync(1, 4 * kWarp);
           if (elected) {
+            // The local copy first, then the peers (NVLink).
             ptx::tma_store_2d(&out_maps.map[p.self_out], stg, p.out_col0 + w0, t0 + c * 32);
+            for (int d = 0; d < p.n_outs; ++d) {
+              if (d != p.self_out) ptx::tma_store_2d(&out_maps.map[d], stg, p.out_col0 + w0, t0 + c * 32);
+            }
             ptx::bulk_commit();
           }
           ++slab;
@@ -1385,18 +1379,6 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore>::kThreads, 1)
       ptx::tc_fence_before();
       ptx::warp_arrive(tmem_empty);
       if constexpr (kTmaStore) {
-        if (forward && threadIdx.x == kEpiWarp0 * kWarp) {
-          // Hand the tile to the forwarder once its local stores have landed;
-          // the forwarder may lag by at most two tiles.
-          const int slot = local & 1;
-          if (!ptx::mbar_wait_idle(&forwarded[slot], static_cast<uint32_t>((local >> 1) & 1) ^ 1u)) {
-            record_timeout(p.err, abort_flag);
-            break;
-          }
-          ptx::bulk_wait_all();
-          ptx::fence_proxy_async_global();
-          ptx::mbar_arrive(&stored[slot]);
-        }
         if (p.done != nullptr && threadIdx.x == kEpiWarp0 * kWarp) {
           // Publish the tile: its stores have completed (not just read
           // shared memory) before the group counter moves.
@@ -1410,46 +1392,6 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore>::kThreads, 1)
     if constexpr (kTmaStore) {
       // Stores must finish reading shared memory before the CTA exits.
       if (threadIdx.x == kEpiWarp0 * kWarp) ptx::bulk_wait_all();
-    }
-  } else if (warp == 2) {
-    // ------------------------------------------------------------------ forwarder
-    // Streams each finished tile back from the local y (L2-resident) through
-    // a two-slab ring and TMA-stores it to every other destination, so the
-    // NVLink traffic overlaps the following tiles' main loops.
-    if (forward && lane == 0) {
-      uint8_t *ring = staging + 2 * C::kSlabBytes;
-      uint32_t q = 0;
-      int local = 0;
-      for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x, ++local) {
-        const int w0 = (tile % p.n_tiles_w) * kBM;
-        const int t0 = (tile / p.n_tiles_w) * BT;
-        const int slot = local & 1;
-        if (!ptx::mbar_wait_idle(&stored[slot], static_cast<uint32_t>((local >> 1) & 1))) {
-          record_timeout(p.err, abort_flag);
-          break;
-        }
-        ptx::fence_proxy_async_global();
-        bool ok = true;
-        for (int c = 0; c < BT / 32 && t0 + c * 32 < p.M; ++c, ++q) {
-          uint8_t *buf = ring + (q & 1) * C::kSlabBytes;
-          ptx::bulk_wait_read<1>();
-          ptx::mbar_expect_tx(&fwd_full[q & 1], C::kSlabBytes);
-          ptx::tma_load_2d(buf, &out_maps.map[p.self_out], &fwd_full[q & 1], p.out_col0 + w0,
-                           t0 + c * 32);
-          if (!ptx::mbar_wait(&fwd_full[q & 1], (q >> 1) & 1u)) {
-            record_timeout(p.err, abort_flag);
-            ok = false;
-            break;
-          }
-          for (int d = 0; d < p.n_outs; ++d) {
-            if (d != p.self_out) ptx::tma_store_2d(&out_maps.map[d], buf, p.out_col0 + w0, t0 + c * 32);
-          }
-          ptx::bulk_commit();
-        }
-        ptx::mbar_arrive(&forwarded[slot]);
-        if (!ok) break;
-      }
-      ptx::bulk_wait_all();
     }
   } else if (warp >= kConvWarp0) {
     // ------------------------------------------------------------------ converters

@@ -105,9 +105,8 @@ class FusedGatherLinear:
     The output y [M, N] is a symmetric-memory buffer (one per GPU, mapped into
     every rank); each rank's kernel writes its own columns into all G copies
     over NVLink as its tiles complete (``cf_lora_linear_int8_allgather``: the
-    epilogue stores the local copy, a forwarding warp pushes each finished tile
-    to the peers), so the exchange overlaps the GEMM tile by tile and no
-    relayout is needed.
+    epilogue TMA-stores each staged block to the local copy and every peer's),
+    so the exchange overlaps the GEMM tile by tile and no relayout is needed.
     A device-side barrier after the launch orders the ranks before y is read.
 
     ``mode="ce"`` moves the exchange to the copy engines

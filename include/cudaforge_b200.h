@@ -144,9 +144,9 @@ CF_API int cf_lora_linear_int8(const void *x, const int8_t *w_codes, const float
  * destination y_dest[0 .. n_dest-1]: each a [m, ldy] row-major matrix,
  * typically the same buffer on each GPU of a tensor-parallel group mapped into
  * this process (peer / symmetric memory over NVLink). y_dest[self_dest] is
- * this GPU's own copy: the epilogue stores each finished tile there, and a
- * forwarding warp of the same kernel streams it from there to the other
- * destinations while later tiles compute. 1 <= n_dest <= 8, 0 <= self_dest <
+ * this GPU's own copy. The epilogue stages each 32-row x 128-column block of
+ * a finished tile in shared memory and TMA-stores it to its own copy, then to
+ * every other destination. 1 <= n_dest <= 8, 0 <= self_dest <
  * n_dest, n a multiple of 128, ldy and col0 multiples of 8, destinations
  * 16-byte aligned. The caller orders the ranks (a barrier after the calls)
  * before reading a destination.
