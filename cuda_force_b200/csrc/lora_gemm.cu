@@ -177,6 +177,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, kInt8>::kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       uint32_t outstanding = 0, issue_parity = 0;
+      bool dep_ready = false;
       const int extra_a_bytes = kBM * p.rank * 2;
       const int extra_b_bytes = BN * p.rank * 2;
       for (int tile = blockIdx.x; tile < p.n_tiles && !aborted(abort_flag); tile += gridDim.x) {
@@ -207,6 +208,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, kInt8>::kThreads, 1)
               ptx::tma_load_2d(sb, &tm_b, &full[stage], k0, n0);
             }
           } else {
+            if (!dep_ready) {  // P comes from the down-projection launched just before
+              ptx::grid_dep_wait();
+              dep_ready = true;
+            }
             ptx::mbar_expect_tx(&full[stage], extra_a_bytes + extra_b_bytes);
             ptx::tma_load_2d(sa, &tm_pa, &full[stage], 0, m0);
             if (p.extra_b_mn) {
@@ -485,6 +490,9 @@ __global__ void __launch_bounds__(DownCfg<R>::kThreads, 1)
     down_proj_kernel(const __grid_constant__ CUtensorMap tm_x,
                      const __grid_constant__ CUtensorMap tm_a, const DownParams p) {
   using C = DownCfg<R>;
+  // The linear kernel that consumes P may start now: it streams its main loop
+  // and waits for this grid only before its first read of P.
+  ptx::grid_dep_launch_dependents();
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -793,6 +801,7 @@ __global__ void __launch_bounds__(W8Cfg<BT, kStaged>::kThreads, W8Cfg<BT, kStage
       int stage = 0;
       uint32_t phase = 0;
       uint32_t outstanding = 0, issue_parity = 0;
+      bool dep_ready = false;
       for (int tile = tile0; tile < p.n_tiles && !aborted(abort_flag); tile += tile_step) {
         const int w0 = (tile % p.n_tiles_w) * kBM;
         const int t0 = (tile / p.n_tiles_w) * BT;
@@ -809,6 +818,10 @@ __global__ void __launch_bounds__(W8Cfg<BT, kStaged>::kThreads, W8Cfg<BT, kStage
             ptx::tma_load_2d(sx, &tm_x, &full[stage], k0, t0);
             ptx::tma_load_2d(sx + C::kXBytes, &tm_codes, &full[stage], k0, w0);
           } else {
+            if (!dep_ready) {  // P comes from the down-projection launched just before
+              ptx::grid_dep_wait();
+              dep_ready = true;
+            }
             ptx::mbar_expect_tx(&full[stage], (kBM + BT) * p.rank * 2);
             if (p.extra_b_mn) {
               for (int c = 0; c < kBM / 64; ++c) {
@@ -1211,6 +1224,7 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore>::kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       uint32_t outstanding = 0, issue_parity = 0;
+      bool dep_ready = false;
       for (int tile = blockIdx.x; tile < p.n_tiles && !aborted(abort_flag); tile += gridDim.x) {
         const int w0 = (tile % p.n_tiles_w) * kBM;
         const int t0 = (tile / p.n_tiles_w) * BT;
@@ -1228,6 +1242,10 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore>::kThreads, 1)
             ptx::tma_load_2d(sx + C::kXHalf, &tm_x, &full[stage], k0, t0 + 256);
             ptx::tma_load_2d(sx + C::kXBytes, &tm_codes, &full[stage], k0, w0);
           } else {
+            if (!dep_ready) {  // P comes from the down-projection launched just before
+              ptx::grid_dep_wait();
+              dep_ready = true;
+            }
             const int j0 = (it - p.num_kb) * kUmmaK;  // adapter columns [j0, j0 + 16)
             ptx::mbar_expect_tx(&full[stage], (kBM + BT) * kUmmaK * 2);
             if (p.extra_b_mn) {
@@ -1501,6 +1519,14 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
+// Launch attribute of the linear kernels: they may begin while the
+// down-projection launched just before them on the stream is still running
+// (their producers wait for it before reading P).
+void set_programmatic_dependency(cudaLaunchAttribute &attr) {
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+}
+
 CUtensorMapSwizzle swizzle_for(int inner_bytes) {
   switch (inner_bytes) {
     case 32: return CU_TENSOR_MAP_SWIZZLE_32B;
@@ -1536,7 +1562,16 @@ int launch_gemm(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &p
   CFB_TRY_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(C::kSmemBytes)));
   const int grid = std::max(1, std::min(params.n_tiles, sm_count()));
-  kernel<<<grid, C::kThreads, C::kSmemBytes, stream>>>(a, b, pa, pb, params);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(C::kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  set_programmatic_dependency(attr[0]);
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  CFB_TRY_CUDA(cudaLaunchKernelEx(&cfg, kernel, a, b, pa, pb, params));
   return check_launch();
 }
 
@@ -1686,13 +1721,14 @@ int launch_w8_swap(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
   cfg.blockDim = dim3(C::kThreads);
   cfg.dynamicSmemBytes = C::kSmemBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  set_programmatic_dependency(attr[1]);
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   CFB_TRY_CUDA(cudaLaunchKernelEx(&cfg, kernel, tm_x, tm_codes, tm_p, tm_bt, p));
   return check_launch();
 }
@@ -1753,7 +1789,16 @@ int launch_w8_wide(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
   CFB_TRY_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(C::kSmemBytes)));
   const int grid = std::max(1, std::min(p.n_tiles, sm_count()));
-  kernel<<<grid, C::kThreads, C::kSmemBytes, stream>>>(tm_x, tm_codes, tm_p, tm_bt, out_maps, p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(C::kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  set_programmatic_dependency(attr[0]);
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  CFB_TRY_CUDA(cudaLaunchKernelEx(&cfg, kernel, tm_x, tm_codes, tm_p, tm_bt, out_maps, p));
   return check_launch();
 }
 
