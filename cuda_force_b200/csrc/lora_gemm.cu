@@ -1133,6 +1133,442 @@ __global__ void __launch_bounds__(W8Cfg<BT, kStaged>::kThreads, W8Cfg<BT, kStage
 }
 
 // ---------------------------------------------------------------------------
+// W8 + LoRA for decode-sized token counts (M <= 128): one 128-feature tile
+// per CTA, K split across a thread-block cluster.
+//
+// Decode is an HBM stream of int8 codes, so the kernel keeps the stream
+// moving with three independent rings, each freed by its last reader:
+//   raw   128 x 128 int8 code tiles (two k-blocks, 16 KB: 128-byte row
+//         segments), loaded by TMA and released by the converter warps once
+//         both k-blocks are converted;
+//   x     BT x 64 activation tiles, loaded by a second TMA thread and
+//         released by the MMA;
+//   conv  128 x 64 bf16/f16 weight tiles written by the converters and
+//         released by the MMA.
+// Each CTA accumulates its K slice of the 128 x BT tile in TMEM (swap-AB: W
+// tile = A operand, tokens = N). The cluster's rank-0 CTA then adds the
+// rank-r adapter as rank/16 more K-steps: the code producer loads the tile's
+// B^T slice into the next raw slot and the activation producer, once the
+// down-projection grid has completed, loads P = (alpha/r) x A into the next
+// activation slot. Every CTA parks its fp32 partial over its spent rings,
+// and after a cluster barrier reduces a share of the rows across the cluster
+// through distributed shared memory and writes them.
+//   warp 0 code producer, warp 1 TMEM owner + MMA issuer, warp 2 activation
+//   producer, warps 4-7 TMEM readers, warps 8-15 converters; all reduce.
+// ---------------------------------------------------------------------------
+
+// Ring waits in the decode kernel poll (no suspend hint): nearly every one of
+// them blocks on memory, and polling resumes as soon as the phase flips.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+template <int BT>
+struct DecCfg {
+  // A raw stage holds kRawKb k-blocks: 128-byte row segments, so one TMA box
+  // moves 16 KB in 128 row requests.
+  static constexpr int kRawKb = 2;
+  static constexpr int kRawBytes = kBM * kBK * kRawKb;  // 16 KB int8 codes
+  static constexpr int kXBytes = BT * kBK * 2;          // activation tile
+  static constexpr int kConvBytes = kBM * kBK * 2;      // 16 KB converted tile
+  static constexpr int kRawStages = BT <= 32 ? 4 : 2;
+  static constexpr int kXStages = BT <= 32 ? 3 : (BT <= 64 ? 3 : 2);
+  static constexpr int kConvSlots = BT <= 32 ? 2 : (BT <= 64 ? 3 : 2);
+  static constexpr int kRawOff = 0;
+  static constexpr int kXOff = kRawOff + kRawStages * kRawBytes;
+  static constexpr int kConvOff = kXOff + kXStages * kXBytes;
+  static constexpr int kRingBytes = kConvOff + kConvSlots * kConvBytes;
+  static constexpr int kPartialBytes = kBM * BT * 4;  // aliases the spent rings
+  static_assert(kPartialBytes <= kRingBytes, "partial tile must fit in the rings");
+  // Adapter operands: B^T slice (128 x rank <= 64) in a raw slot, P (BT x
+  // rank) in an activation slot.
+  static_assert(kBM * 64 * 2 <= kRawBytes && BT * 64 * 2 <= kXBytes, "adapter tiles");
+  static_assert(kXOff % 1024 == 0 && kConvOff % 1024 == 0, "ring alignment");
+  static constexpr int kThreads = 512;
+  static constexpr int kMinBlocks = 2;  // two CTAs per SM: twice the loads in flight
+  static constexpr int kTmemCols = BT < 32 ? 32 : BT;
+  static constexpr size_t kSmemBytes = 1024 + static_cast<size_t>(kRingBytes) + 256;
+};
+
+struct DecParams {
+  int M, N;
+  int num_kb;        // k-blocks of 64
+  int kb_per_split;
+  int splits;        // cluster size
+  int rank;          // adapter rank (16, 32 or 64)
+  int b_mn;          // b stored [rank, N] (N contiguous: MN-major A operand)
+  const float *w_scales;
+  uint16_t *out;     // y [M, N]
+  unsigned *err;
+};
+
+template <int BT, bool kBf16>
+__global__ void __launch_bounds__(DecCfg<BT>::kThreads, DecCfg<BT>::kMinBlocks)
+    w8_decode_kernel(const __grid_constant__ CUtensorMap tm_x,
+                     const __grid_constant__ CUtensorMap tm_codes,
+                     const __grid_constant__ CUtensorMap tm_p,
+                     const __grid_constant__ CUtensorMap tm_bt, const DecParams p) {
+  using C = DecCfg<BT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t *raw_ring = smem + C::kRawOff;
+  uint8_t *x_ring = smem + C::kXOff;
+  uint8_t *conv = smem + C::kConvOff;
+  float *partial = reinterpret_cast<float *>(smem);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kRingBytes);
+  uint64_t *raw_full = bars;
+  uint64_t *raw_empty = raw_full + C::kRawStages;
+  uint64_t *x_full = raw_empty + C::kRawStages;
+  uint64_t *x_empty = x_full + C::kXStages;
+  uint64_t *conv_full = x_empty + C::kXStages;
+  uint64_t *conv_empty = conv_full + C::kConvSlots;
+  uint64_t *tmem_full = conv_empty + C::kConvSlots;
+  uint64_t *drain = tmem_full + 1;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  int *abort_flag = reinterpret_cast<int *>(tmem_slot + 1);
+  constexpr int kConvWarps = kConvThreads / kWarp;
+
+  const int warp = threadIdx.x / kWarp;
+  const int lane = threadIdx.x % kWarp;
+  const int rank = static_cast<int>(ptx::cluster_ctarank());
+  const int tile = static_cast<int>(blockIdx.x) / p.splits;
+  const int w0 = tile * kBM;
+  const int kb0 = rank * p.kb_per_split;
+  const int nkb = max(0, min(p.num_kb, kb0 + p.kb_per_split) - kb0);
+  const bool adapter = rank == 0;  // this CTA adds the rank-r term
+  const int n_raw_loads = (nkb + C::kRawKb - 1) / C::kRawKb;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kRawStages; ++s) {
+      ptx::mbar_init(&raw_full[s], 1);
+      ptx::mbar_init(&raw_empty[s], kConvWarps);
+    }
+    for (int s = 0; s < C::kXStages; ++s) {
+      ptx::mbar_init(&x_full[s], 1);
+      ptx::mbar_init(&x_empty[s], 1);
+    }
+    for (int c = 0; c < C::kConvSlots; ++c) {
+      ptx::mbar_init(&conv_full[c], kConvWarps);
+      ptx::mbar_init(&conv_empty[c], 1);
+    }
+    ptx::mbar_init(tmem_full, 1);
+    ptx::mbar_init(drain, 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, C::kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0 || warp == 2) {
+    // ------------------------------------------------- producers (codes / x)
+    if (lane == 0) {
+      const bool codes = warp == 0;
+      const int n_stages = codes ? C::kRawStages : C::kXStages;
+      uint64_t *full = codes ? raw_full : x_full;
+      uint64_t *empty = codes ? raw_empty : x_empty;
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t outstanding = 0, issue_parity = 0;
+      const int n_loads = (codes ? n_raw_loads : nkb) + (adapter ? 1 : 0);
+      for (int it = 0; it < n_loads; ++it) {
+        if (!ptx::mbar_wait(&empty[stage], phase ^ 1, kWaitLimitNs, false)) {
+          record_timeout(p.err, abort_flag);
+          break;
+        }
+        const bool main = it < n_loads - (adapter ? 1 : 0);
+        if (codes) {
+          uint8_t *dst = raw_ring + stage * C::kRawBytes;
+          if (main) {
+            ptx::mbar_expect_tx(&full[stage], C::kRawBytes);
+            ptx::tma_load_2d(dst, &tm_codes, &full[stage], (kb0 + it * C::kRawKb) * kBK, w0);
+          } else {
+            // The tile's B^T slice: [128 features, rank] as the A operand.
+            ptx::mbar_expect_tx(&full[stage], kBM * p.rank * 2);
+            if (p.b_mn) {
+              for (int c = 0; c < kBM / 64; ++c) {
+                ptx::tma_load_2d(dst + c * (p.rank * 128), &tm_bt, &full[stage], w0 + c * 64, 0);
+              }
+            } else {
+              ptx::tma_load_2d(dst, &tm_bt, &full[stage], 0, w0);
+            }
+          }
+        } else {
+          uint8_t *dst = x_ring + stage * C::kXBytes;
+          if (main) {
+            ptx::mbar_expect_tx(&full[stage], C::kXBytes);
+            ptx::tma_load_2d(dst, &tm_x, &full[stage], (kb0 + it) * kBK, 0);
+          } else {
+            ptx::grid_dep_wait();  // P is the down-projection's output
+            ptx::mbar_expect_tx(&full[stage], BT * p.rank * 2);
+            ptx::tma_load_2d(dst, &tm_p, &full[stage], 0, 0);
+          }
+        }
+        outstanding |= 1u << stage;
+        issue_parity = (issue_parity & ~(1u << stage)) | (phase << stage);
+        if (++stage == n_stages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (aborted(abort_flag)) {
+        for (int s = 0; s < n_stages; ++s) {
+          if (outstanding & (1u << s)) ptx::mbar_wait(&full[s], (issue_parity >> s) & 1u, 200000000ull);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0 && nkb > 0) {
+      const uint32_t idesc = ptx::make_idesc_f16(kBf16, kBM, BT, false, false);
+      int xs = 0;
+      uint32_t x_phase = 0;
+      int c = 0;
+      uint32_t c_phase = 0;
+      bool ok = true;
+      for (int it = 0; it < nkb; ++it) {
+        if (!ptx::mbar_wait(&x_full[xs], x_phase, kWaitLimitNs, false) ||
+            !ptx::mbar_wait(&conv_full[c], c_phase, kWaitLimitNs, false)) {
+          record_timeout(p.err, abort_flag);
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t sa = ptx::smem_addr(conv + c * C::kConvBytes);
+        const uint32_t sx = ptx::smem_addr(x_ring + xs * C::kXBytes);
+        for (int ks = 0; ks < kBK / kUmmaK; ++ks) {
+          ptx::mma_f16(tmem_base, kmajor_desc(sa, 128, ks), kmajor_desc(sx, 128, ks), idesc,
+                       (it > 0 || ks > 0) ? 1u : 0u);
+        }
+        ptx::mma_commit(&x_empty[xs]);
+        ptx::mma_commit(&conv_empty[c]);
+        if (++xs == C::kXStages) {
+          xs = 0;
+          x_phase ^= 1;
+        }
+        if (++c == C::kConvSlots) {
+          c = 0;
+          c_phase ^= 1;
+        }
+      }
+      if (ok && adapter) {
+        // Adapter K-steps: A = B^T slice (next raw slot), B = P (next x slot).
+        const int rs = n_raw_loads % C::kRawStages;
+        const uint32_t r_phase = static_cast<uint32_t>((n_raw_loads / C::kRawStages) & 1);
+        if (!ptx::mbar_wait(&raw_full[rs], r_phase, kWaitLimitNs, false) ||
+            !ptx::mbar_wait(&x_full[xs], x_phase, kWaitLimitNs, false)) {
+          record_timeout(p.err, abort_flag);
+          ok = false;
+        } else {
+          ptx::tc_fence_after();
+          const uint32_t idesc_ad = ptx::make_idesc_f16(kBf16, kBM, BT, p.b_mn != 0, false);
+          const uint32_t sa = ptx::smem_addr(raw_ring + rs * C::kRawBytes);
+          const uint32_t sx = ptx::smem_addr(x_ring + xs * C::kXBytes);
+          const int row_bytes = p.rank * 2;
+          for (int ks = 0; ks < p.rank / kUmmaK; ++ks) {
+            const uint64_t adesc = p.b_mn ? mnmajor_desc(sa, 128, p.rank * 128, ks)
+                                          : kmajor_desc(sa, row_bytes, ks);
+            ptx::mma_f16(tmem_base, adesc, kmajor_desc(sx, row_bytes, ks), idesc_ad, 1u);
+          }
+        }
+      }
+      if (ok) ptx::mma_commit(tmem_full);
+      if (aborted(abort_flag)) {
+        ptx::mma_commit(drain);
+        ptx::mbar_wait(drain, 0, 200000000ull);
+      }
+    }
+  } else if (warp >= kConvWarp0) {
+    // ------------------------------------------------------------------ converters
+    // Lane l handles row (group * 8 + l / 4), 16-code chunk l % 4, of the
+    // 128 x 64 code tile, writing 32 bytes of the 128B-swizzled bf16 row.
+    constexpr int kGroups = kBM / 8 / kConvWarps;  // 2
+    // Scales run kScaleAhead k-blocks ahead and each load is issued after the
+    // iteration's proxy fence, which would otherwise wait for it.
+    constexpr int kScaleAhead = 3;
+    const int cw = warp - kConvWarp0;
+    const int sub_row = lane / 4;
+    const int chunk = lane % 4;
+    const float *srow[kGroups];
+    float sq[kGroups][kScaleAhead];
+#pragma unroll
+    for (int g = 0; g < kGroups; ++g) {
+      const int n = w0 + (cw + g * kConvWarps) * 8 + sub_row;
+      srow[g] = n < p.N ? p.w_scales + static_cast<int64_t>(n) * p.num_kb + kb0 : nullptr;
+#pragma unroll
+      for (int a = 0; a < kScaleAhead; ++a) {
+        sq[g][a] = (srow[g] != nullptr && a < nkb) ? __ldg(srow[g] + a) : 0.0f;
+      }
+    }
+    int rs = 0;
+    uint32_t r_phase = 0;
+    int c = 0;
+    uint32_t c_phase = 0;
+    for (int it = 0; it < nkb; ++it) {
+      const int sub = it % C::kRawKb;  // k-block within the raw stage
+      if (sub == 0 &&
+          __any_sync(0xffffffffu, !ptx::mbar_wait(&raw_full[rs], r_phase, kWaitLimitNs, false))) {
+        if (lane == 0) record_timeout(p.err, abort_flag);
+        break;
+      }
+      uint4 codes[kGroups];
+      const uint8_t *raw = raw_ring + rs * C::kRawBytes + sub * kBK;
+#pragma unroll
+      for (int g = 0; g < kGroups; ++g) {
+        const int r = (cw + g * kConvWarps) * 8 + sub_row;
+        codes[g] = *reinterpret_cast<const uint4 *>(raw + r * (kBK * C::kRawKb) + chunk * 16);
+      }
+      if (__any_sync(0xffffffffu,
+                     !ptx::mbar_wait(&conv_empty[c], c_phase ^ 1u, kWaitLimitNs, false))) {
+        if (lane == 0) record_timeout(p.err, abort_flag);
+        break;
+      }
+      uint8_t *dst = conv + c * C::kConvBytes;
+#pragma unroll
+      for (int g = 0; g < kGroups; ++g) {
+        const int r = (cw + g * kConvWarps) * 8 + sub_row;
+        const uint32_t words[4] = {codes[g].x, codes[g].y, codes[g].z, codes[g].w};
+        uint32_t outw[8];
+        const uint64_t sc2 = ptx::splat_f32x2(sq[g][0]);
+#pragma unroll
+        for (int wd = 0; wd < 4; ++wd) {
+          const uint32_t u = words[wd] ^ 0x80808080u;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            // 2^23 + (q + 128) as floats, then (that - (2^23 + 128)) * s for
+            // two codes per packed f32x2 add and multiply: exactly q * s.
+            const uint32_t b0 = __byte_perm(u, 0x4B000000u, 0x7440u | (2 * h));
+            const uint32_t b1 = __byte_perm(u, 0x4B000000u, 0x7440u | (2 * h + 1));
+            float lo, hi;
+            ptx::dequant_pair(b0, b1, sc2, lo, hi);
+            outw[2 * wd + h] = kBf16 ? ptx::pack_bf16x2(lo, hi) : ptx::pack_f16x2(lo, hi);
+          }
+        }
+        uint8_t *dst_row = dst + r * 128;
+        const int sw = r & 7;
+        *reinterpret_cast<uint4 *>(dst_row + (((2 * chunk) ^ sw) << 4)) =
+            make_uint4(outw[0], outw[1], outw[2], outw[3]);
+        *reinterpret_cast<uint4 *>(dst_row + (((2 * chunk + 1) ^ sw) << 4)) =
+            make_uint4(outw[4], outw[5], outw[6], outw[7]);
+      }
+      // The proxy fence orders this warp's generic reads of the raw slot and
+      // writes of the converted slot before the TMA refill and the MMA.
+      ptx::fence_proxy_async_smem();
+      const bool stage_done = sub == C::kRawKb - 1 || it + 1 == nkb;
+      if (stage_done) ptx::warp_arrive(&raw_empty[rs]);
+      ptx::warp_arrive(&conv_full[c]);
+      if (stage_done && ++rs == C::kRawStages) {
+        rs = 0;
+        r_phase ^= 1;
+      }
+      if (++c == C::kConvSlots) {
+        c = 0;
+        c_phase ^= 1;
+      }
+#pragma unroll
+      for (int g = 0; g < kGroups; ++g) {
+#pragma unroll
+        for (int a = 0; a + 1 < kScaleAhead; ++a) sq[g][a] = sq[g][a + 1];
+        const int kb = it + kScaleAhead;
+        sq[g][kScaleAhead - 1] = (srow[g] != nullptr && kb < nkb) ? __ldg(srow[g] + kb) : 0.0f;
+      }
+    }
+  }
+
+  // ---------------------------------------------------------------- partial tile
+  // Every MMA has completed once tmem_full fires, and every ring load was
+  // consumed before it, so the rings can hold the fp32 partial.
+  if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) {
+    const int quarter = warp % 4;
+    const int row = quarter * 32 + lane;
+    bool have = nkb > 0;
+    if (have) {
+      const bool ok = ptx::mbar_wait(tmem_full, 0, kWaitLimitNs, false);
+      if (__any_sync(0xffffffffu, !ok)) {
+        if (lane == 0) record_timeout(p.err, abort_flag);
+        have = false;
+      }
+    }
+    if (have) ptx::tc_fence_after();
+    const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+#pragma unroll 1
+    for (int c = 0; c < (BT + 31) / 32; ++c) {
+      uint32_t v[32];
+      if (have) {
+        ptx::tmem_ld_32x32b_x32(t_row + c * 32, v);
+        ptx::tmem_ld_wait();
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = 0u;
+      }
+      float *prow = partial + row * BT + c * 32;
+#pragma unroll
+      for (int j = 0; j < 32 && c * 32 + j < BT; j += 4) {
+        *reinterpret_cast<float4 *>(prow + j) =
+            make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
+                        __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+      }
+    }
+  }
+
+  // ------------------------------------------------------ cluster reduction
+  ptx::tc_fence_before();
+  ptx::cluster_sync();
+  {
+    const int r0 = rank * kBM / p.splits;
+    const int r1 = (rank + 1) * kBM / p.splits;
+    const int rows = r1 - r0;
+    const uint32_t base = ptx::smem_addr(partial);
+    for (int item = threadIdx.x; item < rows * (BT / 4); item += C::kThreads) {
+      const int row = r0 + item % rows;
+      const int t4 = (item / rows) * 4;
+      const int n = w0 + row;
+      const uint32_t off = static_cast<uint32_t>((row * BT + t4) * 4);
+      // Peers' partials are requested four at a time before they are summed.
+      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+      for (int p0 = 0; p0 < 8; p0 += 4) {
+        float4 part[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          if (p0 + q < p.splits) {
+            part[q] = ptx::ld_shared_cluster_f4(ptx::map_shared_rank(base + off, p0 + q));
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          if (p0 + q < p.splits) {
+            acc[0] += part[q].x;
+            acc[1] += part[q].y;
+            acc[2] += part[q].z;
+            acc[3] += part[q].w;
+          }
+        }
+      }
+      if (n >= p.N) continue;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int t = t4 + q;
+        if (t < p.M) {
+          const uint32_t h = kBf16 ? ptx::pack_bf16x2(acc[q], 0.0f) : ptx::pack_f16x2(acc[q], 0.0f);
+          p.out[static_cast<int64_t>(t) * p.N + n] = static_cast<uint16_t>(h & 0xffffu);
+        }
+      }
+    }
+  }
+  // No CTA may leave while a peer can still read its shared memory.
+  ptx::cluster_sync();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // W8 + LoRA, swap-AB with 512-token tiles (prefill).
 //
 // Each converted 128 x 32 weight tile feeds two N = 256 MMAs (tokens
@@ -1733,6 +2169,65 @@ int launch_w8_swap(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
   return check_launch();
 }
 
+template <int BT, bool kBf16>
+int launch_w8_decode(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
+  using C = DecCfg<BT>;
+  const int r = static_cast<int>(L.r);
+  CUtensorMap tm_x, tm_codes, tm_p, tm_bt;
+  int st = CF_OK;
+  if ((st = make_map(&tm_x, L.x, 2, L.k, L.m, kBK, BT, true))) return st;
+  if ((st = make_map(&tm_codes, L.w, 1, L.k, L.n, kBK * C::kRawKb, kBM, false))) return st;
+  if ((st = make_map(&tm_p, L.ws, 2, r, L.m, r, BT, true))) return st;
+  DecParams p{};
+  if (L.b_layout == CF_LAYOUT_REF) {
+    // b [r, N]: N contiguous -> MN-major A operand, chunks of 64 features x r.
+    if ((st = make_map(&tm_bt, L.b, 2, L.n, r, 64, r, true))) return st;
+    p.b_mn = 1;
+  } else {
+    // b^T [N, r]: r contiguous -> K-major A operand.
+    if ((st = make_map(&tm_bt, L.b, 2, r, L.n, r, kBM, true))) return st;
+    p.b_mn = 0;
+  }
+  p.M = static_cast<int>(L.m);
+  p.N = static_cast<int>(L.n);
+  p.num_kb = static_cast<int>(L.k / kBK);
+  p.rank = r;
+  p.w_scales = L.w_scales;
+  p.out = static_cast<uint16_t *>(L.y);
+  p.err = err;
+  const int n_tiles = static_cast<int>((L.n + kBM - 1) / kBM);
+  // Largest K split (cluster size <= 8) that keeps the whole grid resident.
+  const int slots = sm_count() * C::kMinBlocks;
+  int splits = 1;
+  for (int s = 8; s >= 2; --s) {
+    if (n_tiles * s <= slots && s <= p.num_kb) {
+      splits = s;
+      break;
+    }
+  }
+  p.splits = splits;
+  // Whole raw stages per CTA: every slice but the last starts on a stage.
+  p.kb_per_split = ((p.num_kb + splits - 1) / splits + C::kRawKb - 1) / C::kRawKb * C::kRawKb;
+  auto kernel = w8_decode_kernel<BT, kBf16>;
+  CFB_TRY_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(C::kSmemBytes)));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(n_tiles * splits));
+  cfg.blockDim = dim3(C::kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  set_programmatic_dependency(attr[1]);
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  CFB_TRY_CUDA(cudaLaunchKernelEx(&cfg, kernel, tm_x, tm_codes, tm_p, tm_bt, p));
+  return check_launch();
+}
+
 template <bool kBf16, bool kTmaStore>
 int launch_w8_wide(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
   using C = W8WideCfg<kTmaStore>;
@@ -1814,7 +2309,9 @@ int run_linear(const LinearArgs &L, cudaStream_t stream) {
   }
   if (st != CF_OK) return st;
   if (L.int8) {
-    if (L.m <= 128 && L.n_dest == 0) return launch_w8_swap<32, kBf16, false>(L, err, stream);
+    if (L.n_dest == 0 && L.m <= 32) return launch_w8_decode<32, kBf16>(L, err, stream);
+    if (L.n_dest == 0 && L.m <= 64) return launch_w8_decode<64, kBf16>(L, err, stream);
+    if (L.n_dest == 0 && L.m <= 128) return launch_w8_decode<128, kBf16>(L, err, stream);
     return launch_w8_wide<kBf16, true>(L, err, stream);
   }
 

@@ -250,3 +250,19 @@ def test_copy_engine_entry_point_rejects_bad_arguments(cuda_device):
     assert lib.cf_lora_linear_int8_allgather_ce(*args, 1, *tail) == _abi.CF_ERR_INVALID_ARGUMENT
     # workspace smaller than the counters need
     assert lib.cf_lora_linear_int8_allgather_ce(*args, 0, *tail) == _abi.CF_ERR_WORKSPACE
+
+
+@pytest.mark.parametrize(("m", "rank", "b_t"), [(1, 16, False), (17, 32, True), (32, 64, False),
+                                                (33, 16, True), (64, 32, False), (100, 64, True),
+                                                (128, 16, False)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_w8_decode_shapes(m, rank, b_t, dtype, cuda_device):
+    # Token counts up to 128 take the split-K decode kernel; n = 1000 leaves a
+    # ragged last feature tile and k = 1536 a K split that does not divide.
+    x, w, a, b = make(m, 1536, 1000, rank, dtype, seed=300 + m + rank)
+    dev = cuda_device
+    codes, scales = cf.quantize_int8(w.to(dev))
+    y = cf.lora_linear_int8(x.to(dev), codes, scales, a.to(dev), as_layout(b.to(dev), b_t), 2.0)
+    ref = linear_ref.lora_linear_int8(x, codes.cpu(), scales.cpu(), a, b, 2.0)
+    assert linear_ref.max_rel_error(y, ref) <= TIGHT
+    assert _abi.load().cf_device_status() == _abi.CF_OK
