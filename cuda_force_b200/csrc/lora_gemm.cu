@@ -9,25 +9,26 @@
 // memory: q * s in fp32 exactly as the dequantiser does, then rounded to the
 // activation dtype for the MMA.
 //
-// Two launches per call:
+// Two launches per call, the second allowed to start while the first runs
+// (programmatic dependent launch; it waits for the first only before reading P):
 //   1. down-projection  P = scale * x A  -> workspace [M, r] (bf16/f16), split-K
 //      over a thread-block cluster (down_proj_kernel);
 //   2. main product     y = x W^T + P B  with the adapter folded into the MMA as
-//      r/16 extra K-steps at the end of every output tile (A operand = P tile,
-//      B operand = B slice), so the rank-r update costs no epilogue arithmetic.
-//
-// Kernel structure (one CTA per SM, persistent over output tiles):
-//   warp 0      TMA producer: x tile + W tile (or int8 code tile) per k-block
-//               into a kStages-deep shared-memory ring (mbarrier full/empty);
-//   warp 1      TMEM allocator and single-thread MMA issuer
-//               (tcgen05.mma.cta_group::1.kind::f16, 128 x BN x 16 per instruction);
-//   warps 4-7   epilogue: tcgen05.ld the fp32 accumulator (thread = output row),
-//               round to bf16/f16, store; double-buffered TMEM accumulators let
-//               the next tile's mainloop run under this epilogue;
-//   warps 8-15  (W8 only) converters: int8 codes -> q*s (fp32) -> bf16/f16 into
-//               the 128B-swizzled K-major operand layout the MMA reads.
-// Every mbarrier wait is bounded (2 s of global time); on expiry the kernel
-// records CF_ERR_DEVICE_TIMEOUT in the device error word and unwinds.
+//      r/16 extra K-steps (P and the B slice as operands), so the rank-r update
+//      costs no epilogue arithmetic:
+//        lora_gemm_kernel   bf16/f16 W, 128 x BN tiles of y, persistent;
+//        w8_wide_kernel     int8 W, M > 128: swap-AB 128-feature x 512-token
+//                           tiles, codes converted to bf16/f16 in shared memory
+//                           by eight converter warps, persistent; also the
+//                           fused all-gather (TMA-store epilogue to every
+//                           destination);
+//        w8_decode_kernel   int8 W, M <= 128: one 128-feature tile per CTA with
+//                           K split across a cluster and a DSMEM reduction.
+// Roles: one TMA producer thread, one MMA-issuing thread that also owns TMEM,
+// four TMEM-reading epilogue warps (thread = accumulator lane), and for int8
+// weights eight converter warps. Every mbarrier wait is bounded (2 s of global
+// time); on expiry the kernel records CF_ERR_DEVICE_TIMEOUT in the device error
+// word and unwinds.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -50,16 +51,15 @@ constexpr int kEpiWarp0 = 4;    // first epilogue warp (warp % 4 = TMEM lane qua
 constexpr int kConvWarp0 = 8;   // first converter warp (W8 only)
 constexpr int kConvThreads = 256;
 
-enum BSource : int { kBKMajor = 0, kBMNMajor = 1, kBInt8 = 2 };
+enum BSource : int { kBKMajor = 0, kBMNMajor = 1 };
 
-template <int BN, bool kInt8>
+template <int BN>
 struct GemmCfg {
   static constexpr int kABytes = kBM * kBK * 2;                // 16 KB
   static constexpr int kBBytes = (BN < 64 ? 64 : BN) * kBK * 2;  // >= 8 KB so extras fit
-  static constexpr int kRawBytes = kInt8 ? BN * kBK : 0;       // int8 code tile
-  static constexpr int kStageBytes = kABytes + kBBytes + kRawBytes;
-  static constexpr int kStages = kInt8 ? 3 : (BN >= 128 ? 4 : 8);
-  static constexpr int kThreads = kInt8 ? 512 : 256;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = BN >= 128 ? 4 : 8;
+  static constexpr int kThreads = 256;
   static constexpr int kTmemCols = (2 * BN) <= 32 ? 32 : (2 * BN) <= 64 ? 64
                                    : (2 * BN) <= 128 ? 128 : (2 * BN) <= 256 ? 256 : 512;
   static constexpr size_t kSmemBytes = 1024 /*alignment slack*/ +
@@ -78,8 +78,6 @@ struct GemmParams {
   float out_scale;     // multiplier applied in the epilogue
   void *out;           // [M, ldo] row-major, 16-bit
   int ldo;
-  const float *w_scales;  // W8: [N, K/64]
-  int kb_per_row;         // W8: K / 64
   int n_tiles_n;
   int n_tiles;
   unsigned *err;
@@ -116,21 +114,20 @@ __device__ __forceinline__ bool aborted(const int *abort_flag) {
   return *reinterpret_cast<const volatile int *>(abort_flag) != 0;
 }
 
-template <int BN, bool kBf16, bool kInt8>
-__global__ void __launch_bounds__(GemmCfg<BN, kInt8>::kThreads, 1)
+template <int BN, bool kBf16>
+__global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
     lora_gemm_kernel(const __grid_constant__ CUtensorMap tm_a,
                      const __grid_constant__ CUtensorMap tm_b,
                      const __grid_constant__ CUtensorMap tm_pa,
                      const __grid_constant__ CUtensorMap tm_pb, const GemmParams p) {
-  using C = GemmCfg<BN, kInt8>;
+  using C = GemmCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kStages * C::kStageBytes);
   uint64_t *full = bars;                       // [kStages] TMA -> consumers
   uint64_t *empty = bars + C::kStages;         // [kStages] MMA -> producer
-  uint64_t *conv_full = bars + 2 * C::kStages; // [kStages] converters -> MMA (W8)
-  uint64_t *tmem_full = bars + 3 * C::kStages; // [2] MMA -> epilogue
+  uint64_t *tmem_full = bars + 2 * C::kStages; // [2] MMA -> epilogue
   uint64_t *tmem_empty = tmem_full + 2;        // [2] epilogue -> MMA
   uint64_t *drain = tmem_empty + 2;             // [1] MMA retirement on abort
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
@@ -144,7 +141,6 @@ __global__ void __launch_bounds__(GemmCfg<BN, kInt8>::kThreads, 1)
     for (int s = 0; s < C::kStages; ++s) {
       ptx::mbar_init(&full[s], 1);
       ptx::mbar_init(&empty[s], 1);
-      ptx::mbar_init(&conv_full[s], kConvThreads / kWarp);
     }
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(&tmem_full[a], 1);
@@ -192,12 +188,9 @@ __global__ void __launch_bounds__(GemmCfg<BN, kInt8>::kThreads, 1)
           uint8_t *sb = sa + C::kABytes;
           if (it < p.num_kb) {
             const int k0 = it * kBK;
-            const int b_bytes = kInt8 ? C::kRawBytes : BN * kBK * 2;
-            ptx::mbar_expect_tx(&full[stage], C::kABytes + b_bytes);
+            ptx::mbar_expect_tx(&full[stage], C::kABytes + BN * kBK * 2);
             ptx::tma_load_2d(sa, &tm_a, &full[stage], k0, m0);
-            if (kInt8) {
-              ptx::tma_load_2d(sb + C::kBBytes, &tm_b, &full[stage], k0, n0);
-            } else if (p.b_src == kBMNMajor) {
+            if (p.b_src == kBMNMajor) {
               // chunks of min(BN, 64) columns x 64 k-rows, one swizzle row each
               constexpr int kChunkCols = BN < 64 ? BN : 64;
               for (int c = 0; c < BN / kChunkCols; ++c) {
@@ -245,7 +238,6 @@ __global__ void __launch_bounds__(GemmCfg<BN, kInt8>::kThreads, 1)
       const uint32_t idesc_extra = ptx::make_idesc_f16(bf16, kBM, BN, false, p.extra_b_mn != 0);
       int stage = 0;
       uint32_t phase = 0;
-      uint32_t conv_parity = 0;
       int local = 0;
       for (int tile = blockIdx.x; tile < p.n_tiles && !aborted(abort_flag);
            tile += gridDim.x, ++local) {
@@ -260,12 +252,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, kInt8>::kThreads, 1)
         bool ok = true;
         for (int it = 0; it < num_iters; ++it) {
           const bool main_kb = it < p.num_kb;
-          // conv_full[s] completes once per *main* k-block on stage s (the adapter
-          // block skips the converters), so its parity is tracked per stage.
-          const bool via_conv = kInt8 && main_kb;
-          const uint32_t want = via_conv ? (conv_parity >> stage) & 1u : phase;
-          if (via_conv) conv_parity ^= 1u << stage;
-          if (!ptx::mbar_wait(via_conv ? &conv_full[stage] : &full[stage], want)) {
+          if (!ptx::mbar_wait(&full[stage], phase)) {
             record_timeout(p.err, abort_flag);
             ok = false;
             break;
@@ -278,9 +265,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, kInt8>::kThreads, 1)
               const uint64_t adesc = kmajor_desc(sa, 128, ks);
               constexpr int kChunkCols = BN < 64 ? BN : 64;
               const uint64_t bdesc =
-                  (!kInt8 && p.b_src == kBMNMajor)
-                      ? mnmajor_desc(sb, kChunkCols * 2, kBK * kChunkCols * 2, ks)
-                      : kmajor_desc(sb, 128, ks);
+                  p.b_src == kBMNMajor ? mnmajor_desc(sb, kChunkCols * 2, kBK * kChunkCols * 2, ks)
+                                       : kmajor_desc(sb, 128, ks);
               ptx::mma_f16(d_tmem, adesc, bdesc, idesc_main, (it > 0 || ks > 0) ? 1u : 0u);
             }
           } else {
@@ -355,90 +341,6 @@ __global__ void __launch_bounds__(GemmCfg<BN, kInt8>::kThreads, 1)
       }
       ptx::tc_fence_before();
       ptx::warp_arrive(&tmem_empty[acc]);
-    }
-  } else if (kInt8 && warp >= kConvWarp0) {
-    // ------------------------------------------------------------------ converters
-    // Lane l of a converter warp handles row (group * 8 + l / 4) and 16-code
-    // chunk (l % 4) of the int8 tile; it writes 32 bytes (two 16-byte chunks)
-    // of the 128B-swizzled bf16 row: logical chunk c sits at c ^ (row % 8).
-    // Block scales are read from global memory one k-block ahead (registers),
-    // so their latency hides behind the current k-block's conversion.
-    constexpr int kGroups = BN >= 64 ? BN / 8 / (kConvThreads / kWarp) : 1;  // rows per thread
-    const int cw = warp - kConvWarp0;
-    const int sub_row = lane / 4;
-    const int chunk = lane % 4;
-    int stage = 0;
-    uint32_t phase = 0;
-    for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x) {
-      const int n0 = (tile % p.n_tiles_n) * BN;
-      const float *srow[kGroups];
-      float s_cur[kGroups], s_next[kGroups];
-#pragma unroll
-      for (int g = 0; g < kGroups; ++g) {
-        const int n = n0 + (cw + g * (kConvThreads / kWarp)) * 8 + sub_row;
-        srow[g] = n < p.N ? p.w_scales + static_cast<int64_t>(n) * p.kb_per_row : nullptr;
-        s_cur[g] = srow[g] != nullptr ? __ldg(srow[g]) : 0.0f;
-      }
-      bool ok = true;
-      for (int it = 0; it < num_iters; ++it) {
-        if (it < p.num_kb) {
-#pragma unroll
-          for (int g = 0; g < kGroups; ++g) {
-            s_next[g] = (srow[g] != nullptr && it + 1 < p.num_kb) ? __ldg(srow[g] + it + 1) : 0.0f;
-          }
-          const bool got = ptx::mbar_wait(&full[stage], phase);
-          if (__any_sync(0xffffffffu, !got)) {
-            if (lane == 0) record_timeout(p.err, abort_flag);
-            ok = false;
-            break;
-          }
-          uint8_t *sb = smem + stage * C::kStageBytes + C::kABytes;
-          const uint8_t *raw = sb + C::kBBytes;
-#pragma unroll
-          for (int g = 0; g < kGroups; ++g) {
-            const int r = (cw + g * (kConvThreads / kWarp)) * 8 + sub_row;
-            const float sc = s_cur[g];
-            const uint4 codes = *reinterpret_cast<const uint4 *>(raw + r * kBK + chunk * 16);
-            const uint32_t words[4] = {codes.x, codes.y, codes.z, codes.w};
-            uint32_t outw[8];
-#pragma unroll
-            for (int wd = 0; wd < 4; ++wd) {
-              const uint32_t u = words[wd] ^ 0x80808080u;
-              float f[4];
-#pragma unroll
-              for (int b = 0; b < 4; ++b) {
-                // 2^23 + (q + 128) as a float, minus (2^23 + 128): exactly q.
-                const float biased = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7440u | b));
-                f[b] = __fmul_rn(biased - 8388736.0f, sc);
-              }
-              outw[2 * wd] = kBf16 ? ptx::pack_bf16x2(f[0], f[1]) : ptx::pack_f16x2(f[0], f[1]);
-              outw[2 * wd + 1] = kBf16 ? ptx::pack_bf16x2(f[2], f[3]) : ptx::pack_f16x2(f[2], f[3]);
-            }
-            uint8_t *dst_row = sb + r * 128;
-            const int sw = r & 7;
-            *reinterpret_cast<uint4 *>(dst_row + (((2 * chunk) ^ sw) << 4)) =
-                make_uint4(outw[0], outw[1], outw[2], outw[3]);
-            *reinterpret_cast<uint4 *>(dst_row + (((2 * chunk + 1) ^ sw) << 4)) =
-                make_uint4(outw[4], outw[5], outw[6], outw[7]);
-          }
-          ptx::fence_proxy_async_smem();
-          ptx::warp_arrive(&conv_full[stage]);
-#pragma unroll
-          for (int g = 0; g < kGroups; ++g) s_cur[g] = s_next[g];
-        } else if (!ptx::mbar_wait(&full[stage], phase)) {
-          // Adapter stages are not converted, but waiting for them keeps this
-          // warp within one phase of every stage's barrier (a parity wait
-          // cannot tell phase u from phase u - 2).
-          if (lane == 0) record_timeout(p.err, abort_flag);
-          ok = false;
-          break;
-        }
-        if (++stage == C::kStages) {
-          stage = 0;
-          phase ^= 1;
-        }
-      }
-      if (!ok) break;
     }
   }
 
@@ -670,63 +572,21 @@ __global__ void __launch_bounds__(DownCfg<R>::kThreads, 1)
   }
 }
 
-// ---------------------------------------------------------------------------
-// W8 + LoRA in swap-AB form: D^T = W x^T.
-//
-// The int8 weight tile is the MMA's A operand (128 rows of W = 128 output
-// features, the TMEM lanes) and the activations are the B operand (BT tokens,
-// the TMEM columns). Per k-block the converters turn only 128 x 64 codes into
-// bf16/f16 for a 128 x BT x 64 MMA, half the conversion per FLOP of the
-// x-as-A orientation, and for decode (few tokens) BT = 32 keeps the MMA small
-// while W streams through every SM. The adapter adds r/16 K-steps with
-// A = B^T slice (rows = output features) and B = P tile (rows = tokens).
-//
-// Small token counts split K across a thread-block cluster: each CTA of the
-// cluster accumulates a K slice, parks its 128 x BT partial in shared memory,
-// and after a cluster barrier every CTA reduces a share of the rows across the
-// cluster through distributed shared memory and writes them (one tile per
-// cluster). Without a split the grid is persistent over tiles with
-// double-buffered TMEM accumulators.
-//   warp 0 TMA producer, warp 1 TMEM owner + MMA issuer, warps 4-7 epilogue,
-//   warps 8-15 converters.
-// ---------------------------------------------------------------------------
-template <int BT, bool kStaged>
-struct W8Cfg {
-  static constexpr int kABytes = kBM * kBK * 2;   // converted W tile / adapter B^T tile
-  static constexpr int kXBytes = BT * kBK * 2;    // x tile / P tile
-  static constexpr int kRawBytes = kBM * kBK;     // int8 codes
-  static constexpr int kStageBytes = kABytes + kXBytes + kRawBytes;
-  // Pipeline depth: 4 when shared memory allows; the staged epilogue's
-  // 8 KB transpose tile costs one stage at BT = 256.
-  static constexpr int kStages = (BT > 32 && kStaged) || BT <= 32 ? 3 : 4;
-  static constexpr bool kSplit = BT <= 32;
-  static constexpr int kPartialBytes = kSplit ? kBM * BT * 4 : (kStaged ? kBM * 32 * 2 : 0);
-  static constexpr int kThreads = 512;
-  static constexpr int kMinBlocks = BT <= 32 ? 2 : 1;
-  static constexpr int kTmemCols = 2 * BT <= 32 ? 32 : 2 * BT;
-  static constexpr size_t kSmemBytes =
-      1024 + static_cast<size_t>(kStages) * kStageBytes + kPartialBytes + 256;
-  static_assert(kStageBytes % 1024 == 0, "stage alignment");
-};
-
 constexpr int kMaxOuts = 8;
 
 struct W8Params {
   int M;             // tokens
   int N;             // output features (rows of W)
-  int num_kb;
-  int kb_per_split;
-  int splits;        // cluster size along K (1 = persistent, no split)
+  int num_kb;        // k-blocks of 32
   int extra_ksteps;  // rank / 16
   int rank;
   int extra_b_mn;    // B stored [rank, N] (N contiguous)
   const float *w_scales;
-  int kb_per_row;
-  void *out;         // y [M, ldo] (split path)
+  int kb_per_row;    // scales per row (K / 64)
   int ldo;           // row stride of every destination (elements)
   int out_col0;      // first column of this call's features in the destination
-  int n_outs;        // destinations written by the transposing epilogue
-  int self_out;      // wide kernel: index of the destination on this GPU (stored first)
+  int n_outs;        // destinations written by the epilogue
+  int self_out;      // index of the destination on this GPU (stored first)
   void *outs[kMaxOuts];
   int n_tiles_w;
   int n_tiles;
@@ -737,400 +597,6 @@ struct W8Params {
   int rb_per_group;
   int n_groups;
 };
-
-template <int BT, bool kBf16, bool kStaged>
-__global__ void __launch_bounds__(W8Cfg<BT, kStaged>::kThreads, W8Cfg<BT, kStaged>::kMinBlocks)
-    w8_swap_kernel(const __grid_constant__ CUtensorMap tm_x,
-                   const __grid_constant__ CUtensorMap tm_codes,
-                   const __grid_constant__ CUtensorMap tm_p,
-                   const __grid_constant__ CUtensorMap tm_bt, const W8Params p) {
-  using C = W8Cfg<BT, kStaged>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  float *partial = reinterpret_cast<float *>(smem + C::kStages * C::kStageBytes);
-  uint8_t *staging = smem + C::kStages * C::kStageBytes;  // (no split) transpose tile
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kStages * C::kStageBytes +
-                                                C::kPartialBytes);
-  uint64_t *full = bars;
-  uint64_t *empty = bars + C::kStages;
-  uint64_t *conv_full = bars + 2 * C::kStages;
-  uint64_t *tmem_full = bars + 3 * C::kStages;
-  uint64_t *tmem_empty = tmem_full + 2;
-  uint64_t *drain = tmem_empty + 2;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
-  int *abort_flag = reinterpret_cast<int *>(tmem_slot + 1);
-
-  const int warp = threadIdx.x / kWarp;
-  const int lane = threadIdx.x % kWarp;
-  const bool split = p.splits > 1;
-  const int rank = split ? static_cast<int>(ptx::cluster_ctarank()) : 0;
-  const int tile0 = split ? static_cast<int>(blockIdx.x) / p.splits : static_cast<int>(blockIdx.x);
-  const int tile_step = split ? p.n_tiles : static_cast<int>(gridDim.x);  // split: one tile
-  const int kb0 = rank * p.kb_per_split;
-  const int nkb = max(0, min(p.num_kb, kb0 + p.kb_per_split) - kb0);
-  const bool has_extra = rank == 0 && p.extra_ksteps > 0;
-  const int num_iters = nkb + (has_extra ? 1 : 0);
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < C::kStages; ++s) {
-      ptx::mbar_init(&full[s], 1);
-      ptx::mbar_init(&empty[s], 1);
-      ptx::mbar_init(&conv_full[s], kConvThreads / kWarp);
-    }
-    for (int a = 0; a < 2; ++a) {
-      ptx::mbar_init(&tmem_full[a], 1);
-      ptx::mbar_init(&tmem_empty[a], 4);
-    }
-    ptx::mbar_init(drain, 1);
-    *abort_flag = 0;
-    ptx::fence_mbar_init();
-  }
-  if (warp == 1) {
-    ptx::tmem_alloc(tmem_slot, C::kTmemCols);
-    ptx::tmem_relinquish();
-  }
-  ptx::tc_fence_before();
-  __syncthreads();
-  ptx::tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-
-  if (warp == 0) {
-    // ------------------------------------------------------------------ producer
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      uint32_t outstanding = 0, issue_parity = 0;
-      bool dep_ready = false;
-      for (int tile = tile0; tile < p.n_tiles && !aborted(abort_flag); tile += tile_step) {
-        const int w0 = (tile % p.n_tiles_w) * kBM;
-        const int t0 = (tile / p.n_tiles_w) * BT;
-        for (int it = 0; it < num_iters; ++it) {
-          if (!ptx::mbar_wait(&empty[stage], phase ^ 1)) {
-            record_timeout(p.err, abort_flag);
-            break;
-          }
-          uint8_t *sa = smem + stage * C::kStageBytes;
-          uint8_t *sx = sa + C::kABytes;
-          if (it < nkb) {
-            const int k0 = (kb0 + it) * kBK;
-            ptx::mbar_expect_tx(&full[stage], C::kXBytes + C::kRawBytes);
-            ptx::tma_load_2d(sx, &tm_x, &full[stage], k0, t0);
-            ptx::tma_load_2d(sx + C::kXBytes, &tm_codes, &full[stage], k0, w0);
-          } else {
-            if (!dep_ready) {  // P comes from the down-projection launched just before
-              ptx::grid_dep_wait();
-              dep_ready = true;
-            }
-            ptx::mbar_expect_tx(&full[stage], (kBM + BT) * p.rank * 2);
-            if (p.extra_b_mn) {
-              for (int c = 0; c < kBM / 64; ++c) {
-                ptx::tma_load_2d(sa + c * (p.rank * 128), &tm_bt, &full[stage], w0 + c * 64, 0);
-              }
-            } else {
-              ptx::tma_load_2d(sa, &tm_bt, &full[stage], 0, w0);
-            }
-            ptx::tma_load_2d(sx, &tm_p, &full[stage], 0, t0);
-          }
-          outstanding |= 1u << stage;
-          issue_parity = (issue_parity & ~(1u << stage)) | (phase << stage);
-          if (++stage == C::kStages) {
-            stage = 0;
-            phase ^= 1;
-          }
-        }
-      }
-      if (aborted(abort_flag)) {
-        for (int s = 0; s < C::kStages; ++s) {
-          if (outstanding & (1u << s)) ptx::mbar_wait(&full[s], (issue_parity >> s) & 1u, 200000000ull);
-        }
-      }
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0 && num_iters > 0) {
-      const uint32_t idesc_main = ptx::make_idesc_f16(kBf16, kBM, BT, false, false);
-      const uint32_t idesc_extra = ptx::make_idesc_f16(kBf16, kBM, BT, p.extra_b_mn != 0, false);
-      int stage = 0;
-      uint32_t phase = 0;
-      uint32_t conv_parity = 0;
-      int local = 0;
-      for (int tile = tile0; tile < p.n_tiles && !aborted(abort_flag); tile += tile_step, ++local) {
-        const int acc = local & 1;
-        const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
-        if (!ptx::mbar_wait(&tmem_empty[acc], acc_phase ^ 1)) {
-          record_timeout(p.err, abort_flag);
-          break;
-        }
-        ptx::tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BT;
-        bool ok = true;
-        for (int it = 0; it < num_iters; ++it) {
-          const bool main_kb = it < nkb;
-          const uint32_t want = main_kb ? (conv_parity >> stage) & 1u : phase;
-          if (main_kb) conv_parity ^= 1u << stage;
-          if (!ptx::mbar_wait(main_kb ? &conv_full[stage] : &full[stage], want)) {
-            record_timeout(p.err, abort_flag);
-            ok = false;
-            break;
-          }
-          ptx::tc_fence_after();
-          const uint32_t sa = ptx::smem_addr(smem + stage * C::kStageBytes);
-          const uint32_t sx = sa + C::kABytes;
-          if (main_kb) {
-            for (int ks = 0; ks < kBK / kUmmaK; ++ks) {
-              ptx::mma_f16(d_tmem, kmajor_desc(sa, 128, ks), kmajor_desc(sx, 128, ks), idesc_main,
-                           (it > 0 || ks > 0) ? 1u : 0u);
-            }
-          } else {
-            const int row_bytes = p.rank * 2;
-            for (int ks = 0; ks < p.extra_ksteps; ++ks) {
-              const uint64_t adesc = p.extra_b_mn ? mnmajor_desc(sa, 128, p.rank * 128, ks)
-                                                  : kmajor_desc(sa, row_bytes, ks);
-              ptx::mma_f16(d_tmem, adesc, kmajor_desc(sx, row_bytes, ks), idesc_extra,
-                           (it > 0 || ks > 0) ? 1u : 0u);
-            }
-          }
-          ptx::mma_commit(&empty[stage]);
-          if (++stage == C::kStages) {
-            stage = 0;
-            phase ^= 1;
-          }
-        }
-        if (!ok) break;
-        ptx::mma_commit(&tmem_full[acc]);
-      }
-      if (aborted(abort_flag)) {
-        ptx::mma_commit(drain);
-        ptx::mbar_wait(drain, 0, 200000000ull);
-      }
-    }
-  } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) {
-    // ------------------------------------------------------------------ epilogue
-    const int quarter = warp % 4;
-    int local = 0;
-    for (int tile = tile0; tile < p.n_tiles; tile += tile_step, ++local) {
-      const int acc = local & 1;
-      const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
-      const int w0 = (tile % p.n_tiles_w) * kBM;
-      const int t0 = (tile / p.n_tiles_w) * BT;
-      const int row = quarter * 32 + lane;  // output feature within the tile
-      bool have = num_iters > 0;
-      if (have) {
-        const bool ok = ptx::warp_wait(&tmem_full[acc], acc_phase);
-        if (__any_sync(0xffffffffu, !ok)) {
-          if (lane == 0) record_timeout(p.err, abort_flag);
-          have = false;
-        }
-      }
-      if (have) ptx::tc_fence_after();
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BT;
-      const int n = w0 + row;
-      uint16_t *out = static_cast<uint16_t *>(p.out);
-#pragma unroll 1
-      for (int c = 0; c < BT / 32; ++c) {
-        uint32_t v[32];
-        if (have) {
-          ptx::tmem_ld_32x32b_x32(t_row + c * 32, v);
-          ptx::tmem_ld_wait();
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = 0u;
-        }
-        if constexpr (C::kSplit) {
-          if (split) {
-            float *prow = partial + row * BT + c * 32;
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              *reinterpret_cast<float4 *>(prow + j) =
-                  make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
-                              __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
-            }
-            continue;
-          }
-        }
-        if constexpr (!C::kSplit && kStaged) {
-          // Transpose through shared memory: feature-major accumulator rows
-          // become token rows of 128 features (256 contiguous bytes), written
-          // with 16-byte stores to every destination (this GPU's y and, for
-          // the fused all-gather, each peer's y over NVLink).
-          uint16_t *stg = reinterpret_cast<uint16_t *>(staging);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float f = __uint_as_float(v[j]);
-            const uint32_t h = kBf16 ? ptx::pack_bf16x2(f, 0.0f) : ptx::pack_f16x2(f, 0.0f);
-            stg[j * kBM + row] = static_cast<uint16_t>(h & 0xffffu);
-          }
-          ptx::named_bar_sync(1, 4 * kWarp);
-          const int et = threadIdx.x - kEpiWarp0 * kWarp;  // 0..127
-#pragma unroll
-          for (int pass = 0; pass < 4; ++pass) {
-            const int idx = pass * 4 * kWarp + et;
-            const int j = idx / 16;
-            const int seg = idx % 16;
-            const int t = t0 + c * 32 + j;
-            const int col = w0 + seg * 8;
-            if (t < p.M && col < p.N) {
-              const uint4 val = *reinterpret_cast<const uint4 *>(stg + j * kBM + seg * 8);
-              const int64_t off = static_cast<int64_t>(t) * p.ldo + p.out_col0 + col;
-              for (int d = 0; d < p.n_outs; ++d) {
-                *reinterpret_cast<uint4 *>(static_cast<uint16_t *>(p.outs[d]) + off) = val;
-              }
-            }
-          }
-          ptx::named_bar_sync(1, 4 * kWarp);
-        } else if (n < p.N) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int t = t0 + c * 32 + j;
-            if (t < p.M) {
-              const float f = __uint_as_float(v[j]);
-              const uint32_t h = kBf16 ? ptx::pack_bf16x2(f, 0.0f) : ptx::pack_f16x2(f, 0.0f);
-              out[static_cast<int64_t>(t) * p.ldo + p.out_col0 + n] = static_cast<uint16_t>(h & 0xffffu);
-            }
-          }
-        }
-      }
-      ptx::tc_fence_before();
-      ptx::warp_arrive(&tmem_empty[acc]);
-    }
-  } else if (warp >= kConvWarp0) {
-    // ------------------------------------------------------------------ converters
-    // Lane l handles row (group * 8 + l / 4), 16-code chunk l % 4, of the
-    // 128 x 64 code tile, writing 32 bytes of the 128B-swizzled row.
-    constexpr int kWarpsC = kConvThreads / kWarp;
-    constexpr int kGroups = kBM / 8 / kWarpsC;  // 2
-    const int cw = warp - kConvWarp0;
-    const int sub_row = lane / 4;
-    const int chunk = lane % 4;
-    int stage = 0;
-    uint32_t phase = 0;
-    for (int tile = tile0; tile < p.n_tiles; tile += tile_step) {
-      const int w0 = (tile % p.n_tiles_w) * kBM;
-      const float *srow[kGroups];
-      float s_cur[kGroups], s_next[kGroups];
-#pragma unroll
-      for (int g = 0; g < kGroups; ++g) {
-        const int n = w0 + (cw + g * kWarpsC) * 8 + sub_row;
-        srow[g] = n < p.N ? p.w_scales + static_cast<int64_t>(n) * p.kb_per_row : nullptr;
-        s_cur[g] = (srow[g] != nullptr && nkb > 0) ? __ldg(srow[g] + kb0) : 0.0f;
-      }
-      bool ok = true;
-      for (int it = 0; it < num_iters; ++it) {
-        if (it < nkb) {
-#pragma unroll
-          for (int g = 0; g < kGroups; ++g) {
-            s_next[g] = (srow[g] != nullptr && it + 1 < nkb) ? __ldg(srow[g] + kb0 + it + 1) : 0.0f;
-          }
-          const bool got = ptx::mbar_wait(&full[stage], phase);
-          if (__any_sync(0xffffffffu, !got)) {
-            if (lane == 0) record_timeout(p.err, abort_flag);
-            ok = false;
-            break;
-          }
-          uint8_t *sa = smem + stage * C::kStageBytes;
-          const uint8_t *raw = sa + C::kABytes + C::kXBytes;
-#pragma unroll
-          for (int g = 0; g < kGroups; ++g) {
-            const int r = (cw + g * kWarpsC) * 8 + sub_row;
-            const float sc = s_cur[g];
-            const uint4 codes = *reinterpret_cast<const uint4 *>(raw + r * kBK + chunk * 16);
-            const uint32_t words[4] = {codes.x, codes.y, codes.z, codes.w};
-            uint32_t outw[8];
-            const uint64_t sc2 = ptx::splat_f32x2(sc);
-#pragma unroll
-            for (int wd = 0; wd < 4; ++wd) {
-              const uint32_t u = words[wd] ^ 0x80808080u;
-#pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                // 2^23 + (q + 128) as floats, then (that - (2^23 + 128)) * s for
-                // two codes per packed f32x2 add and multiply: exactly q * s.
-                const uint32_t b0 = __byte_perm(u, 0x4B000000u, 0x7440u | (2 * h));
-                const uint32_t b1 = __byte_perm(u, 0x4B000000u, 0x7440u | (2 * h + 1));
-                float lo, hi;
-                ptx::dequant_pair(b0, b1, sc2, lo, hi);
-                outw[2 * wd + h] = kBf16 ? ptx::pack_bf16x2(lo, hi) : ptx::pack_f16x2(lo, hi);
-              }
-            }
-            uint8_t *dst_row = sa + r * 128;
-            const int sw = r & 7;
-            *reinterpret_cast<uint4 *>(dst_row + (((2 * chunk) ^ sw) << 4)) =
-                make_uint4(outw[0], outw[1], outw[2], outw[3]);
-            *reinterpret_cast<uint4 *>(dst_row + (((2 * chunk + 1) ^ sw) << 4)) =
-                make_uint4(outw[4], outw[5], outw[6], outw[7]);
-          }
-          ptx::fence_proxy_async_smem();
-          ptx::warp_arrive(&conv_full[stage]);
-#pragma unroll
-          for (int g = 0; g < kGroups; ++g) s_cur[g] = s_next[g];
-        } else if (!ptx::mbar_wait(&full[stage], phase)) {
-          // Adapter stages are not converted, but waiting for them keeps this
-          // warp within one phase of every stage's barrier (a parity wait
-          // cannot tell phase u from phase u - 2).
-          if (lane == 0) record_timeout(p.err, abort_flag);
-          ok = false;
-          break;
-        }
-        if (++stage == C::kStages) {
-          stage = 0;
-          phase ^= 1;
-        }
-      }
-      if (!ok) break;
-    }
-  }
-
-  if constexpr (C::kSplit) {
-    if (split) {
-      // Reduce the cluster's partials: CTA `rank` owns rows [r0, r1) of the tile.
-      ptx::tc_fence_before();
-      ptx::cluster_sync();
-      const int tile = tile0;
-      const int w0 = (tile % p.n_tiles_w) * kBM;
-      const int t0 = (tile / p.n_tiles_w) * BT;
-      const int r0 = rank * kBM / p.splits;
-      const int r1 = (rank + 1) * kBM / p.splits;
-      const int rows = r1 - r0;
-      const uint32_t base = ptx::smem_addr(partial);
-      uint16_t *out = static_cast<uint16_t *>(p.out);
-      for (int item = threadIdx.x; item < rows * (BT / 4); item += C::kThreads) {
-        const int row = r0 + item % rows;
-        const int t4 = (item / rows) * 4;
-        const uint32_t off = static_cast<uint32_t>((row * BT + t4) * 4);
-        float4 acc = make_float4(0, 0, 0, 0);
-        for (int peer = 0; peer < p.splits; ++peer) {
-          const float4 v = ptx::ld_shared_cluster_f4(ptx::map_shared_rank(base + off, peer));
-          acc.x += v.x;
-          acc.y += v.y;
-          acc.z += v.z;
-          acc.w += v.w;
-        }
-        const int n = w0 + row;
-        if (n < p.N) {
-          const float vals[4] = {acc.x, acc.y, acc.z, acc.w};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int t = t0 + t4 + j;
-            if (t < p.M) {
-              const uint32_t h = kBf16 ? ptx::pack_bf16x2(vals[j], 0.0f)
-                                       : ptx::pack_f16x2(vals[j], 0.0f);
-              out[static_cast<int64_t>(t) * p.ldo + p.out_col0 + n] =
-                  static_cast<uint16_t>(h & 0xffffu);
-            }
-          }
-        }
-      }
-      ptx::cluster_sync();
-    }
-  }
-
-  ptx::tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    ptx::tc_fence_after();
-    ptx::tmem_dealloc(tmem_base, C::kTmemCols);
-  }
-}
 
 // ---------------------------------------------------------------------------
 // W8 + LoRA for decode-sized token counts (M <= 128): one 128-feature tile
@@ -1573,8 +1039,8 @@ __global__ void __launch_bounds__(DecCfg<BT>::kThreads, DecCfg<BT>::kMinBlocks)
 //
 // Each converted 128 x 32 weight tile feeds two N = 256 MMAs (tokens
 // [t0, t0+256) and [t0+256, t0+512)), so every int8 code is converted once per
-// 512 tokens instead of once per 256 — half the conversion work per FLOP of
-// w8_swap_kernel<256>. The 128 x 512 fp32 accumulator takes all 512 TMEM
+// 512 tokens instead of once per 256 (half the conversion work per FLOP of a
+// 256-token tile). The 128 x 512 fp32 accumulator takes all 512 TMEM
 // columns (single buffer); k-blocks are 32 wide (64-byte swizzled rows) so the
 // ring stays 5 stages deep. The adapter runs as rank/16 extra iterations of
 // one K = 16 step each (A = 16 columns of B^T, B = 16 columns of P).
@@ -1990,11 +1456,11 @@ int make_map(CUtensorMap *map, const void *base, int esize, int64_t inner, int64
   return r == CUDA_SUCCESS ? CF_OK : CF_ERR_UNSUPPORTED;
 }
 
-template <int BN, bool kBf16, bool kInt8>
+template <int BN, bool kBf16>
 int launch_gemm(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &pa,
                 const CUtensorMap &pb, const GemmParams &params, cudaStream_t stream) {
-  using C = GemmCfg<BN, kInt8>;
-  auto kernel = lora_gemm_kernel<BN, kBf16, kInt8>;
+  using C = GemmCfg<BN>;
+  auto kernel = lora_gemm_kernel<BN, kBf16>;
   CFB_TRY_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(C::kSmemBytes)));
   const int grid = std::max(1, std::min(params.n_tiles, sm_count()));
@@ -2092,83 +1558,6 @@ int launch_down_projection(const LinearArgs &L, unsigned *err, cudaStream_t stre
   return check_launch();
 }
 
-template <int BT, bool kBf16, bool kStaged>
-int launch_w8_swap(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
-  using C = W8Cfg<BT, kStaged>;
-  const int r = static_cast<int>(L.r);
-  CUtensorMap tm_x, tm_codes, tm_p, tm_bt;
-  int st = CF_OK;
-  if ((st = make_map(&tm_x, L.x, 2, L.k, L.m, kBK, BT, true))) return st;
-  if ((st = make_map(&tm_codes, L.w, 1, L.k, L.n, kBK, kBM, false))) return st;
-  if ((st = make_map(&tm_p, L.ws, 2, r, L.m, r, BT, true))) return st;
-  W8Params p{};
-  if (L.b_layout == CF_LAYOUT_REF) {
-    // b [r, N]: N contiguous -> MN-major A operand, chunks of 64 features x r.
-    if ((st = make_map(&tm_bt, L.b, 2, L.n, r, 64, r, true))) return st;
-    p.extra_b_mn = 1;
-  } else {
-    // b^T [N, r]: r contiguous -> K-major A operand.
-    if ((st = make_map(&tm_bt, L.b, 2, r, L.n, r, kBM, true))) return st;
-    p.extra_b_mn = 0;
-  }
-  p.M = static_cast<int>(L.m);
-  p.N = static_cast<int>(L.n);
-  p.num_kb = static_cast<int>(L.k / kBK);
-  p.extra_ksteps = r / kUmmaK;
-  p.rank = r;
-  p.w_scales = L.w_scales;
-  p.kb_per_row = static_cast<int>(L.k / kBK);
-  p.out = L.y;
-  if (L.n_dest > 0) {
-    p.ldo = static_cast<int>(L.ldy);
-    p.out_col0 = static_cast<int>(L.col0);
-    p.n_outs = L.n_dest;
-    p.self_out = L.self_dest;
-    for (int d = 0; d < L.n_dest; ++d) p.outs[d] = L.dest[d];
-  } else {
-    p.ldo = static_cast<int>(L.n);
-    p.out_col0 = 0;
-    p.n_outs = 1;
-    p.outs[0] = L.y;
-  }
-  p.n_tiles_w = static_cast<int>((L.n + kBM - 1) / kBM);
-  p.n_tiles = p.n_tiles_w * static_cast<int>((L.m + BT - 1) / BT);
-  p.err = err;
-  int splits = 1;
-  if (C::kSplit) {
-    // Largest split that keeps every CTA resident (kMinBlocks per SM).
-    const int slots = sm_count() * C::kMinBlocks;
-    for (int s = 8; s >= 2; --s) {
-      if (p.n_tiles * s <= slots && s <= p.num_kb) {
-        splits = s;
-        break;
-      }
-    }
-  }
-  p.splits = splits;
-  p.kb_per_split = (p.num_kb + splits - 1) / splits;
-
-  auto kernel = w8_swap_kernel<BT, kBf16, kStaged>;
-  CFB_TRY_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(C::kSmemBytes)));
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(
-      splits > 1 ? p.n_tiles * splits : std::min(p.n_tiles, sm_count() * C::kMinBlocks)));
-  cfg.blockDim = dim3(C::kThreads);
-  cfg.dynamicSmemBytes = C::kSmemBytes;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  set_programmatic_dependency(attr[1]);
-  cfg.attrs = attr;
-  cfg.numAttrs = 2;
-  CFB_TRY_CUDA(cudaLaunchKernelEx(&cfg, kernel, tm_x, tm_codes, tm_p, tm_bt, p));
-  return check_launch();
-}
-
 template <int BT, bool kBf16>
 int launch_w8_decode(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
   using C = DecCfg<BT>;
@@ -2252,9 +1641,6 @@ int launch_w8_wide(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
   p.rank = r;
   p.w_scales = L.w_scales;
   p.kb_per_row = static_cast<int>(L.k / kBK);
-  p.splits = 1;
-  p.kb_per_split = p.num_kb;
-  p.out = L.y;
   OutMaps out_maps;
   std::memset(&out_maps, 0, sizeof(out_maps));
   if (L.n_dest > 0) {
@@ -2320,10 +1706,7 @@ int run_linear(const LinearArgs &L, cudaStream_t stream) {
   CUtensorMap tm_x, tm_w, tm_p, tm_b;
   if ((st = make_map(&tm_x, L.x, 2, L.k, L.m, kBK, kBM, true))) return st;
   GemmParams p{};
-  if (L.int8) {
-    if ((st = make_map(&tm_w, L.w, 1, L.k, L.n, kBK, BN, false))) return st;
-    p.b_src = kBInt8;
-  } else if (L.w_layout == CF_LAYOUT_T) {
+  if (L.w_layout == CF_LAYOUT_T) {
     if ((st = make_map(&tm_w, L.w, 2, L.k, L.n, kBK, BN, true))) return st;
     p.b_src = kBKMajor;
   } else {
@@ -2350,13 +1733,10 @@ int run_linear(const LinearArgs &L, cudaStream_t stream) {
   p.out_scale = 1.0f;
   p.out = L.y;
   p.ldo = static_cast<int>(L.n);
-  p.w_scales = L.w_scales;
-  p.kb_per_row = static_cast<int>(L.k / kBK);
   p.n_tiles_n = static_cast<int>((L.n + BN - 1) / BN);
   p.n_tiles = static_cast<int>((L.m + kBM - 1) / kBM) * p.n_tiles_n;
   p.err = err;
-  if (L.int8) return launch_gemm<BN, kBf16, true>(tm_x, tm_w, tm_p, tm_b, p, stream);
-  return launch_gemm<BN, kBf16, false>(tm_x, tm_w, tm_p, tm_b, p, stream);
+  return launch_gemm<BN, kBf16>(tm_x, tm_w, tm_p, tm_b, p, stream);
 }
 
 int validate_and_run(const LinearArgs &L, cf_stream_t stream) {

@@ -127,20 +127,6 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
       : "memory");
 }
 
-// Tiled tensor prefetch into L2 (no shared-memory destination, no completion
-// signal): later loads of the same box hit L2.
-__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap *map, int32_t c0, int32_t c1) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(c0), "r"(c1)
-               : "memory");
-}
-
-// Prefetch of the line holding `ptr` into L2.
-__device__ __forceinline__ void prefetch_l2(const void *ptr) {
-  asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(ptr)));
-}
-
 // Non-tensor bulk copy global -> shared, completing on an mbarrier (16-byte
 // aligned addresses, size a multiple of 16).
 __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes,
