@@ -483,6 +483,7 @@ class LoraLinear:
     m, k, n, r, alpha = 8192, 4096, 4096, 16, 32.0
     int8 = False
     x_std, w_std, ab_std = 1.0, 0.02, 0.01
+    main_kernel = "lora_gemm_kernel<256>"
 
     def __init__(self, dist: Dist, _layers: int = 0):
         self.dist = dist
@@ -490,7 +491,7 @@ class LoraLinear:
                        f"{'GB/s' if self.unit == 'GB/s' else 'TFLOP/s'} "
                        f"(x [{self.m},{self.k}], W [{self.n},{self.k}], r {self.r})")
         self.dtype = "bf16 x int8->bf16 (fp32 acc)" if self.int8 else "bf16 (fp32 acc)"
-        self.kernel = "lora_gemm_kernel (down-projection + main, one call)"
+        self.kernel = self.main_kernel + " + down_proj_kernel (one call; PDL-overlapped)"
 
     def flops(self) -> float:
         return 2.0 * self.m * self.n * self.k + 2.0 * self.m * self.r * (self.k + self.n)
@@ -621,6 +622,7 @@ class W8Decode(LoraLinear):
     bound = "hbm"
     m, k, n, r = 32, 4096, 11008, 16
     int8 = True
+    main_kernel = "w8_decode_kernel<32> (split-K cluster of 3, 258 CTAs)"
 
 
 class W8Prefill(LoraLinear):
@@ -629,6 +631,7 @@ class W8Prefill(LoraLinear):
     name = "w8_lora_prefill_4096x4096x11008"
     m, k, n, r = 4096, 4096, 11008, 16
     int8 = True
+    main_kernel = "w8_wide_kernel (128 x 512 tiles, TMA-store epilogue)"
 
 
 class W8ColumnSharded:

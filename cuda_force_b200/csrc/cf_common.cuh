@@ -4,6 +4,7 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 
 #include "cudaforge_b200.h"
@@ -49,3 +50,24 @@ inline bool aligned_to(const void *p, uintptr_t bytes) {
     cudaError_t cfb_err_ = (expr);                           \
     if (cfb_err_ != cudaSuccess) return ::cfb::record_cuda_error(cfb_err_); \
   } while (0)
+
+namespace cfb {
+
+// Raises `Kernel`'s dynamic shared-memory limit once per device; the
+// attribute lasts for the life of the CUDA context, so later launches skip the
+// driver call (a context torn down by cudaDeviceReset would need it again).
+template <auto Kernel>
+int allow_dynamic_smem(size_t bytes) {
+  static std::atomic<uint64_t> done{0};
+  int dev = 0;
+  CFB_TRY_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return CF_ERR_UNSUPPORTED;
+  const uint64_t bit = uint64_t{1} << dev;
+  if (done.load(std::memory_order_acquire) & bit) return CF_OK;
+  CFB_TRY_CUDA(cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(bytes)));
+  done.fetch_or(bit, std::memory_order_release);
+  return CF_OK;
+}
+
+}  // namespace cfb

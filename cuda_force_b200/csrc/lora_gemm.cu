@@ -1461,8 +1461,7 @@ int launch_gemm(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &p
                 const CUtensorMap &pb, const GemmParams &params, cudaStream_t stream) {
   using C = GemmCfg<BN>;
   auto kernel = lora_gemm_kernel<BN, kBf16>;
-  CFB_TRY_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(C::kSmemBytes)));
+  if (int st = allow_dynamic_smem<lora_gemm_kernel<BN, kBf16>>(C::kSmemBytes)) return st;
   const int grid = std::max(1, std::min(params.n_tiles, sm_count()));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
@@ -1540,8 +1539,7 @@ int launch_down_projection(const LinearArgs &L, unsigned *err, cudaStream_t stre
   p.kb_per_split = (p.num_kb + splits - 1) / splits;
 
   auto kernel = down_proj_kernel<R, kBf16>;
-  CFB_TRY_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(C::kSmemBytes)));
+  if (int st_ = allow_dynamic_smem<down_proj_kernel<R, kBf16>>(C::kSmemBytes)) return st_;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(m_tiles * splits));
   cfg.blockDim = dim3(C::kThreads);
@@ -1598,8 +1596,7 @@ int launch_w8_decode(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
   // Whole raw stages per CTA: every slice but the last starts on a stage.
   p.kb_per_split = ((p.num_kb + splits - 1) / splits + C::kRawKb - 1) / C::kRawKb * C::kRawKb;
   auto kernel = w8_decode_kernel<BT, kBf16>;
-  CFB_TRY_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(C::kSmemBytes)));
+  if (int st_ = allow_dynamic_smem<w8_decode_kernel<BT, kBf16>>(C::kSmemBytes)) return st_;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(n_tiles * splits));
   cfg.blockDim = dim3(C::kThreads);
@@ -1667,8 +1664,7 @@ int launch_w8_wide(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
   p.rb_per_group = L.rb_per_group;
   p.n_groups = L.n_groups;
   auto kernel = w8_wide_kernel<kBf16, kTmaStore>;
-  CFB_TRY_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(C::kSmemBytes)));
+  if (int st_ = allow_dynamic_smem<w8_wide_kernel<kBf16, kTmaStore>>(C::kSmemBytes)) return st_;
   const int grid = std::max(1, std::min(p.n_tiles, sm_count()));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));

@@ -675,9 +675,7 @@ bool tma_eligible(const void *in, const int8_t *codes, const float *scales) {
 template <typename T>
 int launch_tma_quant(const GroupedArgs &args, int64_t tiles, cudaStream_t stream) {
   using C = TmaQuantCfg<T>;
-  CFB_TRY_CUDA(cudaFuncSetAttribute(quantize_tma_kernel<T>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(C::kSmemBytes)));
+  if (int st = allow_dynamic_smem<quantize_tma_kernel<T>>(C::kSmemBytes)) return st;
   unsigned *err = device_error_word();
   if (err == nullptr) return record_cuda_error(cudaGetLastError());
   const int64_t ctas = (tiles + C::kWarps - 1) / C::kWarps;
