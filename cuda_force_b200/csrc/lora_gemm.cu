@@ -1398,6 +1398,348 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore>::kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// fp32 LoRA linear on the tensor cores: kind::tf32 with a three-product split.
+//
+// The reference's CUDA lora_linear is fp32 (cpp/src/bindings.cpp:94-127,
+// cuda/src/lora_linear.cu:237-277, CUDA-core FMA); its tests hold it to 1e-3
+// of an fp32 CPU product. One tf32 pass (10 explicit mantissa bits) is not
+// that accurate, so every operand v is split into hi = tf32(v) and
+// lo = v - hi (exact in fp32) and the MMA accumulates hi*hi + hi*lo + lo*hi in
+// fp32; the dropped lo*lo term is below 2^-22 of the product.
+//
+// One kernel serves both launches of a call: the down-projection (B = A_lora,
+// N = rank, out = P scaled by alpha/r) and the main product, whose adapter is
+// ceil(rank/32) extra k-blocks with A = P tile and B = the B_lora slice. The
+// splitters write hi over the loaded tile and lo into a twin buffer 16 KB
+// above it, both K-major (128-byte rows of 32 k, 128B-swizzled), which is the
+// only operand form the MMA is given. A B operand stored [K, N] (N
+// contiguous) arrives as four 32-column x 32-row chunks and is transposed by
+// the splitters in 4 x 4 register blocks on the way.
+//   warp 0 TMA producer, warp 1 TMEM owner + MMA issuer, warps 4-7 epilogue
+//   (thread = output row), warps 8-15 splitters; 128 x 128 tiles, persistent,
+//   double-buffered TMEM accumulators.
+// ---------------------------------------------------------------------------
+struct F32Cfg {
+  static constexpr int BN = 128;
+  static constexpr int kBKf = 32;                      // k-block: 32 fp32 = one 128 B row
+  static constexpr int kTileBytes = 128 * kBKf * 4;    // 16 KB (A or B, hi or lo)
+  static constexpr int kStageBytes = 4 * kTileBytes;   // A hi, A lo, B hi, B lo
+  static constexpr int kStages = 3;
+  static constexpr int kThreads = 512;
+  static constexpr int kTmemCols = 2 * BN;
+  static constexpr size_t kSmemBytes = 1024 + static_cast<size_t>(kStages) * kStageBytes + 256;
+};
+
+struct F32Params {
+  int M, N;
+  int num_kb;       // main k-blocks (ceil(K / 32))
+  int extra_kb;     // adapter k-blocks (ceil(rank / 32)); 0 for the down-projection
+  int n_mma;        // MMA N (16..128, multiple of 16)
+  int b_mn;         // main B stored [K, N]
+  int e_mn;         // adapter B stored [rank, N]
+  int ldo;          // output row stride (elements)
+  float out_scale;
+  float *out;       // [M, ldo] fp32
+  int n_tiles_n;
+  int n_tiles;
+  unsigned *err;
+};
+
+__global__ void __launch_bounds__(F32Cfg::kThreads, 1)
+    lora_f32_kernel(const __grid_constant__ CUtensorMap tm_a,
+                    const __grid_constant__ CUtensorMap tm_b,
+                    const __grid_constant__ CUtensorMap tm_pa,
+                    const __grid_constant__ CUtensorMap tm_pb, const F32Params p) {
+  using C = F32Cfg;
+  // A second launch that consumes this one's output (P) may start now; it
+  // waits for this grid before its first read of P.
+  ptx::grid_dep_launch_dependents();
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kStages * C::kStageBytes);
+  uint64_t *full = bars;                        // [kStages] TMA -> splitters
+  uint64_t *split = bars + C::kStages;          // [kStages] splitters -> MMA
+  uint64_t *empty = bars + 2 * C::kStages;      // [kStages] MMA -> producer
+  uint64_t *tmem_full = bars + 3 * C::kStages;  // [2] MMA -> epilogue
+  uint64_t *tmem_empty = tmem_full + 2;         // [2] epilogue -> MMA
+  uint64_t *drain = tmem_empty + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  int *abort_flag = reinterpret_cast<int *>(tmem_slot + 1);
+  constexpr int kSplitWarps = kConvThreads / kWarp;
+
+  const int warp = threadIdx.x / kWarp;
+  const int lane = threadIdx.x % kWarp;
+  const int num_iters = p.num_kb + p.extra_kb;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      ptx::mbar_init(&full[s], 1);
+      ptx::mbar_init(&split[s], kSplitWarps);
+      ptx::mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      ptx::mbar_init(&tmem_full[a], 1);
+      ptx::mbar_init(&tmem_empty[a], 4);
+    }
+    ptx::mbar_init(drain, 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, C::kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t outstanding = 0, issue_parity = 0;
+      bool dep_ready = false;
+      for (int tile = blockIdx.x; tile < p.n_tiles && !aborted(abort_flag); tile += gridDim.x) {
+        const int m0 = (tile / p.n_tiles_n) * 128;
+        const int n0 = (tile % p.n_tiles_n) * C::BN;
+        for (int it = 0; it < num_iters; ++it) {
+          if (!ptx::mbar_wait(&empty[stage], phase ^ 1)) {
+            record_timeout(p.err, abort_flag);
+            break;
+          }
+          uint8_t *sa = smem + stage * C::kStageBytes;
+          uint8_t *sb = sa + 2 * C::kTileBytes;
+          const bool main_kb = it < p.num_kb;
+          if (!main_kb && !dep_ready) {  // P comes from the launch just before
+            ptx::grid_dep_wait();
+            dep_ready = true;
+          }
+          const CUtensorMap *ma = main_kb ? &tm_a : &tm_pa;
+          const CUtensorMap *mb = main_kb ? &tm_b : &tm_pb;
+          const bool mn = main_kb ? p.b_mn != 0 : p.e_mn != 0;
+          const int k0 = (main_kb ? it : it - p.num_kb) * C::kBKf;
+          ptx::mbar_expect_tx(&full[stage], 2 * C::kTileBytes);
+          ptx::tma_load_2d(sa, ma, &full[stage], k0, m0);
+          if (mn) {
+            // [K, N]: four 32-column chunks of 32 k-rows, 128B-swizzled.
+            for (int c = 0; c < C::BN / 32; ++c) {
+              ptx::tma_load_2d(sb + c * 4096, mb, &full[stage], n0 + c * 32, k0);
+            }
+          } else {
+            ptx::tma_load_2d(sb, mb, &full[stage], k0, n0);
+          }
+          outstanding |= 1u << stage;
+          issue_parity = (issue_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (aborted(abort_flag)) {
+        for (int s = 0; s < C::kStages; ++s) {
+          if (outstanding & (1u << s)) ptx::mbar_wait(&full[s], (issue_parity >> s) & 1u, 200000000ull);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = ptx::make_idesc_tf32(128, p.n_mma, false, false);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (int tile = blockIdx.x; tile < p.n_tiles && !aborted(abort_flag);
+           tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
+        if (!ptx::mbar_wait(&tmem_empty[acc], acc_phase ^ 1)) {
+          record_timeout(p.err, abort_flag);
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * C::BN;
+        bool ok = true;
+        for (int it = 0; it < num_iters; ++it) {
+          if (!ptx::mbar_wait(&split[stage], phase)) {
+            record_timeout(p.err, abort_flag);
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint32_t a_hi = ptx::smem_addr(smem + stage * C::kStageBytes);
+          const uint32_t a_lo = a_hi + C::kTileBytes;
+          const uint32_t b_hi = a_hi + 2 * C::kTileBytes;
+          const uint32_t b_lo = a_hi + 3 * C::kTileBytes;
+          for (int ks = 0; ks < C::kBKf / 8; ++ks) {
+            // K = 8 per MMA: 32 bytes along the 128-byte K-major rows.
+            const uint64_t ah = kmajor_desc(a_hi, 128, ks);
+            const uint64_t al = kmajor_desc(a_lo, 128, ks);
+            const uint64_t bh = kmajor_desc(b_hi, 128, ks);
+            const uint64_t bl = kmajor_desc(b_lo, 128, ks);
+            const uint32_t first = (it == 0 && ks == 0) ? 0u : 1u;
+            ptx::mma_tf32(d_tmem, ah, bh, idesc, first);
+            ptx::mma_tf32(d_tmem, ah, bl, idesc, 1u);
+            ptx::mma_tf32(d_tmem, al, bh, idesc, 1u);
+          }
+          ptx::mma_commit(&empty[stage]);
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        ptx::mma_commit(&tmem_full[acc]);
+      }
+      if (aborted(abort_flag)) {
+        ptx::mma_commit(drain);
+        ptx::mbar_wait(drain, 0, 200000000ull);
+      }
+    }
+  } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) {
+    // ------------------------------------------------------------------ epilogue
+    const int quarter = warp % 4;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
+      const bool ok = ptx::warp_wait(&tmem_full[acc], acc_phase);
+      if (__any_sync(0xffffffffu, !ok)) {
+        if (lane == 0) record_timeout(p.err, abort_flag);
+        break;
+      }
+      ptx::tc_fence_after();
+      const int m0 = (tile / p.n_tiles_n) * 128;
+      const int n0 = (tile % p.n_tiles_n) * C::BN;
+      const int row = m0 + quarter * 32 + lane;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * C::BN;
+      float *out_row = p.out + static_cast<int64_t>(row) * p.ldo;
+#pragma unroll 1
+      for (int c = 0; c < p.n_mma / 16; ++c) {
+        uint32_t v[32];
+        ptx::tmem_ld_32x32b_x16(t_row + c * 16, v);
+        ptx::tmem_ld_wait();
+        if (row < p.M) {
+          const int col0 = n0 + c * 16;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            if (col0 + q * 4 < p.N) {
+              *reinterpret_cast<float4 *>(out_row + col0 + q * 4) =
+                  make_float4(__uint_as_float(v[4 * q]) * p.out_scale,
+                              __uint_as_float(v[4 * q + 1]) * p.out_scale,
+                              __uint_as_float(v[4 * q + 2]) * p.out_scale,
+                              __uint_as_float(v[4 * q + 3]) * p.out_scale);
+            }
+          }
+        }
+      }
+      ptx::tc_fence_before();
+      ptx::warp_arrive(&tmem_empty[acc]);
+    }
+  } else if (warp >= kConvWarp0) {
+    // ------------------------------------------------------------------ splitters
+    // A tile (and a K-major B tile): thread t splits float4 q = i * 256 + t
+    // in place (hi) and 16 KB above (lo); the swizzle is the same for both.
+    // An MN-major B tile: thread t owns the 4 x 4 block at n = 4 (t % 32),
+    // k = 4 (t / 32), reads it from its chunk, and after all splitters have
+    // read, writes it transposed as four 16-byte K-major row pieces.
+    // A warp whose wait gives up (or that sees another role give up) switches
+    // to abort mode: it skips waits and work but still takes part in every
+    // named barrier the other splitters will reach, so none can wait forever.
+    const int t = threadIdx.x - kConvWarp0 * kWarp;
+    int stage = 0;
+    uint32_t phase = 0;
+    bool abort_mode = false;
+    for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x) {
+      for (int it = 0; it < num_iters; ++it) {
+        if (!abort_mode) {
+          if (__any_sync(0xffffffffu, !ptx::mbar_wait(&full[stage], phase))) {
+            if (lane == 0) record_timeout(p.err, abort_flag);
+            abort_mode = true;
+          } else if (aborted(abort_flag)) {
+            abort_mode = true;
+          }
+        }
+        uint8_t *base = smem + stage * C::kStageBytes;
+        const bool mn = it < p.num_kb ? p.b_mn != 0 : p.e_mn != 0;
+        const int n_flat = mn ? 4 : 8;  // float4s split element-wise per thread
+        if (!abort_mode) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            if (i >= n_flat) break;
+            const int q = i * kConvThreads + t;  // A: 0..1023, B (K-major): 1024..2047
+            uint8_t *hi = base + (q >> 10) * 2 * C::kTileBytes + (q & 1023) * 16;
+            const float4 v = *reinterpret_cast<float4 *>(hi);
+            float4 h, l;
+            h.x = ptx::round_tf32(v.x); l.x = v.x - h.x;
+            h.y = ptx::round_tf32(v.y); l.y = v.y - h.y;
+            h.z = ptx::round_tf32(v.z); l.z = v.z - h.z;
+            h.w = ptx::round_tf32(v.w); l.w = v.w - h.w;
+            *reinterpret_cast<float4 *>(hi) = h;
+            *reinterpret_cast<float4 *>(hi + C::kTileBytes) = l;
+          }
+        }
+        if (mn) {
+          uint8_t *bt = base + 2 * C::kTileBytes;
+          const int n0 = 4 * (t % 32);
+          const int k0 = 4 * (t / 32);
+          const int chunk = n0 / 32;
+          const int j = (n0 % 32) / 4;  // 16-byte column of the chunk row
+          const bool work = !abort_mode;
+          float blk[4][4];              // [k][n]
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const int k = k0 + kk;
+            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (work) {
+              v = *reinterpret_cast<const float4 *>(bt + chunk * 4096 + k * 128 +
+                                                    ((j ^ (k & 7)) << 4));
+            }
+            blk[kk][0] = v.x;
+            blk[kk][1] = v.y;
+            blk[kk][2] = v.z;
+            blk[kk][3] = v.w;
+          }
+          ptx::named_bar_sync(2, kConvThreads);  // every chunk read before any row is written
+          if (work) {
+#pragma unroll
+            for (int nn = 0; nn < 4; ++nn) {
+              const int n = n0 + nn;
+              float4 h, l;
+              h.x = ptx::round_tf32(blk[0][nn]); l.x = blk[0][nn] - h.x;
+              h.y = ptx::round_tf32(blk[1][nn]); l.y = blk[1][nn] - h.y;
+              h.z = ptx::round_tf32(blk[2][nn]); l.z = blk[2][nn] - h.z;
+              h.w = ptx::round_tf32(blk[3][nn]); l.w = blk[3][nn] - h.w;
+              uint8_t *dst = bt + n * 128 + (((k0 / 4) ^ (n & 7)) << 4);
+              *reinterpret_cast<float4 *>(dst) = h;
+              *reinterpret_cast<float4 *>(dst + C::kTileBytes) = l;
+            }
+          }
+        }
+        if (!abort_mode) {
+          ptx::fence_proxy_async_smem();
+          ptx::warp_arrive(&split[stage]);
+        }
+        if (++stage == C::kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side: tensor maps and launches.
 // ---------------------------------------------------------------------------
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
@@ -1447,8 +1789,9 @@ int make_map(CUtensorMap *map, const void *base, int esize, int64_t inner, int64
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(inner) * esize};
   const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_outer)};
   const cuuint32_t estr[2] = {1, 1};
-  const CUtensorMapDataType dt =
-      esize == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
+  const CUtensorMapDataType dt = esize == 1   ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                 : esize == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16
+                                              : CU_TENSOR_MAP_DATA_TYPE_UINT32;
   const CUresult r = fn(map, dt, 2, const_cast<void *>(base), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE,
                         swizzle ? swizzle_for(box_inner * esize) : CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -1476,9 +1819,11 @@ int launch_gemm(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &p
   return check_launch();
 }
 
-size_t workspace_bytes(int64_t m, int64_t r) {
+// Down-projection workspace P [m, r]: 16-bit for bf16/f16 calls, fp32 for
+// fp32 calls.
+size_t workspace_bytes(int64_t m, int64_t r, int elem_bytes = 2) {
   if (m <= 0 || r <= 0) return 0;
-  const size_t bytes = static_cast<size_t>(m) * static_cast<size_t>(r) * 2;
+  const size_t bytes = static_cast<size_t>(m) * static_cast<size_t>(r) * elem_bytes;
   return (bytes + 255) & ~static_cast<size_t>(255);
 }
 
@@ -1735,6 +2080,75 @@ int run_linear(const LinearArgs &L, cudaStream_t stream) {
   return launch_gemm<BN, kBf16>(tm_x, tm_w, tm_p, tm_b, p, stream);
 }
 
+// fp32 call: two launches of lora_f32_kernel (down-projection, then the main
+// product with the adapter as extra k-blocks), the second overlapping the
+// first through programmatic dependent launch.
+int launch_f32(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &pa,
+               const CUtensorMap &pb, const F32Params &p, bool dependent, cudaStream_t stream) {
+  if (int st = allow_dynamic_smem<lora_f32_kernel>(F32Cfg::kSmemBytes)) return st;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(std::max(1, std::min(p.n_tiles, sm_count()))));
+  cfg.blockDim = dim3(F32Cfg::kThreads);
+  cfg.dynamicSmemBytes = F32Cfg::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  set_programmatic_dependency(attr[0]);
+  cfg.attrs = attr;
+  cfg.numAttrs = dependent ? 1 : 0;
+  CFB_TRY_CUDA(cudaLaunchKernelEx(&cfg, lora_f32_kernel, a, b, pa, pb, p));
+  return check_launch();
+}
+
+// Map of an fp32 B operand: [K, N] (N contiguous) as 32-column x 32-row
+// MN-major chunks, or [N, K] as 128 rows of 32 K-major elements.
+int make_f32_b_map(CUtensorMap *map, const void *base, bool mn, int64_t k, int64_t n) {
+  return mn ? make_map(map, base, 4, n, k, 32, 32, true) : make_map(map, base, 4, k, n, 32, 128, true);
+}
+
+int run_linear_f32(const LinearArgs &L, cudaStream_t stream) {
+  unsigned *err = device_error_word();
+  if (err == nullptr) return record_cuda_error(cudaGetLastError());
+  const int r = static_cast<int>(L.r);
+  const bool a_mn = L.a_layout == CF_LAYOUT_REF;  // A [K, r]: r contiguous
+  const bool w_mn = L.w_layout == CF_LAYOUT_REF;  // W [K, N]: N contiguous
+  const bool b_mn = L.b_layout == CF_LAYOUT_REF;  // B [r, N]: N contiguous
+  CUtensorMap tm_x, tm_a, tm_w, tm_p, tm_b;
+  int st = CF_OK;
+  if ((st = make_map(&tm_x, L.x, 4, L.k, L.m, 32, 128, true))) return st;
+  if ((st = make_f32_b_map(&tm_a, L.a, a_mn, L.k, r))) return st;
+  if ((st = make_f32_b_map(&tm_w, L.w, w_mn, L.k, L.n))) return st;
+  if ((st = make_map(&tm_p, L.ws, 4, r, L.m, 32, 128, true))) return st;
+  if ((st = make_f32_b_map(&tm_b, L.b, b_mn, r, L.n))) return st;
+  const int m_tiles = static_cast<int>((L.m + 127) / 128);
+  F32Params d{};
+  d.M = static_cast<int>(L.m);
+  d.N = r;
+  d.num_kb = static_cast<int>((L.k + F32Cfg::kBKf - 1) / F32Cfg::kBKf);
+  d.extra_kb = 0;
+  d.n_mma = r;
+  d.b_mn = a_mn ? 1 : 0;
+  d.e_mn = 0;
+  d.ldo = r;
+  d.out_scale = L.scale;
+  d.out = static_cast<float *>(L.ws);
+  d.n_tiles_n = 1;
+  d.n_tiles = m_tiles;
+  d.err = err;
+  if ((st = launch_f32(tm_x, tm_a, tm_x, tm_a, d, false, stream))) return st;
+  F32Params p = d;
+  p.N = static_cast<int>(L.n);
+  p.extra_kb = (r + F32Cfg::kBKf - 1) / F32Cfg::kBKf;
+  p.n_mma = F32Cfg::BN;
+  p.b_mn = w_mn ? 1 : 0;
+  p.e_mn = b_mn ? 1 : 0;
+  p.ldo = static_cast<int>(L.n);
+  p.out_scale = 1.0f;
+  p.out = static_cast<float *>(L.y);
+  p.n_tiles_n = static_cast<int>((L.n + F32Cfg::BN - 1) / F32Cfg::BN);
+  p.n_tiles = m_tiles * p.n_tiles_n;
+  return launch_f32(tm_x, tm_w, tm_p, tm_b, p, true, stream);
+}
+
 int validate_and_run(const LinearArgs &L, cf_stream_t stream) {
   if (L.m < 0 || L.k < 0 || L.n < 0 || L.r < 0) return CF_ERR_INVALID_ARGUMENT;
   if (L.m == 0 || L.n == 0) return CF_OK;
@@ -1742,9 +2156,14 @@ int validate_and_run(const LinearArgs &L, cf_stream_t stream) {
       (L.int8 && L.w_scales == nullptr)) {
     return CF_ERR_INVALID_ARGUMENT;
   }
-  if (L.dtype != CF_DTYPE_BF16 && L.dtype != CF_DTYPE_F16) return CF_ERR_UNSUPPORTED;
+  const bool f32 = L.dtype == CF_DTYPE_F32;
+  if (L.dtype != CF_DTYPE_BF16 && L.dtype != CF_DTYPE_F16 && !(f32 && !L.int8)) {
+    return CF_ERR_UNSUPPORTED;
+  }
   if (L.r != 16 && L.r != 32 && L.r != 64) return CF_ERR_UNSUPPORTED;
-  if (L.k == 0 || L.k % (L.int8 ? kBK : 8) != 0 || L.n % 8 != 0) return CF_ERR_UNSUPPORTED;
+  // Row strides must be whole 16-byte units for TMA.
+  const int64_t k_align = L.int8 ? kBK : (f32 ? 4 : 8);
+  if (L.k == 0 || L.k % k_align != 0 || L.n % (f32 ? 4 : 8) != 0) return CF_ERR_UNSUPPORTED;
   if ((L.w_layout != CF_LAYOUT_REF && L.w_layout != CF_LAYOUT_T) ||
       (L.a_layout != CF_LAYOUT_REF && L.a_layout != CF_LAYOUT_T) ||
       (L.b_layout != CF_LAYOUT_REF && L.b_layout != CF_LAYOUT_T)) {
@@ -1754,9 +2173,12 @@ int validate_and_run(const LinearArgs &L, cf_stream_t stream) {
   for (const void *ptr : {L.x, L.w, L.a, L.b, static_cast<const void *>(L.y)}) {
     if (!aligned_to(ptr, 16)) return CF_ERR_MISALIGNED;
   }
-  if (L.ws == nullptr || L.ws_bytes < workspace_bytes(L.m, L.r)) return CF_ERR_WORKSPACE;
+  if (L.ws == nullptr || L.ws_bytes < workspace_bytes(L.m, L.r, f32 ? 4 : 2)) {
+    return CF_ERR_WORKSPACE;
+  }
   if (!aligned_to(L.ws, 16)) return CF_ERR_MISALIGNED;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (f32) return run_linear_f32(L, s);
   return L.dtype == CF_DTYPE_BF16 ? run_linear<true>(L, s) : run_linear<false>(L, s);
 }
 
@@ -1776,8 +2198,9 @@ int validate_and_run(const LinearArgs &L, cf_stream_t stream) {
 // the library holds until the process exits.
 //
 // Limits and rules:
-//   * at most kNoAllocScratchBytes (4 MiB) of workspace: m * rank * 2 bytes,
-//     rounded up to 256 (m <= 131072 at rank 16, m <= 32768 at rank 64);
+//   * at most kNoAllocScratchBytes (4 MiB) of workspace: m * rank * 2 bytes
+//     (4 for fp32 calls), rounded up to 256 (bf16/f16: m <= 131072 at rank 16,
+//     m <= 32768 at rank 64);
 //     larger calls return CF_ERR_WORKSPACE and launch nothing;
 //   * the array is shared by every call on a device and keeps the last call's
 //     contents. Nothing needs to start at zero: each call's down-projection
@@ -1820,7 +2243,7 @@ int cf_lora_linear_noalloc(const void *x, const void *w, int w_layout, const voi
                            int64_t k, int64_t n, int64_t rank, float scale, int dtype,
                            cf_stream_t stream) {
   if (m < 0 || rank < 0) return CF_ERR_INVALID_ARGUMENT;
-  const size_t need = cfb::workspace_bytes(m, rank);
+  const size_t need = cfb::workspace_bytes(m, rank, dtype == CF_DTYPE_F32 ? 4 : 2);
   if (need > cfb::kNoAllocScratchBytes) return CF_ERR_WORKSPACE;
   void *scratch = nullptr;
   if (m > 0 && n > 0) {
@@ -1832,7 +2255,8 @@ int cf_lora_linear_noalloc(const void *x, const void *w, int w_layout, const voi
 }
 
 size_t cf_lora_linear_workspace_bytes(int64_t m, int64_t rank) {
-  return cfb::workspace_bytes(m, rank);
+  // Enough for every dtype (fp32 calls keep P in fp32).
+  return cfb::workspace_bytes(m, rank, 4);
 }
 
 int cf_lora_linear(const void *x, const void *w, int w_layout, const void *a, int a_layout,

@@ -234,6 +234,24 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64
       : "memory");
 }
 
+// D (TMEM, fp32) [+]= A * B with A, B fp32 read as tf32 (kind::tf32, K = 8).
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// fp32 rounded to the nearest tf32 (10 explicit mantissa bits, ties away).
+__device__ __forceinline__ float round_tf32(float v) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
+  return __uint_as_float(r);
+}
+
 // Arrives on `bar` once all previously issued tcgen05.mma of this thread retire.
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
   asm volatile(
@@ -339,6 +357,15 @@ __host__ __device__ constexpr uint32_t make_idesc_f16(bool bf16, int m, int n, b
   return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
          ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
          ((static_cast<uint32_t>(n) >> 3) << 17) | ((static_cast<uint32_t>(m) >> 4) << 24);
+}
+
+// Instruction descriptor of kind::tf32 with fp32 accumulation (A and B format
+// code 2 = tf32; other fields as make_idesc_f16).
+__host__ __device__ constexpr uint32_t make_idesc_tf32(int m, int n, bool a_mn_major,
+                                                       bool b_mn_major) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((a_mn_major ? 1u : 0u) << 15) |
+         ((b_mn_major ? 1u : 0u) << 16) | ((static_cast<uint32_t>(n) >> 3) << 17) |
+         ((static_cast<uint32_t>(m) >> 4) << 24);
 }
 
 // Both lanes of a packed f32x2 set to v.

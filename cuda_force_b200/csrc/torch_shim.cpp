@@ -165,9 +165,6 @@ at::Tensor lora_linear_cuda(const at::Tensor &x, const at::Tensor &w, const at::
   TORCH_CHECK(x.dim() == 2, "x must be 2-D, got ", x.dim(), " dimensions");
   check_contiguous(x, "x");
   const int dtype = dtype_code(x, "x");
-  TORCH_CHECK(dtype != CF_DTYPE_F32,
-              "lora_linear: float32 inputs are not supported by the tensor-core path; "
-              "pass bfloat16 or float16");
   for (const at::Tensor *t : {&w, &a, &b}) {
     TORCH_CHECK(t->scalar_type() == x.scalar_type(), "x, w, a and b must share one dtype");
   }
@@ -186,14 +183,42 @@ at::Tensor lora_linear_cuda(const at::Tensor &x, const at::Tensor &w, const at::
   int alp = al, blp = bl;
   const int64_t rp = padded_rank(r);
   pad_adapter(ap, bp, alp, blp, r, rp);
-  at::Tensor y = at::empty({m, n}, x.options());
+  // The kernels read rows with TMA, whose row strides are whole 16-byte units
+  // (8 16-bit or 4 fp32 elements). Other feature counts are zero-padded here,
+  // which leaves the product unchanged, and the output is cut back.
+  const int64_t unit = dtype == CF_DTYPE_F32 ? 4 : 8;
+  const int64_t kp = (k + unit - 1) / unit * unit;
+  const int64_t np = (n + unit - 1) / unit * unit;
+  at::Tensor xp = x, wp = w;
+  int wlp = wl;
+  if (kp != k || np != n) {
+    if (kp != k) {
+      xp = at::zeros({m, kp}, x.options());
+      xp.narrow(1, 0, k).copy_(x);
+      at::Tensor a2 = at::zeros({kp, rp}, ap.options());
+      a2.narrow(0, 0, k).copy_(ap);
+      ap = a2;
+      alp = CF_LAYOUT_REF;
+    }
+    wp = at::zeros({kp, np}, w.options());
+    wp.narrow(0, 0, k).narrow(1, 0, n).copy_(w);
+    wlp = CF_LAYOUT_REF;
+    if (np != n) {
+      at::Tensor b2 = at::zeros({rp, np}, bp.options());
+      b2.narrow(1, 0, n).copy_(bp);
+      bp = b2;
+      blp = CF_LAYOUT_REF;
+    }
+  }
+  at::Tensor y = at::empty({m, np}, x.options());
   const size_t ws_bytes = cf_lora_linear_workspace_bytes(m, rp);
   at::Tensor ws = at::empty({static_cast<int64_t>(ws_bytes)}, x.options().dtype(at::kByte));
-  check_status(cf_lora_linear(x.data_ptr(), w.data_ptr(), wl, ap.data_ptr(), alp, bp.data_ptr(),
-                              blp, y.data_ptr(), m, k, n, rp, static_cast<float>(scale), dtype,
-                              ws.data_ptr(), ws_bytes, current_stream()),
+  check_status(cf_lora_linear(xp.data_ptr(), wp.data_ptr(), wlp, ap.data_ptr(), alp,
+                              bp.data_ptr(), blp, y.data_ptr(), m, kp, np, rp,
+                              static_cast<float>(scale), dtype, ws.data_ptr(), ws_bytes,
+                              current_stream()),
                "lora_linear");
-  return y;
+  return np == n ? y : y.narrow(1, 0, n).contiguous();
 }
 
 // x [M, K]; w_codes int8 [N, K] (nn.Linear layout, blocks of 64 along K);

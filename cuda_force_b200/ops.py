@@ -11,8 +11,10 @@ three differences that are deliberate:
   or autograd is needed. Here every call runs the sm_100a kernels through
   ``torch.ops.cudaforge``; a CPU tensor, a missing extension or a
   grad-requiring input raises instead of silently changing implementation;
-* bfloat16 and float16 reach the kernels (the reference gates its CUDA path on
-  float32, ops.py:329 and :457);
+* bfloat16 and float16 reach the kernels as well as float32 (the reference
+  gates its CUDA path on float32, ops.py:329 and :457); float32 linears run
+  on the tensor cores as three tf32 products (hi*hi + hi*lo + lo*hi), which
+  keeps fp32 accuracy;
 * ``lora_linear`` accepts ``weight``/``lora_a``/``lora_b`` either contiguous in
   the reference's layout or as the transpose of a contiguous tensor (the
   nn.Linear / ``training/lora.py`` storage), without copying.
@@ -51,10 +53,11 @@ _EXTENSION_LOADED, _LOAD_MESSAGE = _load_extension()
 #: True when the extension is loaded and a CUDA device is visible.
 CUDA_KERNELS_AVAILABLE: bool = _EXTENSION_LOADED and torch.cuda.is_available()
 
-#: Storage dtypes with a kernel. Quantisation accepts all three; the linears
-#: run on the tensor cores and take float16 / bfloat16.
+#: Storage dtypes with a kernel. Quantisation and lora_linear accept all
+#: three; lora_linear_int8 takes float16 / bfloat16 activations.
 KERNEL_DTYPES: frozenset[torch.dtype] = frozenset({torch.float32, torch.float16, torch.bfloat16})
-LINEAR_DTYPES: frozenset[torch.dtype] = frozenset({torch.float16, torch.bfloat16})
+LINEAR_DTYPES: frozenset[torch.dtype] = KERNEL_DTYPES
+INT8_LINEAR_DTYPES: frozenset[torch.dtype] = frozenset({torch.float16, torch.bfloat16})
 
 
 @dataclass(frozen=True)
@@ -185,7 +188,7 @@ def lora_linear(
     """LoRA-adapted linear layer: ``x @ weight + scale * (x @ lora_a) @ lora_b``.
 
     Args:
-        x: ``[..., in_features]`` (bfloat16 or float16).
+        x: ``[..., in_features]`` (float32, bfloat16 or float16).
         weight: ``[in_features, out_features]`` — contiguous, or ``W.t()`` of an
             nn.Linear weight ``W [out_features, in_features]``.
         lora_a: ``[in_features, rank]`` (or the transpose of ``[rank, in_features]``).

@@ -89,13 +89,19 @@ def test_lora_abi_validates_shapes_and_workspace():
     assert call(128, 100, 256, 16, ws) == _abi.CF_ERR_UNSUPPORTED        # k % 64 != 0
     assert call(128, 256, 250, 16, ws) == _abi.CF_ERR_UNSUPPORTED        # n % 16 != 0
     assert call(128, 256, 256, 24, ws) == _abi.CF_ERR_UNSUPPORTED        # rank not 16/32/64
-    assert call(128, 256, 256, 16, ws - 16) == _abi.CF_ERR_WORKSPACE
+    assert call(128, 256, 256, 16, 128 * 16 * 2 - 16) == _abi.CF_ERR_WORKSPACE  # P is 16-bit here
     assert call(128, 256, 256, 16, ws, None) == _abi.CF_ERR_WORKSPACE
     assert call(-1, 256, 256, 16, ws) == _abi.CF_ERR_INVALID_ARGUMENT
     assert lib.cf_lora_linear(None, f, 1, f, 0, f, 0, f, 128, 256, 256, 16, 2.0,
                               _abi.CF_DTYPE_BF16, f, ws, None) == _abi.CF_ERR_INVALID_ARGUMENT
-    assert lib.cf_lora_linear(f, f, 1, f, 0, f, 0, f, 128, 256, 256, 16, 2.0,
+    # fp32 rows must be whole 16-byte units (k, n multiples of 4) ...
+    assert lib.cf_lora_linear(f, f, 1, f, 0, f, 0, f, 128, 258, 256, 16, 2.0,
                               _abi.CF_DTYPE_F32, f, ws, None) == _abi.CF_ERR_UNSUPPORTED
+    # ... and its workspace holds P in fp32
+    assert ws >= args["m"] * args["r"] * 4
+    # int8 weights take 16-bit activations only
+    assert lib.cf_lora_linear_int8(f, f, f, f, 0, f, 0, f, 128, 256, 256, 16, 2.0,
+                                   _abi.CF_DTYPE_F32, f, ws, None) == _abi.CF_ERR_UNSUPPORTED
     misaligned = ctypes.c_void_p(0x1008)
     assert lib.cf_lora_linear(misaligned, f, 1, f, 0, f, 0, f, 128, 256, 256, 16, 2.0,
                               _abi.CF_DTYPE_BF16, f, ws, None) == _abi.CF_ERR_MISALIGNED

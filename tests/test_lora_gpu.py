@@ -266,3 +266,83 @@ def test_w8_decode_shapes(m, rank, b_t, dtype, cuda_device):
     ref = linear_ref.lora_linear_int8(x, codes.cpu(), scales.cpu(), a, b, 2.0)
     assert linear_ref.max_rel_error(y, ref) <= TIGHT
     assert _abi.load().cf_device_status() == _abi.CF_OK
+
+
+# ---------------------------------------------------------------------------
+# fp32 lora_linear (the reference's own CUDA dtype): three tf32 products on the
+# tensor cores. Checked against an fp64 CPU composition with the reference's
+# own tolerances (tests/python/test_ops.py:105-138: rtol = atol = 1e-4; the
+# CUDA kernel test, tests/cuda/test_lora.cu:107, uses 1e-3).
+# ---------------------------------------------------------------------------
+def _f64_lora(x, w, a, b, scale):
+    x, w, a, b = (t.detach().cpu().double() for t in (x, w, a, b))
+    return x @ w + scale * ((x @ a) @ b)
+
+
+@pytest.mark.parametrize(("batch", "k", "n", "rank"),
+                         [(1, 8, 4, 2), (4, 64, 32, 8), (7, 129, 65, 3), (16, 256, 256, 16)])
+def test_f32_matches_the_definition_at_the_reference_tolerance(batch, k, n, rank, cuda_device):
+    g = torch.Generator().manual_seed(batch * 1000 + k)
+    x = torch.randn(batch, k, generator=g)
+    w = torch.randn(k, n, generator=g)
+    a = torch.randn(k, rank, generator=g)
+    b = torch.randn(rank, n, generator=g)
+    y = cf.lora_linear(x.to(cuda_device), w.to(cuda_device), a.to(cuda_device), b.to(cuda_device),
+                       0.25)
+    assert y.dtype == torch.float32 and y.shape == (batch, n)
+    torch.testing.assert_close(y.cpu().double(), _f64_lora(x, w, a, b, 0.25), rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize(("m", "k", "n", "rank"), [(300, 1024, 768, 16), (1024, 4096, 1024, 64),
+                                                   (129, 512, 4100, 32)])
+@pytest.mark.parametrize("w_t", [False, True])
+@pytest.mark.parametrize("ab_t", [False, True])
+def test_f32_shapes_and_layouts(m, k, n, rank, w_t, ab_t, cuda_device):
+    g = torch.Generator().manual_seed(m + k + n + rank)
+    x = torch.randn(m, k, generator=g)
+    w = torch.randn(k, n, generator=g) * 0.05
+    a = torch.randn(k, rank, generator=g) * 0.05
+    b = torch.randn(rank, n, generator=g) * 0.05
+    dev = cuda_device
+    y = cf.lora_linear(x.to(dev), as_layout(w.to(dev), w_t), as_layout(a.to(dev), ab_t),
+                       as_layout(b.to(dev), ab_t), 2.0)
+    ref = _f64_lora(x, w, a, b, 2.0)
+    # K up to 4096: measured against the output's scale (fp32 accumulation
+    # alone moves elements by ~1e-5 of it).
+    assert (y.cpu().double() - ref).abs().max() <= 1e-4 * ref.abs().max()
+
+
+def test_f32_zero_b_reduces_to_the_frozen_layer(cuda_device):
+    # The reference's shapes and tolerance (tests/python/test_ops.py:117-126).
+    g = torch.Generator().manual_seed(11)
+    x, w = torch.randn(4, 32, generator=g), torch.randn(32, 16, generator=g)
+    a, b = torch.randn(32, 4, generator=g), torch.zeros(4, 16)
+    y = cf.lora_linear(x.to(cuda_device), w.to(cuda_device), a.to(cuda_device), b.to(cuda_device),
+                       1.0)
+    torch.testing.assert_close(y.cpu().double(), x.double() @ w.double(), rtol=1e-5, atol=1e-5)
+    # and at K = 320, against the output's scale
+    x, w = torch.randn(64, 320, generator=g), torch.randn(320, 160, generator=g)
+    a, b = torch.randn(320, 4, generator=g), torch.zeros(4, 160)
+    y = cf.lora_linear(x.to(cuda_device), w.to(cuda_device), a.to(cuda_device), b.to(cuda_device),
+                       1.0).cpu().double()
+    ref = x.double() @ w.double()
+    assert (y - ref).abs().max() <= 1e-5 * ref.abs().max()
+
+
+def test_f32_through_the_c_abi(cuda_device):
+    m, k, n, r = 256, 512, 384, 32
+    g = torch.Generator().manual_seed(12)
+    x, w = torch.randn(m, k, generator=g), torch.randn(k, n, generator=g) * 0.05
+    a, b = torch.randn(k, r, generator=g) * 0.05, torch.randn(r, n, generator=g) * 0.05
+    xd, wd, ad, bd = (t.to(cuda_device) for t in (x, w, a, b))
+    lib = _abi.load()
+    y = torch.empty(m, n, dtype=torch.float32, device=cuda_device)
+    ws_bytes = lib.cf_lora_linear_workspace_bytes(m, r)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=cuda_device)
+    s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    _abi.check(lib.cf_lora_linear(p(xd), p(wd), _abi.CF_LAYOUT_REF, p(ad), _abi.CF_LAYOUT_REF,
+                                  p(bd), _abi.CF_LAYOUT_REF, p(y), m, k, n, r, 0.5,
+                                  _abi.CF_DTYPE_F32, p(ws), ws_bytes, s), "cf_lora_linear")
+    torch.testing.assert_close(y.cpu().double(), _f64_lora(x, w, a, b, 0.5), rtol=1e-4, atol=1e-4)
+    assert lib.cf_device_status() == _abi.CF_OK
