@@ -112,15 +112,18 @@ CF_API int cf_quantize_int8_many(const cf_quant_segment *segments, int nseg, int
 /* ---- LoRA linear --------------------------------------------------------- */
 
 /* y[m, n] = sum_k x[m,k] W[k,n] + scale * sum_j (sum_k x[m,k] A[k,j]) B[j,n]
- * x: [m, k] row-major, y: [m, n] row-major, both of `dtype` (f16 or bf16),
- * fp32 accumulation. `w`, `a`, `b` are stored as described by cf_layout.
- * Requirements: k % 64 == 0, n % 16 == 0, rank in {16, 32, 64} (rank < 16 and
- * other ranks are zero-padded by the caller), all pointers 16-byte aligned.
- * Workspace: cf_lora_linear_workspace_bytes(m, rank) bytes of device memory,
- * 16-byte aligned, holding the down-projection P = scale * x A between two
- * launches. Replaces launch_lora_linear (reference
+ * x: [m, k] row-major, y: [m, n] row-major, all operands of `dtype` (f32,
+ * f16 or bf16), fp32 accumulation. f32 runs on the tensor cores as three tf32
+ * products of a hi/lo operand split (hi*hi + hi*lo + lo*hi), which keeps fp32
+ * accuracy. `w`, `a`, `b` are stored as described by cf_layout.
+ * Requirements: rows of whole 16-byte units (k and n multiples of 8 for
+ * f16/bf16, of 4 for f32; zero-pad otherwise), rank in {16, 32, 64} (smaller
+ * ranks are zero-padded by the caller), all pointers 16-byte aligned.
+ * Workspace: cf_lora_linear_workspace_bytes(m, rank) bytes of device memory
+ * (enough for every dtype), 16-byte aligned, holding the down-projection
+ * P = scale * x A between two launches. Replaces launch_lora_linear (reference
  * cuda/include/cudaforge/lora_linear.cuh:45-48) and lora_workspace_bytes
- * (cuda/src/lora_linear.cu:218-223); the reference supports f32 only. */
+ * (cuda/src/lora_linear.cu:218-223), whose kernels are f32 only. */
 CF_API size_t cf_lora_linear_workspace_bytes(int64_t m, int64_t rank);
 CF_API int cf_lora_linear(const void *x, const void *w, int w_layout, const void *a, int a_layout,
                    const void *b, int b_layout, void *y, int64_t m, int64_t k, int64_t n,
