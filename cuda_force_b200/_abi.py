@@ -68,6 +68,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_p, _p, _p, _p, _int, _p, _int, _int, ctypes.POINTER(_p), _int, _i64, _i64, _i64, _i64,
          _i64, _i64, ctypes.c_float, _int, _p, ctypes.c_size_t, _p],
     ),
+    "cf_matmul_f32": (_int, [_p, _p, _int, _p, _i64, _i64, _i64, _int, _p]),
     "cf_lora_linear_noalloc": (
         _int,
         [_p, _p, _int, _p, _int, _p, _int, _p, _i64, _i64, _i64, _i64, ctypes.c_float, _int, _p],

@@ -1438,6 +1438,7 @@ struct F32Params {
   int b_mn;         // main B stored [K, N]
   int e_mn;         // adapter B stored [rank, N]
   int ldo;          // output row stride (elements)
+  int products;     // 3: hi*hi + hi*lo + lo*hi (fp32 accuracy); 1: hi*hi (tf32)
   float out_scale;
   float *out;       // [M, ldo] fp32
   int n_tiles_n;
@@ -1582,8 +1583,10 @@ __global__ void __launch_bounds__(F32Cfg::kThreads, 1)
             const uint64_t bl = kmajor_desc(b_lo, 128, ks);
             const uint32_t first = (it == 0 && ks == 0) ? 0u : 1u;
             ptx::mma_tf32(d_tmem, ah, bh, idesc, first);
-            ptx::mma_tf32(d_tmem, ah, bl, idesc, 1u);
-            ptx::mma_tf32(d_tmem, al, bh, idesc, 1u);
+            if (p.products == 3) {
+              ptx::mma_tf32(d_tmem, ah, bl, idesc, 1u);
+              ptx::mma_tf32(d_tmem, al, bh, idesc, 1u);
+            }
           }
           ptx::mma_commit(&empty[stage]);
           if (++stage == C::kStages) {
@@ -2129,6 +2132,7 @@ int run_linear_f32(const LinearArgs &L, cudaStream_t stream) {
   d.b_mn = a_mn ? 1 : 0;
   d.e_mn = 0;
   d.ldo = r;
+  d.products = 3;
   d.out_scale = L.scale;
   d.out = static_cast<float *>(L.ws);
   d.n_tiles_n = 1;
@@ -2147,6 +2151,34 @@ int run_linear_f32(const LinearArgs &L, cudaStream_t stream) {
   p.n_tiles_n = static_cast<int>((L.n + F32Cfg::BN - 1) / F32Cfg::BN);
   p.n_tiles = m_tiles * p.n_tiles_n;
   return launch_f32(tm_x, tm_w, tm_p, tm_b, p, true, stream);
+}
+
+// c [m, n] = a [m, k] b [k, n] in fp32 (one launch of lora_f32_kernel with
+// no adapter).
+int run_matmul_f32(const float *a, const float *b, int b_layout, float *c, int64_t m, int64_t n,
+                   int64_t k, int precise, cudaStream_t stream) {
+  unsigned *err = device_error_word();
+  if (err == nullptr) return record_cuda_error(cudaGetLastError());
+  const bool b_mn = b_layout == CF_LAYOUT_REF;
+  CUtensorMap tm_a, tm_b;
+  int st = CF_OK;
+  if ((st = make_map(&tm_a, a, 4, k, m, 32, 128, true))) return st;
+  if ((st = make_f32_b_map(&tm_b, b, b_mn, k, n))) return st;
+  F32Params p{};
+  p.M = static_cast<int>(m);
+  p.N = static_cast<int>(n);
+  p.num_kb = static_cast<int>((k + F32Cfg::kBKf - 1) / F32Cfg::kBKf);
+  p.extra_kb = 0;
+  p.n_mma = F32Cfg::BN;
+  p.b_mn = b_mn ? 1 : 0;
+  p.ldo = static_cast<int>(n);
+  p.products = precise ? 3 : 1;
+  p.out_scale = 1.0f;
+  p.out = c;
+  p.n_tiles_n = static_cast<int>((n + F32Cfg::BN - 1) / F32Cfg::BN);
+  p.n_tiles = static_cast<int>((m + 127) / 128) * p.n_tiles_n;
+  p.err = err;
+  return launch_f32(tm_a, tm_b, tm_a, tm_b, p, false, stream);
 }
 
 int validate_and_run(const LinearArgs &L, cf_stream_t stream) {
@@ -2461,4 +2493,20 @@ int cf_lora_linear_int8_allgather_ce(const void *x, const int8_t *w_codes, const
     CFB_TRY_CUDA(cudaStreamWaitEvent(s, lanes->finished[d], 0));
   }
   return CF_OK;
+}
+
+int cf_matmul_f32(const float *a, const float *b, int b_layout, float *c, int64_t m, int64_t n,
+                  int64_t k, int precise, cf_stream_t stream) {
+  if (m < 0 || n < 0 || k < 0) return CF_ERR_INVALID_ARGUMENT;
+  if (m == 0 || n == 0) return CF_OK;
+  if (a == nullptr || b == nullptr || c == nullptr) return CF_ERR_INVALID_ARGUMENT;
+  if (b_layout != CF_LAYOUT_REF && b_layout != CF_LAYOUT_T) return CF_ERR_INVALID_ARGUMENT;
+  if (k == 0 || k % 4 != 0 || n % 4 != 0) return CF_ERR_UNSUPPORTED;
+  if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX) return CF_ERR_UNSUPPORTED;
+  for (const void *ptr : {static_cast<const void *>(a), static_cast<const void *>(b),
+                          static_cast<const void *>(c)}) {
+    if (!cfb::aligned_to(ptr, 16)) return CF_ERR_MISALIGNED;
+  }
+  return cfb::run_matmul_f32(a, b, b_layout, c, m, n, k, precise,
+                             reinterpret_cast<cudaStream_t>(stream));
 }

@@ -149,6 +149,44 @@ def quantize_int8_many(tensors: list[torch.Tensor]) -> list[tuple[torch.Tensor, 
     return [(flat[2 * i], flat[2 * i + 1]) for i in range(len(tensors))]
 
 
+def matmul_f32(a: torch.Tensor, b: torch.Tensor, precise: bool = True) -> torch.Tensor:
+    """``a @ b`` for float32 ``a [m, k]`` and ``b [k, n]`` on the tensor cores.
+
+    ``precise=True`` keeps fp32 accuracy with three tf32 products of a hi/lo
+    split (the reference's ``launch_matmul``, lora_linear.cuh:58-59);
+    ``precise=False`` is one tf32 product (its ``launch_matmul_tensor_core``,
+    tensor_core_matmul.cuh:40-41). ``b`` may be the transpose of a contiguous
+    ``[n, k]`` tensor. Feature counts that are not multiples of 4 are
+    zero-padded.
+    """
+    import ctypes
+
+    from cuda_force_b200 import _abi
+
+    if a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[0]:
+        raise ValueError(f"matmul_f32 needs a [m, k] and b [k, n], got {tuple(a.shape)} and "
+                         f"{tuple(b.shape)}")
+    if a.dtype != torch.float32 or b.dtype != torch.float32:
+        raise ValueError("matmul_f32 takes float32 tensors")
+    _require("matmul_f32", a, b)
+    m, k = a.shape
+    n = b.shape[1]
+    kp, np_ = -(-k // 4) * 4, -(-n // 4) * 4
+    a = a.contiguous()
+    if kp != k:
+        a = torch.nn.functional.pad(a, (0, kp - k))
+    if kp != k or np_ != n:
+        b = torch.nn.functional.pad(b, (0, np_ - n, 0, kp - k)).contiguous()
+    b = _as_stored(b)
+    layout = _abi.CF_LAYOUT_REF if b.is_contiguous() else _abi.CF_LAYOUT_T
+    c = torch.empty(m, np_, dtype=torch.float32, device=a.device)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(a.device).cuda_stream)
+    _abi.check(_abi.load().cf_matmul_f32(
+        ctypes.c_void_p(a.data_ptr()), ctypes.c_void_p(b.data_ptr()), layout,
+        ctypes.c_void_p(c.data_ptr()), m, np_, kp, 1 if precise else 0, stream), "cf_matmul_f32")
+    return c if np_ == n else c[:, :n].contiguous()
+
+
 def quantization_error(x: torch.Tensor) -> torch.Tensor:
     """Maximum absolute round-trip error of int8 quantisation (<= scale / 2 per block)."""
     quantised, scales = quantize_int8(x)

@@ -130,6 +130,17 @@ CF_API int cf_lora_linear(const void *x, const void *w, int w_layout, const void
                    int64_t rank, float scale, int dtype, void *workspace,
                    size_t workspace_bytes, cf_stream_t stream);
 
+/* c[m, n] = a[m, k] b[k, n] in fp32 on the tensor cores, a and c row-major,
+ * b stored as cf_layout says. precise != 0: three tf32 products of a hi/lo
+ * split, fp32 accuracy (replaces launch_matmul, reference
+ * cuda/include/cudaforge/lora_linear.cuh:58-59, CUDA-core FMA); precise == 0:
+ * one tf32 product (replaces launch_matmul_tensor_core,
+ * cuda/include/cudaforge/tensor_core_matmul.cuh:40-41, TF32 WMMA, whose shape
+ * restrictions do not apply here). Requirements: k and n multiples of 4,
+ * pointers 16-byte aligned. */
+CF_API int cf_matmul_f32(const float *a, const float *b, int b_layout, float *c, int64_t m,
+                         int64_t n, int64_t k, int precise, cf_stream_t stream);
+
 /* Same product with W given as block-INT8: w_codes int8[n, k] (the output of
  * cf_quantize_int8 on an nn.Linear weight [out, in]) and w_scales
  * float[n * k / 64]. Semantics: lora_linear(x, dequantize(w_codes, w_scales)^T,

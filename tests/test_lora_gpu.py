@@ -346,3 +346,18 @@ def test_f32_through_the_c_abi(cuda_device):
                                   _abi.CF_DTYPE_F32, p(ws), ws_bytes, s), "cf_lora_linear")
     torch.testing.assert_close(y.cpu().double(), _f64_lora(x, w, a, b, 0.5), rtol=1e-4, atol=1e-4)
     assert lib.cf_device_status() == _abi.CF_OK
+
+
+@pytest.mark.parametrize(("m", "k", "n"), [(7, 129, 65), (256, 1024, 512), (1000, 2048, 3000)])
+@pytest.mark.parametrize("b_t", [False, True])
+def test_matmul_f32(m, k, n, b_t, cuda_device):
+    g = torch.Generator().manual_seed(m + k + n)
+    a, b = torch.randn(m, k, generator=g), torch.randn(k, n, generator=g)
+    ref = a.double() @ b.double()
+    bd = as_layout(b.to(cuda_device), b_t)
+    precise = cf.matmul_f32(a.to(cuda_device), bd).cpu().double()
+    assert (precise - ref).abs().max() <= 2e-5 * ref.abs().max()
+    tf32 = cf.matmul_f32(a.to(cuda_device), bd, precise=False).cpu().double()
+    # one tf32 product: operands rounded to 10 explicit mantissa bits
+    assert (tf32 - ref).abs().max() <= 5e-3 * ref.abs().max()
+    assert (tf32 - ref).abs().max() > (precise - ref).abs().max()
