@@ -13,6 +13,7 @@ from cuda_force_b200.ops import (
     kernel_supports,
     lora_linear,
     lora_linear_int8,
+    lora_merge_quantize_int8,
     matmul_f32,
     quantization_error,
     quantize_dequantize,
@@ -32,6 +33,7 @@ __all__ = [
     "kernel_supports",
     "lora_linear",
     "lora_linear_int8",
+    "lora_merge_quantize_int8",
     "matmul_f32",
     "quantization_error",
     "quantize_dequantize",

@@ -26,7 +26,7 @@ LIB = PKG / "libcudaforge_b200.so"
 SHIM = PKG / "_C.so"
 
 CUDA_SOURCES = ["abi.cu", "quant.cu", "lora_gemm.cu"]
-HEADERS = ["cf_common.cuh", "ptx.cuh"]
+HEADERS = ["quant_math.cuh", "cf_common.cuh", "ptx.cuh"]
 
 NVCC_FLAGS = [
     "-O3",

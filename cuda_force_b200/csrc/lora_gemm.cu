@@ -40,6 +40,7 @@
 
 #include "cf_common.cuh"
 #include "ptx.cuh"
+#include "quant_math.cuh"
 
 namespace cfb {
 namespace {
@@ -1743,6 +1744,294 @@ __global__ void __launch_bounds__(F32Cfg::kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// LoRA merge + block-INT8 quantisation in one pass:
+//   codes, scales = quantize_int8(W + scaling * (lora_b @ lora_a))
+// with the module's layouts (training/lora.py:95-102: W [out, in], lora_a
+// [rank, in], lora_b [out, rank]) and 16-bit W, lora_a, lora_b.
+//
+// The rank-r product is a tcgen05 MMA per 128-row x 256-column tile of W
+// (A operand = lora_b rows, K-major; B operand = lora_a, MN-major in 64-column
+// chunks; K = rank), accumulated in TMEM. The epilogue thread owns one row of
+// W, so each 64-element quantisation block is 64 consecutive accumulator
+// columns of one thread: it rounds like the module's dtype does (the product
+// to the dtype, times scaling to the dtype, plus W to the dtype), takes the
+// block absmax with no cross-thread reduction, and writes the codes and the
+// scale with the quantiser's exact arithmetic. The W tile arrives by TMA in
+// the same stage (128B-swizzled 64-column boxes, so a warp's row reads spread
+// over the banks); a stage is released once the MMA and every epilogue warp
+// are done with it. W is read once and the merged weight never reaches memory.
+//   warp 0 TMA producer, warp 1 TMEM owner + MMA issuer, warps 4-19 epilogue.
+// ---------------------------------------------------------------------------
+struct MergeCfg {
+  static constexpr int BK = 256;                         // columns of W per tile
+  static constexpr int kBBytes = kBM * 64 * 2;            // lora_b rows, rank <= 64
+  static constexpr int kABytes = 64 * BK * 2;             // lora_a columns, rank <= 64
+  static constexpr int kWBytes = kBM * BK * 2;            // W tile: 4 boxes of 128 x 64
+  static constexpr int kStageBytes = kBBytes + kABytes + kWBytes;  // 112 KB
+  // Two stages fill shared memory, which also keeps one CTA per SM: the two
+  // 256-column accumulators take all of an SM's TMEM.
+  static constexpr int kStages = 2;
+  // Sixteen epilogue warps (warps 4-19), four per TMEM lane quarter, each
+  // taking one of a tile's four 64-column blocks: the per-element merge and
+  // quantise work needs several warps per scheduler to hide its latency.
+  static constexpr int kEpiWarps = 16;
+  static constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * kWarp;
+  static constexpr int kTmemCols = 2 * BK;
+  static constexpr size_t kSmemBytes = 1024 + static_cast<size_t>(kStages) * kStageBytes + 256;
+};
+
+struct MergeParams {
+  int N, K;              // W is [N, K]
+  int rank;
+  float scaling;
+  const uint16_t *w;
+  int8_t *codes;         // [N, K]
+  float *scales;         // [N, K / 64]
+  int n_tiles_k;
+  int n_tiles;
+  unsigned *err;
+};
+
+// Two floats rounded to the 16-bit storage type and back (one packed
+// conversion for the pair).
+template <bool kBf16>
+__device__ __forceinline__ void round_pair(float &lo, float &hi) {
+  if constexpr (kBf16) {
+    const uint32_t h = ptx::pack_bf16x2(lo, hi);
+    lo = __uint_as_float(h << 16);
+    hi = __uint_as_float(h & 0xffff0000u);
+  } else {
+    const float2 f = __half22float2(__halves2half2(__float2half_rn(lo), __float2half_rn(hi)));
+    lo = f.x;
+    hi = f.y;
+  }
+}
+
+// The two 16-bit values of a word as floats.
+template <bool kBf16>
+__device__ __forceinline__ void unpack_pair(uint32_t w, float &lo, float &hi) {
+  if constexpr (kBf16) {
+    lo = __uint_as_float(w << 16);
+    hi = __uint_as_float(w & 0xffff0000u);
+  } else {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w));
+    lo = f.x;
+    hi = f.y;
+  }
+}
+
+template <bool kBf16>
+__global__ void __launch_bounds__(MergeCfg::kThreads, 1)
+    lora_merge_quant_kernel(const __grid_constant__ CUtensorMap tm_b,
+                            const __grid_constant__ CUtensorMap tm_a,
+                            const __grid_constant__ CUtensorMap tm_w, const MergeParams p) {
+  using C = MergeCfg;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kStages * C::kStageBytes);
+  uint64_t *full = bars;
+  uint64_t *empty = bars + C::kStages;
+  uint64_t *tmem_full = bars + 2 * C::kStages;
+  uint64_t *tmem_empty = tmem_full + 2;
+  uint64_t *drain = tmem_empty + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  int *abort_flag = reinterpret_cast<int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / kWarp;
+  const int lane = threadIdx.x % kWarp;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      ptx::mbar_init(&full[s], 1);
+      ptx::mbar_init(&empty[s], 1 + C::kEpiWarps);  // MMA commit + epilogue warps
+    }
+    for (int a = 0; a < 2; ++a) {
+      ptx::mbar_init(&tmem_full[a], 1);
+      ptx::mbar_init(&tmem_empty[a], C::kEpiWarps);
+    }
+    ptx::mbar_init(drain, 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, C::kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t outstanding = 0, issue_parity = 0;
+      for (int tile = blockIdx.x; tile < p.n_tiles && !aborted(abort_flag); tile += gridDim.x) {
+        const int n0 = (tile / p.n_tiles_k) * kBM;
+        const int k0 = (tile % p.n_tiles_k) * C::BK;
+        if (!ptx::mbar_wait(&empty[stage], phase ^ 1)) {
+          record_timeout(p.err, abort_flag);
+          break;
+        }
+        uint8_t *sb = smem + stage * C::kStageBytes;
+        uint8_t *sa = sb + C::kBBytes;
+        uint8_t *sw = sa + C::kABytes;
+        ptx::mbar_expect_tx(&full[stage], (kBM + C::BK) * p.rank * 2 + C::kWBytes);
+        ptx::tma_load_2d(sb, &tm_b, &full[stage], 0, n0);
+        for (int c = 0; c < C::BK / 64; ++c) {
+          ptx::tma_load_2d(sa + c * (p.rank * 128), &tm_a, &full[stage], k0 + c * 64, 0);
+          ptx::tma_load_2d(sw + c * (kBM * 128), &tm_w, &full[stage], k0 + c * 64, n0);
+        }
+        outstanding |= 1u << stage;
+        issue_parity = (issue_parity & ~(1u << stage)) | (phase << stage);
+        if (++stage == C::kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (aborted(abort_flag)) {
+        for (int s = 0; s < C::kStages; ++s) {
+          if (outstanding & (1u << s)) ptx::mbar_wait(&full[s], (issue_parity >> s) & 1u, 200000000ull);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = ptx::make_idesc_f16(kBf16, kBM, C::BK, false, true);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (int tile = blockIdx.x; tile < p.n_tiles && !aborted(abort_flag);
+           tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
+        if (!ptx::mbar_wait(&tmem_empty[acc], acc_phase ^ 1) ||
+            !ptx::mbar_wait(&full[stage], phase)) {
+          record_timeout(p.err, abort_flag);
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t sb = ptx::smem_addr(smem + stage * C::kStageBytes);
+        const uint32_t sa = sb + C::kBBytes;
+        for (int ks = 0; ks < p.rank / kUmmaK; ++ks) {
+          ptx::mma_f16(tmem_base + acc * C::BK, kmajor_desc(sb, p.rank * 2, ks),
+                       mnmajor_desc(sa, 128, p.rank * 128, ks), idesc, ks > 0 ? 1u : 0u);
+        }
+        ptx::mma_commit(&empty[stage]);
+        ptx::mma_commit(&tmem_full[acc]);
+        if (++stage == C::kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (aborted(abort_flag)) {
+        ptx::mma_commit(drain);
+        ptx::mbar_wait(drain, 0, 200000000ull);
+      }
+    }
+  } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + C::kEpiWarps) {
+    // ------------------------------------------------------------------ epilogue
+    const int quarter = warp % 4;
+    const int blk = (warp - kEpiWarp0) / 4;  // this warp's 64-column block of every tile
+    int local = 0;
+    for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
+      const bool ok = ptx::warp_wait(&tmem_full[acc], acc_phase);
+      if (__any_sync(0xffffffffu, !ok)) {
+        if (lane == 0) record_timeout(p.err, abort_flag);
+        break;
+      }
+      ptx::tc_fence_after();
+      const int row = quarter * 32 + lane;
+      const int n = (tile / p.n_tiles_k) * kBM + row;
+      const int kb = (tile % p.n_tiles_k) * C::BK + blk * 64;
+      const int stage = local % C::kStages;  // one stage per tile
+      const uint8_t *wrow = smem + stage * C::kStageBytes + C::kBBytes + C::kABytes +
+                            blk * (kBM * 128) + row * 128;
+      const uint32_t t_col = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                             acc * C::BK + blk * 64;
+      if (kb < p.K) {  // warp-uniform
+        // Merged values, rounded to the storage type, kept packed two per word.
+        uint32_t mw[32];
+        unsigned amax = 0;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t v[32];
+          ptx::tmem_ld_32x32b_x32(t_col + half * 32, v);
+          ptx::tmem_ld_wait();
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int chunk = half * 4 + q;  // 16-byte chunk of the 128-byte row
+            const uint4 wv = *reinterpret_cast<const uint4 *>(wrow + ((chunk ^ (row & 7)) << 4));
+            const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+              const int e = q * 8 + 2 * h;  // within this half
+              // As the module computes it in its dtype: the product rounded,
+              // scaled and rounded, added to W and rounded.
+              float p0 = __uint_as_float(v[e]), p1 = __uint_as_float(v[e + 1]);
+              round_pair<kBf16>(p0, p1);
+              float u0 = p0 * p.scaling, u1 = p1 * p.scaling;
+              round_pair<kBf16>(u0, u1);
+              float w0, w1;
+              unpack_pair<kBf16>(ww[h], w0, w1);
+              const float m0 = w0 + u0, m1 = w1 + u1;
+              const uint32_t packed = kBf16 ? ptx::pack_bf16x2(m0, m1) : ptx::pack_f16x2(m0, m1);
+              mw[half * 16 + q * 4 + h] = packed;
+              float r0, r1;
+              unpack_pair<kBf16>(packed, r0, r1);
+              amax = max(amax, max(__float_as_uint(r0) & 0x7fffffffu,
+                                   __float_as_uint(r1) & 0x7fffffffu));
+            }
+          }
+        }
+        if (n < p.N) {
+          const float s = block_scale(amax);
+          const bool fast = quotient_path_ok(amax, s);
+          const float r = __frcp_rn(s);
+          uint4 *dst = reinterpret_cast<uint4 *>(p.codes + static_cast<int64_t>(n) * p.K + kb);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint32_t words[4];
+#pragma unroll
+            for (int w4 = 0; w4 < 4; ++w4) {
+              float x0, x1, x2, x3;
+              unpack_pair<kBf16>(mw[q * 8 + 2 * w4], x0, x1);
+              unpack_pair<kBf16>(mw[q * 8 + 2 * w4 + 1], x2, x3);
+              const float xs[4] = {x0, x1, x2, x3};
+              uint32_t word = 0;
+#pragma unroll
+              for (int b4 = 0; b4 < 4; ++b4) {
+                const uint32_t cb = fast ? code_bits_fast(xs[b4], s, r) : code_bits_exact(xs[b4], s);
+                word |= (cb & 0xffu) << (8 * b4);
+              }
+              words[w4] = word;
+            }
+            dst[q] = make_uint4(words[0], words[1], words[2], words[3]);
+          }
+          p.scales[static_cast<int64_t>(n) * (p.K / 64) + kb / 64] = s;
+        }
+      }
+      ptx::tc_fence_before();
+      ptx::warp_arrive(&tmem_empty[acc]);
+      ptx::warp_arrive(&empty[stage]);  // this warp's W reads are done
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side: tensor maps and launches.
 // ---------------------------------------------------------------------------
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
@@ -2181,6 +2470,38 @@ int run_matmul_f32(const float *a, const float *b, int b_layout, float *c, int64
   return launch_f32(tm_a, tm_b, tm_a, tm_b, p, false, stream);
 }
 
+template <bool kBf16>
+int run_merge_quantize(const void *w, const void *lora_a, const void *lora_b, int64_t n,
+                       int64_t k, int64_t r, float scaling, int8_t *codes, float *scales,
+                       cudaStream_t stream) {
+  unsigned *err = device_error_word();
+  if (err == nullptr) return record_cuda_error(cudaGetLastError());
+  CUtensorMap tm_b, tm_a;
+  int st = CF_OK;
+  // lora_b [n, r]: K-major rows of r elements; lora_a [r, k]: 64-column chunks;
+  // W [n, k]: 64-column boxes of 128 rows.
+  CUtensorMap tm_w;
+  if ((st = make_map(&tm_b, lora_b, 2, r, n, r, kBM, true))) return st;
+  if ((st = make_map(&tm_a, lora_a, 2, k, r, 64, r, true))) return st;
+  if ((st = make_map(&tm_w, w, 2, k, n, 64, kBM, true))) return st;
+  MergeParams p{};
+  p.N = static_cast<int>(n);
+  p.K = static_cast<int>(k);
+  p.rank = static_cast<int>(r);
+  p.scaling = scaling;
+  p.w = static_cast<const uint16_t *>(w);
+  p.codes = codes;
+  p.scales = scales;
+  p.n_tiles_k = static_cast<int>((k + MergeCfg::BK - 1) / MergeCfg::BK);
+  p.n_tiles = p.n_tiles_k * static_cast<int>((n + kBM - 1) / kBM);
+  p.err = err;
+  if ((st = allow_dynamic_smem<lora_merge_quant_kernel<kBf16>>(MergeCfg::kSmemBytes))) return st;
+  const int grid = std::max(1, std::min(p.n_tiles, sm_count()));
+  lora_merge_quant_kernel<kBf16><<<grid, MergeCfg::kThreads, MergeCfg::kSmemBytes, stream>>>(
+      tm_b, tm_a, tm_w, p);
+  return check_launch();
+}
+
 int validate_and_run(const LinearArgs &L, cf_stream_t stream) {
   if (L.m < 0 || L.k < 0 || L.n < 0 || L.r < 0) return CF_ERR_INVALID_ARGUMENT;
   if (L.m == 0 || L.n == 0) return CF_OK;
@@ -2509,4 +2830,28 @@ int cf_matmul_f32(const float *a, const float *b, int b_layout, float *c, int64_
   }
   return cfb::run_matmul_f32(a, b, b_layout, c, m, n, k, precise,
                              reinterpret_cast<cudaStream_t>(stream));
+}
+
+int cf_lora_merge_quantize_int8(const void *w, const void *lora_a, const void *lora_b,
+                                int64_t n, int64_t k, int64_t rank, float scaling, int dtype,
+                                int8_t *codes, float *scales, cf_stream_t stream) {
+  if (n < 0 || k < 0 || rank < 0) return CF_ERR_INVALID_ARGUMENT;
+  if (n == 0 || k == 0) return CF_OK;
+  if (w == nullptr || lora_a == nullptr || lora_b == nullptr || codes == nullptr ||
+      scales == nullptr) {
+    return CF_ERR_INVALID_ARGUMENT;
+  }
+  if (dtype != CF_DTYPE_BF16 && dtype != CF_DTYPE_F16) return CF_ERR_UNSUPPORTED;
+  if (rank != 16 && rank != 32 && rank != 64) return CF_ERR_UNSUPPORTED;
+  if (k % cfb::kQuantBlockSize != 0 || n > INT32_MAX || k > INT32_MAX) return CF_ERR_UNSUPPORTED;
+  for (const void *ptr : {w, lora_a, lora_b, static_cast<const void *>(codes)}) {
+    if (!cfb::aligned_to(ptr, 16)) return CF_ERR_MISALIGNED;
+  }
+  if (!cfb::aligned_to(scales, 4)) return CF_ERR_MISALIGNED;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  return dtype == CF_DTYPE_BF16
+             ? cfb::run_merge_quantize<true>(w, lora_a, lora_b, n, k, rank, scaling, codes,
+                                             scales, s)
+             : cfb::run_merge_quantize<false>(w, lora_a, lora_b, n, k, rank, scaling, codes,
+                                              scales, s);
 }

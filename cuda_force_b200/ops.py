@@ -187,6 +187,59 @@ def matmul_f32(a: torch.Tensor, b: torch.Tensor, precise: bool = True) -> torch.
     return c if np_ == n else c[:, :n].contiguous()
 
 
+def lora_merge_quantize_int8(
+    weight: torch.Tensor, lora_a: torch.Tensor, lora_b: torch.Tensor, scaling: float
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """``quantize_int8(weight + scaling * (lora_b @ lora_a))`` in one pass.
+
+    The deployment step after LoRA training (training/lora.py:95-111: merge,
+    then quantise the merged weight for a W8 linear) without materialising the
+    merged weight. Module layouts: ``weight [out, in]``, ``lora_a [rank, in]``,
+    ``lora_b [out, rank]``, all float16 or bfloat16; ``in`` a multiple of 64.
+    Each merged value is rounded as the module computes it in its dtype.
+    Returns ``(codes [out, in] int8, scales [out * in / 64] float32)``.
+    """
+    import ctypes
+
+    from cuda_force_b200 import _abi
+
+    if weight.dim() != 2:
+        raise ValueError(f"weight must be [out_features, in_features], got {tuple(weight.shape)}")
+    out_features, in_features = weight.shape
+    if lora_a.dim() != 2 or lora_a.shape[1] != in_features:
+        raise ValueError(f"lora_a must be [rank, in_features={in_features}], got "
+                         f"{tuple(lora_a.shape)}")
+    rank = lora_a.shape[0]
+    if lora_b.dim() != 2 or tuple(lora_b.shape) != (out_features, rank):
+        raise ValueError(f"lora_b must be [out_features, rank] = [{out_features}, {rank}], got "
+                         f"{tuple(lora_b.shape)}")
+    if weight.dtype not in (torch.float16, torch.bfloat16) or lora_a.dtype != weight.dtype \
+            or lora_b.dtype != weight.dtype:
+        raise ValueError("lora_merge_quantize_int8 takes float16 or bfloat16 tensors of one dtype")
+    if in_features % QUANT_BLOCK_SIZE:
+        raise ValueError(f"in_features must be a multiple of {QUANT_BLOCK_SIZE}, got {in_features}")
+    if not 1 <= rank <= 64:
+        raise ValueError(f"rank must be between 1 and 64, got {rank}")
+    _require("lora_merge_quantize_int8", weight, lora_a, lora_b)
+    padded = 16 if rank <= 16 else 32 if rank <= 32 else 64
+    a = lora_a.contiguous()
+    b = lora_b.contiguous()
+    if padded != rank:
+        a = torch.nn.functional.pad(a, (0, 0, 0, padded - rank))
+        b = torch.nn.functional.pad(b, (0, padded - rank))
+    w = weight.contiguous()
+    codes = torch.empty(out_features, in_features, dtype=torch.int8, device=w.device)
+    scales = torch.empty(out_features * in_features // QUANT_BLOCK_SIZE, dtype=torch.float32,
+                         device=w.device)
+    dtype = _abi.CF_DTYPE_BF16 if w.dtype == torch.bfloat16 else _abi.CF_DTYPE_F16
+    p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    stream = ctypes.c_void_p(torch.cuda.current_stream(w.device).cuda_stream)
+    _abi.check(_abi.load().cf_lora_merge_quantize_int8(
+        p(w), p(a), p(b), out_features, in_features, padded, float(scaling), dtype, p(codes),
+        p(scales), stream), "cf_lora_merge_quantize_int8")
+    return codes, scales
+
+
 def quantization_error(x: torch.Tensor) -> torch.Tensor:
     """Maximum absolute round-trip error of int8 quantisation (<= scale / 2 per block)."""
     quantised, scales = quantize_int8(x)

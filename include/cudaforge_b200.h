@@ -200,6 +200,23 @@ CF_API int cf_lora_linear_int8_allgather_ce(const void *x, const int8_t *w_codes
                                             void *workspace, size_t workspace_bytes,
                                             cf_stream_t stream);
 
+/* LoRA merge + block-INT8 quantisation in one pass:
+ *   codes, scales = quantize_int8(w + scaling * (lora_b @ lora_a))
+ * with the module layouts of training/lora.py:95-102 (w [n, k] = [out, in],
+ * lora_a [rank, k], lora_b [n, rank]), all contiguous and of `dtype` (f16 or
+ * bf16). The merged value is rounded as the module computes it in its dtype
+ * (product, times scaling, plus w, each rounded to the dtype) and quantised
+ * with the reference's arithmetic; the merged weight itself is never stored.
+ * codes int8 [n, k], scales float [n * k / 64]. Requirements: k % 64 == 0,
+ * rank in {16, 32, 64} (smaller ranks zero-padded by the caller), pointers
+ * 16-byte aligned (scales 4). No counterpart launcher in the reference: it
+ * replaces merged_weight() followed by quantize_int8 (training/lora.py:95-111,
+ * cpp/src/bindings.cpp:198-209). */
+CF_API int cf_lora_merge_quantize_int8(const void *w, const void *lora_a, const void *lora_b,
+                                       int64_t n, int64_t k, int64_t rank, float scaling,
+                                       int dtype, int8_t *codes, float *scales,
+                                       cf_stream_t stream);
+
 /* Allocation-free form of cf_lora_linear, for callers that cannot allocate the
  * workspace: hosts whose device memory is reserved up front by another
  * allocator, foreign-language hosts without a CUDA allocator, and loops that
