@@ -1046,22 +1046,17 @@ __global__ void __launch_bounds__(DecCfg<BT>::kThreads, DecCfg<BT>::kMinBlocks)
 // ring stays 5 stages deep. The adapter runs as rank/16 extra iterations of
 // one K = 16 step each (A = 16 columns of B^T, B = 16 columns of P).
 // ---------------------------------------------------------------------------
-// kHalves = 2: 512-token tiles, one 512-column accumulator (least conversion
-// per FLOP). kHalves = 1: 256-token tiles with two 256-column accumulators, so
-// a tile's epilogue (and its stores to peer GPUs) overlaps the next tile's
-// main loop; used when a call writes to many destinations.
-template <bool kTmaStore, int kHalves = 2>
+template <bool kTmaStore>
 struct W8WideCfg {
-  static constexpr int BT = 256 * kHalves;
-  static constexpr int kAccs = kHalves == 1 ? 2 : 1;   // TMEM accumulators
+  static constexpr int BT = 512;
   static constexpr int kBKw = 32;                      // k-block width (elements)
   static constexpr int kRowBytes = kBKw * 2;           // 64 -> 64-byte swizzle
   static constexpr int kABytes = kBM * kRowBytes;      // 8 KB
   static constexpr int kXHalf = 256 * kRowBytes;       // 16 KB
-  static constexpr int kXBytes = kHalves * kXHalf;     // 16 or 32 KB
+  static constexpr int kXBytes = 2 * kXHalf;           // 32 KB
   static constexpr int kRawBytes = kBM * kBKw;         // 4 KB
-  static constexpr int kStageBytes = kABytes + kXBytes + kRawBytes;  // 28 or 44 KB
-  static constexpr int kStages = kHalves == 1 ? 7 : (kTmaStore ? 4 : 5);
+  static constexpr int kStageBytes = kABytes + kXBytes + kRawBytes;  // 44 KB
+  static constexpr int kStages = kTmaStore ? 4 : 5;
   static constexpr int kSlabBytes = 32 * kBM * 2;      // 32 tokens x 128 features, 8 KB
   static constexpr int kStagingBytes = kTmaStore ? 2 * kSlabBytes : 0;
   static constexpr int kThreads = 512;
@@ -1077,14 +1072,14 @@ struct OutMaps {
   CUtensorMap map[kMaxOuts];
 };
 
-template <bool kBf16, bool kTmaStore, int kHalves>
-__global__ void __launch_bounds__(W8WideCfg<kTmaStore, kHalves>::kThreads, 1)
+template <bool kBf16, bool kTmaStore>
+__global__ void __launch_bounds__(W8WideCfg<kTmaStore>::kThreads, 1)
     w8_wide_kernel(const __grid_constant__ CUtensorMap tm_x,
                    const __grid_constant__ CUtensorMap tm_codes,
                    const __grid_constant__ CUtensorMap tm_p,
                    const __grid_constant__ CUtensorMap tm_bt,
                    const __grid_constant__ OutMaps out_maps, const W8Params p) {
-  using C = W8WideCfg<kTmaStore, kHalves>;
+  using C = W8WideCfg<kTmaStore>;
   constexpr int BT = C::BT;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
@@ -1094,9 +1089,9 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore, kHalves>::kThreads, 1)
   uint64_t *full = bars;
   uint64_t *empty = bars + C::kStages;
   uint64_t *conv_full = bars + 2 * C::kStages;
-  uint64_t *tmem_full = bars + 3 * C::kStages;   // [kAccs]
-  uint64_t *tmem_empty = tmem_full + C::kAccs;   // [kAccs]
-  uint64_t *drain = tmem_empty + C::kAccs;
+  uint64_t *tmem_full = bars + 3 * C::kStages;
+  uint64_t *tmem_empty = tmem_full + 1;
+  uint64_t *drain = tmem_empty + 1;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
   int *abort_flag = reinterpret_cast<int *>(tmem_slot + 1);
 
@@ -1111,10 +1106,8 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore, kHalves>::kThreads, 1)
       ptx::mbar_init(&empty[s], 1);
       ptx::mbar_init(&conv_full[s], kConvThreads / kWarp);
     }
-    for (int a = 0; a < C::kAccs; ++a) {
-      ptx::mbar_init(&tmem_full[a], 1);
-      ptx::mbar_init(&tmem_empty[a], 4);
-    }
+    ptx::mbar_init(tmem_full, 1);
+    ptx::mbar_init(tmem_empty, 4);
     ptx::mbar_init(drain, 1);
     *abort_flag = 0;
     ptx::fence_mbar_init();
@@ -1148,9 +1141,8 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore, kHalves>::kThreads, 1)
           if (it < p.num_kb) {
             const int k0 = it * C::kBKw;
             ptx::mbar_expect_tx(&full[stage], C::kXBytes + C::kRawBytes);
-            for (int h = 0; h < kHalves; ++h) {
-              ptx::tma_load_2d(sx + h * C::kXHalf, &tm_x, &full[stage], k0, t0 + h * 256);
-            }
+            ptx::tma_load_2d(sx, &tm_x, &full[stage], k0, t0);
+            ptx::tma_load_2d(sx + C::kXHalf, &tm_x, &full[stage], k0, t0 + 256);
             ptx::tma_load_2d(sx + C::kXBytes, &tm_codes, &full[stage], k0, w0);
           } else {
             if (!dep_ready) {  // P comes from the down-projection launched just before
@@ -1166,9 +1158,8 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore, kHalves>::kThreads, 1)
             } else {
               ptx::tma_load_2d(sa, &tm_bt, &full[stage], j0, w0);
             }
-            for (int h = 0; h < kHalves; ++h) {
-              ptx::tma_load_2d(sx + h * C::kXHalf, &tm_p, &full[stage], j0, t0 + h * 256);
-            }
+            ptx::tma_load_2d(sx, &tm_p, &full[stage], j0, t0);
+            ptx::tma_load_2d(sx + C::kXHalf, &tm_p, &full[stage], j0, t0 + 256);
           }
           outstanding |= 1u << stage;
           issue_parity = (issue_parity & ~(1u << stage)) | (phase << stage);
@@ -1195,14 +1186,11 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore, kHalves>::kThreads, 1)
       int local = 0;
       for (int tile = blockIdx.x; tile < p.n_tiles && !aborted(abort_flag);
            tile += gridDim.x, ++local) {
-        const int acc = local % C::kAccs;
-        const uint32_t acc_phase = static_cast<uint32_t>((local / C::kAccs) & 1);
-        if (!ptx::mbar_wait(&tmem_empty[acc], acc_phase ^ 1u)) {
+        if (!ptx::mbar_wait(tmem_empty, static_cast<uint32_t>(local & 1) ^ 1u)) {
           record_timeout(p.err, abort_flag);
           break;
         }
         ptx::tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BT;
         bool ok = true;
         for (int it = 0; it < num_iters; ++it) {
           const bool main_kb = it < p.num_kb;
@@ -1219,8 +1207,8 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore, kHalves>::kThreads, 1)
           if (main_kb) {
             for (int ks = 0; ks < C::kBKw / kUmmaK; ++ks) {
               const uint64_t adesc = kmajor_desc(sa, C::kRowBytes, ks);
-              for (int h = 0; h < kHalves; ++h) {
-                ptx::mma_f16(d_tmem + h * 256, adesc,
+              for (int h = 0; h < 2; ++h) {
+                ptx::mma_f16(tmem_base + h * 256, adesc,
                              kmajor_desc(sx + h * C::kXHalf, C::kRowBytes, ks), idesc_main,
                              (it > 0 || ks > 0) ? 1u : 0u);
               }
@@ -1228,8 +1216,8 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore, kHalves>::kThreads, 1)
           } else {
             const uint64_t adesc = p.extra_b_mn ? mnmajor_desc(sa, 128, kUmmaK * 128, 0)
                                                 : kmajor_desc(sa, kUmmaK * 2, 0);
-            for (int h = 0; h < kHalves; ++h) {
-              ptx::mma_f16(d_tmem + h * 256, adesc,
+            for (int h = 0; h < 2; ++h) {
+              ptx::mma_f16(tmem_base + h * 256, adesc,
                            kmajor_desc(sx + h * C::kXHalf, kUmmaK * 2, 0), idesc_extra,
                            it > 0 ? 1u : 0u);
             }
@@ -1241,7 +1229,7 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore, kHalves>::kThreads, 1)
           }
         }
         if (!ok) break;
-        ptx::mma_commit(&tmem_full[acc]);
+        ptx::mma_commit(tmem_full);
       }
       if (aborted(abort_flag)) {
         ptx::mma_commit(drain);
@@ -1257,15 +1245,13 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore, kHalves>::kThreads, 1)
     for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x, ++local) {
       const int w0 = (tile % p.n_tiles_w) * kBM;
       const int t0 = (tile / p.n_tiles_w) * BT;
-      const int acc = local % C::kAccs;
-      const bool ok =
-          ptx::warp_wait(&tmem_full[acc], static_cast<uint32_t>((local / C::kAccs) & 1));
+      const bool ok = ptx::warp_wait(tmem_full, static_cast<uint32_t>(local & 1));
       if (!ok) {
         if (lane == 0) record_timeout(p.err, abort_flag);
         break;
       }
       ptx::tc_fence_after();
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BT;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
       const int n = w0 + row;
       uint16_t *out = static_cast<uint16_t *>(p.outs[0]);
 #pragma unroll 1
@@ -1312,7 +1298,7 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore, kHalves>::kThreads, 1)
         }
       }
       ptx::tc_fence_before();
-      ptx::warp_arrive(&tmem_empty[acc]);
+      ptx::warp_arrive(tmem_empty);
       if constexpr (kTmaStore) {
         if (p.done != nullptr && threadIdx.x == kEpiWarp0 * kWarp) {
           // Publish the tile: its stores have completed (not just read
@@ -2265,9 +2251,9 @@ int launch_w8_decode(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
   return check_launch();
 }
 
-template <bool kBf16, bool kTmaStore, int kHalves = 2>
+template <bool kBf16, bool kTmaStore>
 int launch_w8_wide(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
-  using C = W8WideCfg<kTmaStore, kHalves>;
+  using C = W8WideCfg<kTmaStore>;
   const int r = static_cast<int>(L.r);
   CUtensorMap tm_x, tm_codes, tm_p, tm_bt;
   int st = CF_OK;
@@ -2314,10 +2300,8 @@ int launch_w8_wide(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
   p.done = kTmaStore ? L.done : nullptr;
   p.rb_per_group = L.rb_per_group;
   p.n_groups = L.n_groups;
-  auto kernel = w8_wide_kernel<kBf16, kTmaStore, kHalves>;
-  if (int st_ = allow_dynamic_smem<w8_wide_kernel<kBf16, kTmaStore, kHalves>>(C::kSmemBytes)) {
-    return st_;
-  }
+  auto kernel = w8_wide_kernel<kBf16, kTmaStore>;
+  if (int st_ = allow_dynamic_smem<w8_wide_kernel<kBf16, kTmaStore>>(C::kSmemBytes)) return st_;
   const int grid = std::max(1, std::min(p.n_tiles, sm_count()));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
@@ -2347,10 +2331,7 @@ int run_linear(const LinearArgs &L, cudaStream_t stream) {
     if (L.n_dest == 0 && L.m <= 32) return launch_w8_decode<32, kBf16>(L, err, stream);
     if (L.n_dest == 0 && L.m <= 64) return launch_w8_decode<64, kBf16>(L, err, stream);
     if (L.n_dest == 0 && L.m <= 128) return launch_w8_decode<128, kBf16>(L, err, stream);
-    // Six or more destinations (an 8-GPU group): the exchange dominates, so
-    // take 256-token tiles whose stores overlap the next tile's main loop.
-    if (L.n_dest >= 6) return launch_w8_wide<kBf16, true, 1>(L, err, stream);
-    return launch_w8_wide<kBf16, true, 2>(L, err, stream);
+    return launch_w8_wide<kBf16, true>(L, err, stream);
   }
 
   constexpr int BN = 256;
@@ -2775,7 +2756,7 @@ int cf_lora_linear_int8_allgather_ce(const void *x, const int8_t *w_codes, const
   if (m == 0 || n == 0) return CF_OK;
   const size_t lin = cfb::workspace_bytes(m, rank);
   if (workspace == nullptr || workspace_bytes < lin + kCeCounterBytes) return CF_ERR_WORKSPACE;
-  constexpr int kRowBlock = W8WideCfg<true, 2>::BT;
+  constexpr int kRowBlock = W8WideCfg<true>::BT;
   const int64_t n_rb = (m + kRowBlock - 1) / kRowBlock;
   const int rb_per_group = static_cast<int>((n_rb + kCeGroups - 1) / kCeGroups);
   const int n_groups = static_cast<int>((n_rb + rb_per_group - 1) / rb_per_group);
