@@ -204,13 +204,16 @@ def _w8_case(m, k, n, rank, device, seed):
 
 @pytest.mark.parametrize("mode", ["kernel", "ce"])
 @pytest.mark.parametrize(("m", "rank"), [(1536, 64), (700, 16), (5000, 32)])
-def test_multi_destination_entry_points(mode, m, rank, cuda_device):
-    # Three destinations on one GPU stand in for three ranks' copies of y; this
-    # call owns columns [col0, col0 + n) of each [m, ldy] destination.
+@pytest.mark.parametrize("n_dest", [3, 8])
+def test_multi_destination_entry_points(mode, m, rank, n_dest, cuda_device):
+    # n_dest destinations on one GPU (8 = the most a call takes) stand in for
+    # the ranks' copies of y; this call owns columns [col0, col0 + n) of each
+    # [m, ldy] destination.
     k, n, ldy, col0 = 1024, 1024, 3072, 1024
     x, codes, scales, a, b = _w8_case(m, k, n, rank, cuda_device, seed=m + rank)
-    dests = [torch.full((m, ldy), 7.0, dtype=torch.bfloat16, device=cuda_device) for _ in range(3)]
-    ptrs = (ctypes.c_void_p * 3)(*[t.data_ptr() for t in dests])
+    dests = [torch.full((m, ldy), 7.0, dtype=torch.bfloat16, device=cuda_device)
+             for _ in range(n_dest)]
+    ptrs = (ctypes.c_void_p * n_dest)(*[t.data_ptr() for t in dests])
     lib = _abi.load()
     s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
@@ -218,15 +221,15 @@ def test_multi_destination_entry_points(mode, m, rank, cuda_device):
         ws_bytes = lib.cf_lora_linear_int8_allgather_ce_workspace_bytes(m, rank)
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=cuda_device)
         _abi.check(lib.cf_lora_linear_int8_allgather_ce(
-            p(x), p(codes), p(scales), p(a), _abi.CF_LAYOUT_REF, p(b), _abi.CF_LAYOUT_REF, 3, ptrs,
-            1, ldy, col0, m, k, n, rank, 2.0, _abi.CF_DTYPE_BF16, p(ws), ws_bytes, s),
+            p(x), p(codes), p(scales), p(a), _abi.CF_LAYOUT_REF, p(b), _abi.CF_LAYOUT_REF, n_dest,
+            ptrs, 1, ldy, col0, m, k, n, rank, 2.0, _abi.CF_DTYPE_BF16, p(ws), ws_bytes, s),
             "cf_lora_linear_int8_allgather_ce")
     else:
         ws_bytes = lib.cf_lora_linear_workspace_bytes(m, rank)
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=cuda_device)
         _abi.check(lib.cf_lora_linear_int8_allgather(
-            p(x), p(codes), p(scales), p(a), _abi.CF_LAYOUT_REF, p(b), _abi.CF_LAYOUT_REF, 3, ptrs,
-            1, ldy, col0, m, k, n, rank, 2.0, _abi.CF_DTYPE_BF16, p(ws), ws_bytes, s),
+            p(x), p(codes), p(scales), p(a), _abi.CF_LAYOUT_REF, p(b), _abi.CF_LAYOUT_REF, n_dest,
+            ptrs, 1, ldy, col0, m, k, n, rank, 2.0, _abi.CF_DTYPE_BF16, p(ws), ws_bytes, s),
             "cf_lora_linear_int8_allgather")
     torch.cuda.synchronize()
     assert lib.cf_device_status() == _abi.CF_OK
