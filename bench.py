@@ -634,6 +634,180 @@ class W8Prefill(LoraLinear):
     main_kernel = "w8_wide_kernel (128 x 512 tiles, TMA-store epilogue)"
 
 
+class LoraF32(LoraLinear):
+    """fp32 LoRA linear (the reference's own CUDA dtype), BASELINE config 3 shapes."""
+
+    name = "lora_f32_8192x4096x4096"
+    main_kernel = "lora_f32_kernel (three tf32 products)"
+    # tf32 runs at half the bf16 rate and each fp32 multiply-add is three tf32 products.
+    peak_divisor = 6
+    peak_divisor_reason = "tf32 = bf16 / 2, three tf32 products per fp32 product"
+
+    def __init__(self, dist: Dist, _layers: int = 0):
+        super().__init__(dist, _layers)
+        self.metric = (f"LoRA linear fp32 TFLOP/s (x [{self.m},{self.k}], W [{self.n},{self.k}], "
+                       f"r {self.r})")
+        self.dtype = "fp32 (three tf32 tensor-core products, fp32 accumulate)"
+
+    def bytes(self) -> float:
+        return 4 * (self.n * self.k + self.m * self.k + self.k * self.r + self.r * self.n
+                    + self.m * self.n)
+
+    def config(self) -> dict:
+        c = super().config()
+        c["weight"] = "fp32 [out, in] (passed as W.t(), K-major)"
+        return c
+
+    def setup(self) -> None:
+        from cuda_force_b200 import _abi
+
+        dev = self.dist.device
+        g = torch.Generator(device=dev).manual_seed(3)
+        self.x = torch.randn(self.m, self.k, device=dev, generator=g) * self.x_std
+        self.w = torch.randn(self.n, self.k, device=dev, generator=g) * self.w_std
+        self.a = torch.randn(self.k, self.r, device=dev, generator=g) * self.ab_std
+        self.b = torch.randn(self.r, self.n, device=dev, generator=g) * self.ab_std
+        self.scale = self.alpha / self.r
+        self.lib = _abi.load()
+        self.y = torch.empty(self.m, self.n, dtype=torch.float32, device=dev)
+        self.ws_bytes = self.lib.cf_lora_linear_workspace_bytes(self.m, self.r)
+        self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=dev)
+        self.work_per_step = self.flops()
+        self.launches_per_step = 2
+
+    def step(self, stream) -> None:
+        from cuda_force_b200 import _abi
+
+        st = self.lib.cf_lora_linear(
+            self.x.data_ptr(), self.w.data_ptr(), _abi.CF_LAYOUT_T, self.a.data_ptr(),
+            _abi.CF_LAYOUT_REF, self.b.data_ptr(), _abi.CF_LAYOUT_REF, self.y.data_ptr(),
+            self.m, self.k, self.n, self.r, self.scale, _abi.CF_DTYPE_F32, self.ws.data_ptr(),
+            self.ws_bytes, stream.cuda_stream)
+        _abi.check(st, self.name)
+
+    def verify(self) -> None:
+        rows = torch.randperm(self.m, generator=torch.Generator().manual_seed(0))[:128]
+        rows = rows.to(self.x.device)
+        x = self.x[rows].double()
+        ref = x @ self.w.t().double() + self.scale * ((x @ self.a.double()) @ self.b.double())
+        err = ((self.y[rows].double() - ref).abs().max() / ref.abs().max()).item()
+        assert err <= 1e-4, f"{self.name}: max relative error {err}"
+
+    def e2e(self, steps: int) -> dict:
+        import cuda_force_b200 as cf
+
+        dev = self.dist.device
+        hx = self.x.cpu().pin_memory()
+        hy = torch.empty(self.m, self.n, dtype=torch.float32).pin_memory()
+
+        def one():
+            x = hx.to(dev, non_blocking=True)
+            y = cf.lora_linear(x, self.w.t(), self.a, self.b, self.scale)
+            hy.copy_(y, non_blocking=True)
+
+        return timed_e2e(self, one, steps, hx.numel() * 4, hy.numel() * 4,
+                         "cuda_force_b200.lora_linear fp32 (weights resident, x in / y out)")
+
+
+class MergeQuant:
+    """LoRA merge + block-INT8 quantise (training/lora.py:95-111, then quantize_int8)."""
+
+    name = "lora_merge_quant_11008x4096_r16"
+    unit = "GB/s"
+    bound = "hbm"
+    scaling = "weak"
+    flush_l2 = True
+    n, k, r, scaling_factor = 11008, 4096, 16, 2.0
+    kernel = "lora_merge_quant_kernel"
+    dtype = "bf16 -> int8 codes + fp32 scales"
+    metric = "LoRA merge + block-INT8 quantise GB/s (W [11008,4096] bf16, r 16)"
+
+    def __init__(self, dist: Dist, _layers: int = 0):
+        self.dist = dist
+
+    def bytes(self) -> float:
+        return self.n * self.k * (2 + 1 + 4 / 64) + 2 * self.r * (self.n + self.k)
+
+    def config(self) -> dict:
+        return {"workload": self.__doc__.strip() + f" [{self.name}]", "out": self.n, "in": self.k,
+                "rank": self.r, "scaling": self.scaling_factor,
+                "layouts": "W [out, in], lora_a [rank, in], lora_b [out, rank] (module layouts)",
+                "values": "W N(0,0.02), lora_a and lora_b N(0,0.05)",
+                "l2": "flushed between steps (256 MiB write outside the timed events)",
+                "parallelism": f"{self.dist.world} independent replica(s)"}
+
+    def setup(self) -> None:
+        from cuda_force_b200 import _abi
+
+        dev = self.dist.device
+        g = torch.Generator(device=dev).manual_seed(9)
+        self.w = (torch.randn(self.n, self.k, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        self.a = (torch.randn(self.r, self.k, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+        self.b = (torch.randn(self.n, self.r, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+        self.codes = torch.empty(self.n, self.k, dtype=torch.int8, device=dev)
+        self.scales = torch.empty(self.n * self.k // 64, dtype=torch.float32, device=dev)
+        self.lib = _abi.load()
+        self.work_per_step = self.bytes()
+        self.launches_per_step = 1
+
+    def step(self, stream) -> None:
+        from cuda_force_b200 import _abi
+
+        st = self.lib.cf_lora_merge_quantize_int8(
+            self.w.data_ptr(), self.a.data_ptr(), self.b.data_ptr(), self.n, self.k, self.r,
+            self.scaling_factor, _abi.CF_DTYPE_BF16, self.codes.data_ptr(),
+            self.scales.data_ptr(), stream.cuda_stream)
+        _abi.check(st, self.name)
+
+    def verify(self) -> None:
+        import cuda_force_b200 as cf
+
+        merged = self.w + self.scaling_factor * (self.b @ self.a)
+        ref_codes, ref_scales = cf.quantize_int8(merged)
+        diff = (self.codes.int() - ref_codes.int()).abs()
+        assert diff.max().item() <= 1 and (diff > 0).float().mean().item() <= 1e-3, self.name
+        rel = ((self.scales - ref_scales).abs() / ref_scales).max().item()
+        assert rel <= 2.0 ** -7, f"{self.name}: scale error {rel}"
+
+    def e2e(self, steps: int) -> dict:
+        import cuda_force_b200 as cf
+
+        dev = self.dist.device
+        hw = self.w.cpu().pin_memory()
+        hc = torch.empty(self.n, self.k, dtype=torch.int8).pin_memory()
+        hs = torch.empty(self.n * self.k // 64, dtype=torch.float32).pin_memory()
+
+        def one():
+            w = hw.to(dev, non_blocking=True)
+            codes, scales = cf.lora_merge_quantize_int8(w, self.a, self.b, self.scaling_factor)
+            hc.copy_(codes, non_blocking=True)
+            hs.copy_(scales, non_blocking=True)
+
+        return timed_e2e(self, one, steps, hw.numel() * 2, hc.numel() + hs.numel() * 4,
+                         "cuda_force_b200.lora_merge_quantize_int8 (adapter resident, W in, "
+                         "codes and scales out)")
+
+    def cpu_sample(self):
+        from oracle import build_ref
+
+        rows = 512
+        w, a, b = self.w[:rows].cpu(), self.a.cpu(), self.b[:rows].cpu()
+        have_ref = build_ref.load()
+
+        def fn():
+            merged = w + self.scaling_factor * (b @ a)   # the module's merged_weight()
+            if have_ref:
+                torch.ops.cudaforge_ref.quantize_int8(merged)
+            else:
+                from oracle import quant_ref
+
+                quant_ref.quantize(merged.float().numpy().reshape(-1))
+
+        return (fn, self.work_per_step * rows / self.n, "reference" if have_ref else "port",
+                f"{rows} of {self.n} rows: merged_weight() in bf16 then the reference's CPU "
+                f"quantize_int8")
+
+
 class W8ColumnSharded:
     """column-sharded W8 + LoRA on a Llama-70B MLP shape + NCCL all-gather."""
 
@@ -786,7 +960,7 @@ class W8ColumnSharded:
 
 
 WORKLOADS = {w.name: w for w in (LlamaStackQuant, Config1Quant, Config1Dequant, LoraLinear,
-                                W8Decode, W8Prefill, W8ColumnSharded)}
+                                W8Decode, W8Prefill, W8ColumnSharded, LoraF32, MergeQuant)}
 
 
 # ---------------------------------------------------------------------------
@@ -846,6 +1020,10 @@ def run_ours(args, dist: Dist) -> dict | None:
         peak, peak_key, peak_unit = peaks["hbm_gbs"], "hbm_gbs", "GB/s"
     else:
         peak, peak_key, peak_unit = peaks["bf16_tflops"], "bf16_tflops (burst)", "TFLOP/s"
+    divisor = getattr(wl, "peak_divisor", 1)
+    if divisor != 1:
+        peak = round(peak / divisor, 2)
+        peak_key += f" / {divisor} ({wl.peak_divisor_reason})"
     traffic_info = load_traffic().get(wl.name)
     traffic = traffic_info.get("dram_bytes_per_step") if traffic_info else None
 
