@@ -705,6 +705,11 @@ __global__ void __launch_bounds__(DecCfg<BT>::kThreads, DecCfg<BT>::kMinBlocks)
   const int n_raw_loads = (nkb + C::kRawKb - 1) / C::kRawKb;
 
   if (threadIdx.x == 0) {
+    // Descriptor fetches overlap the setup instead of the first loads.
+    ptx::prefetch_tensor_map(&tm_codes);
+    ptx::prefetch_tensor_map(&tm_x);
+    ptx::prefetch_tensor_map(&tm_p);
+    ptx::prefetch_tensor_map(&tm_bt);
     for (int s = 0; s < C::kRawStages; ++s) {
       ptx::mbar_init(&raw_full[s], 1);
       ptx::mbar_init(&raw_empty[s], kConvWarps);
@@ -1101,6 +1106,11 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore>::kThreads, 1)
   const int num_iters = p.num_kb + n_extra;
 
   if (threadIdx.x == 0) {
+    // Descriptor fetches overlap the setup instead of the first loads.
+    ptx::prefetch_tensor_map(&tm_codes);
+    ptx::prefetch_tensor_map(&tm_x);
+    ptx::prefetch_tensor_map(&tm_p);
+    ptx::prefetch_tensor_map(&tm_bt);
     for (int s = 0; s < C::kStages; ++s) {
       ptx::mbar_init(&full[s], 1);
       ptx::mbar_init(&empty[s], 1);
@@ -1475,6 +1485,11 @@ __global__ void __launch_bounds__(F32Cfg::kThreads, 1)
   const int num_iters = p.num_kb + p.extra_kb;
 
   if (threadIdx.x == 0) {
+    // Descriptor fetches overlap the setup instead of the first loads.
+    ptx::prefetch_tensor_map(&tm_a);
+    ptx::prefetch_tensor_map(&tm_b);
+    ptx::prefetch_tensor_map(&tm_pa);
+    ptx::prefetch_tensor_map(&tm_pb);
     for (int s = 0; s < C::kStages; ++s) {
       ptx::mbar_init(&full[s], 1);
       ptx::mbar_init(&split[s], kSplitWarps);
@@ -1842,6 +1857,10 @@ __global__ void __launch_bounds__(MergeCfg::kThreads, 1)
   const int lane = threadIdx.x % kWarp;
 
   if (threadIdx.x == 0) {
+    // Descriptor fetches overlap the setup instead of the first loads.
+    ptx::prefetch_tensor_map(&tm_b);
+    ptx::prefetch_tensor_map(&tm_a);
+    ptx::prefetch_tensor_map(&tm_w);
     for (int s = 0; s < C::kStages; ++s) {
       ptx::mbar_init(&full[s], 1);
       ptx::mbar_init(&empty[s], 1 + C::kEpiWarps);  // MMA commit + epilogue warps
