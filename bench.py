@@ -808,6 +808,106 @@ class MergeQuant:
                 f"quantize_int8")
 
 
+class W8SwiGLU:
+    """LLaMA MLP gate + up projections with block-INT8 weights and SwiGLU fused."""
+
+    name = "w8_swiglu_4096x4096x11008"
+    unit = "TFLOP/s"
+    bound = "tensor"
+    scaling = "weak"
+    flush_l2 = True
+    m, k, n = 4096, 4096, 11008
+    kernel = "w8_swiglu_kernel (gate and up tiles per stage, silu(g) * u in the epilogue)"
+    dtype = "bf16 x int8->bf16 (fp32 acc)"
+    metric = "W8 gate+up+SwiGLU TFLOP/s (x [4096,4096], Wg and Wu [11008,4096] int8)"
+
+    def __init__(self, dist: Dist, _layers: int = 0):
+        self.dist = dist
+
+    def flops(self) -> float:
+        return 2 * 2.0 * self.m * self.n * self.k
+
+    def config(self) -> dict:
+        return {"workload": self.__doc__.strip() + f" [{self.name}]", "m": self.m, "k": self.k,
+                "n": self.n, "weights": "block-64 int8 codes + fp32 scales (gate, up)",
+                "values": "x N(0,1), Wg and Wu N(0,0.02)",
+                "l2": "flushed between steps (256 MiB write outside the timed events)",
+                "parallelism": f"{self.dist.world} independent replica(s)"}
+
+    def setup(self) -> None:
+        import cuda_force_b200 as cf
+        from cuda_force_b200 import _abi
+
+        dev = self.dist.device
+        g = torch.Generator(device=dev).manual_seed(11)
+        self.x = torch.randn(self.m, self.k, device=dev, generator=g).to(torch.bfloat16)
+        wg = (torch.randn(self.n, self.k, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        wu = (torch.randn(self.n, self.k, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        self.gc, self.gs = cf.quantize_int8(wg)
+        self.uc, self.us = cf.quantize_int8(wu)
+        del wg, wu
+        self.y = torch.empty(self.m, self.n, dtype=torch.bfloat16, device=dev)
+        self.lib = _abi.load()
+        self.work_per_step = self.flops()
+        self.launches_per_step = 1
+
+    def step(self, stream) -> None:
+        from cuda_force_b200 import _abi
+
+        st = self.lib.cf_w8_swiglu_int8(
+            self.x.data_ptr(), self.gc.data_ptr(), self.gs.data_ptr(), self.uc.data_ptr(),
+            self.us.data_ptr(), self.y.data_ptr(), self.m, self.k, self.n, _abi.CF_DTYPE_BF16,
+            stream.cuda_stream)
+        _abi.check(st, self.name)
+
+    def verify(self) -> None:
+        from oracle import linear_ref
+
+        rows = torch.randperm(self.m, generator=torch.Generator().manual_seed(0))[:64]
+        rows = rows.to(self.x.device)
+        xf = self.x[rows].float()
+        g = (xf @ linear_ref.dequantized_weight_t(self.gc, self.gs).to(xf.device)).bfloat16().float()
+        u = (xf @ linear_ref.dequantized_weight_t(self.uc, self.us).to(xf.device)).bfloat16().float()
+        ref = g / (1.0 + torch.exp(-g)) * u
+        err = ((self.y[rows].float() - ref).abs().max() / ref.abs().max()).item()
+        assert err <= 2e-2, f"{self.name}: max relative error {err}"
+
+    def e2e(self, steps: int) -> dict:
+        import cuda_force_b200 as cf
+
+        dev = self.dist.device
+        hx = self.x.cpu().pin_memory()
+        hy = torch.empty(self.m, self.n, dtype=torch.bfloat16).pin_memory()
+
+        def one():
+            x = hx.to(dev, non_blocking=True)
+            hy.copy_(cf.w8_swiglu_int8(x, self.gc, self.gs, self.uc, self.us), non_blocking=True)
+
+        return timed_e2e(self, one, steps, hx.numel() * 2, hy.numel() * 2,
+                         "cuda_force_b200.w8_swiglu_int8 (weights resident, x in / h out)")
+
+    def cpu_sample(self):
+        from oracle import build_ref
+
+        rows = 64
+        x = self.x[:rows].float().cpu()
+        gc, gs, uc, us = self.gc.cpu(), self.gs.cpu(), self.uc.cpu(), self.us.cpu()
+        have_ref = build_ref.load()
+
+        def fn():
+            if have_ref:
+                wg = torch.ops.cudaforge_ref.dequantize_int8(gc, gs).reshape(self.n, self.k)
+                wu = torch.ops.cudaforge_ref.dequantize_int8(uc, us).reshape(self.n, self.k)
+                torch.ops.cudaforge_ref.swiglu(x @ wg.t(), x @ wu.t())
+            else:
+                g, u = x @ gc.float().t(), x @ uc.float().t()
+                g / (1.0 + torch.exp(-g)) * u
+
+        return (fn, self.work_per_step * rows / self.m, "reference" if have_ref else "port",
+                f"{rows} of {self.m} rows: the reference's CPU dequantize_int8, x @ W.T and "
+                f"swiglu")
+
+
 class W8ColumnSharded:
     """column-sharded W8 + LoRA on a Llama-70B MLP shape + NCCL all-gather."""
 
@@ -960,7 +1060,8 @@ class W8ColumnSharded:
 
 
 WORKLOADS = {w.name: w for w in (LlamaStackQuant, Config1Quant, Config1Dequant, LoraLinear,
-                                W8Decode, W8Prefill, W8ColumnSharded, LoraF32, MergeQuant)}
+                                W8Decode, W8Prefill, W8ColumnSharded, LoraF32, MergeQuant,
+                                W8SwiGLU)}
 
 
 # ---------------------------------------------------------------------------

@@ -19,6 +19,7 @@ from cuda_force_b200.ops import (
     quantize_dequantize,
     quantize_int8,
     quantize_int8_many,
+    w8_swiglu_int8,
 )
 
 __version__ = "0.1.0"
@@ -39,4 +40,5 @@ __all__ = [
     "quantize_dequantize",
     "quantize_int8",
     "quantize_int8_many",
+    "w8_swiglu_int8",
 ]

@@ -69,6 +69,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          _i64, _i64, ctypes.c_float, _int, _p, ctypes.c_size_t, _p],
     ),
     "cf_matmul_f32": (_int, [_p, _p, _int, _p, _i64, _i64, _i64, _int, _p]),
+    "cf_w8_swiglu_int8": (_int, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p]),
     "cf_lora_merge_quantize_int8": (
         _int, [_p, _p, _p, _i64, _i64, _i64, ctypes.c_float, _int, _p, _p, _p]),
     "cf_lora_linear_noalloc": (

@@ -1255,7 +1255,10 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore>::kThreads, 1)
     for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x, ++local) {
       const int w0 = (tile % p.n_tiles_w) * kBM;
       const int t0 = (tile / p.n_tiles_w) * BT;
-      const bool ok = ptx::warp_wait(tmem_full, static_cast<uint32_t>(local & 1));
+      // With the TMA-store path the four epilogue warps share named barriers,
+      // so they decide together whether to go on.
+      bool ok = ptx::warp_wait(tmem_full, static_cast<uint32_t>(local & 1));
+      if constexpr (kTmaStore) ok = ptx::named_bar_all(1, 4 * kWarp, ok);
       if (!ok) {
         if (lane == 0) record_timeout(p.err, abort_flag);
         break;
@@ -2051,6 +2054,330 @@ __global__ void __launch_bounds__(MergeCfg::kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// W8 gate and up projections of a LLaMA MLP with the SwiGLU fused into the
+// epilogue (SURVEY row "SwiGLU after the up-projection"; the reference's
+// examples/transformer_block.py:70-89 computes swiglu(gate(x), up(x)), and its
+// cuda/src/activations.cu:19-21, 68-76 defines silu(x) = x / (1 + exp(-x))):
+//   h[t, f] = silu(g) * u,  g = round(x Wg^T)[t, f],  u = round(x Wu^T)[t, f]
+// with g and u rounded to the activation dtype as the two projections' outputs
+// would be, and h computed in fp32 and rounded once.
+//
+// Swap-AB like w8_wide_kernel: a tile is 128 features x 256 tokens; each stage
+// carries the gate and the up code tiles of the same 128 features (32-wide
+// k-blocks) and one activation tile, the converters turn both into bf16/f16,
+// and per k-step two N = 256 MMAs accumulate g into TMEM columns 0-255 and u
+// into 256-511 against the same activation operand. The epilogue thread owns
+// feature row f of both accumulators, so silu(g) * u needs no exchange; the
+// result goes out through the staged TMA-store path. Only h reaches memory.
+//   warp 0 TMA producer, warp 1 TMEM owner + MMA issuer, warps 4-7 epilogue,
+//   warps 8-15 converters.
+// ---------------------------------------------------------------------------
+struct SwigluCfg {
+  static constexpr int BT = 256;                       // tokens per tile
+  static constexpr int kBKw = 32;                      // k-block width
+  static constexpr int kRowBytes = kBKw * 2;           // 64 -> 64-byte swizzle
+  static constexpr int kABytes = kBM * kRowBytes;      // 8 KB per converted tile
+  static constexpr int kXBytes = BT * kRowBytes;       // 16 KB
+  static constexpr int kRawBytes = kBM * kBKw;         // 4 KB per code tile
+  // [gate bf16][up bf16][x][gate codes][up codes]
+  static constexpr int kStageBytes = 2 * kABytes + kXBytes + 2 * kRawBytes;  // 40 KB
+  static constexpr int kStages = 5;
+  static constexpr int kSlabBytes = 32 * kBM * 2;      // 32 tokens x 128 features
+  static constexpr int kStagingBytes = 2 * kSlabBytes;
+  static constexpr int kThreads = 512;
+  static constexpr int kTmemCols = 512;                // g: 0-255, u: 256-511
+  static constexpr size_t kSmemBytes =
+      1024 + static_cast<size_t>(kStages) * kStageBytes + kStagingBytes + 256;
+  static_assert(kStageBytes % 1024 == 0, "stage alignment");
+};
+
+struct SwigluParams {
+  int M, N;
+  int num_kb;               // k-blocks of 32
+  int kb_per_row;           // scales per weight row (K / 64)
+  const float *g_scales;
+  const float *u_scales;
+  int n_tiles_w;
+  int n_tiles;
+  unsigned *err;
+};
+
+template <bool kBf16>
+__global__ void __launch_bounds__(SwigluCfg::kThreads, 1)
+    w8_swiglu_kernel(const __grid_constant__ CUtensorMap tm_x,
+                     const __grid_constant__ CUtensorMap tm_g,
+                     const __grid_constant__ CUtensorMap tm_u,
+                     const __grid_constant__ CUtensorMap tm_y, const SwigluParams p) {
+  using C = SwigluCfg;
+  constexpr int BT = C::BT;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t *staging = smem + C::kStages * C::kStageBytes;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(staging + C::kStagingBytes);
+  uint64_t *full = bars;
+  uint64_t *empty = bars + C::kStages;
+  uint64_t *conv_full = bars + 2 * C::kStages;
+  uint64_t *tmem_full = bars + 3 * C::kStages;
+  uint64_t *tmem_empty = tmem_full + 1;
+  uint64_t *drain = tmem_empty + 1;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  int *abort_flag = reinterpret_cast<int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / kWarp;
+  const int lane = threadIdx.x % kWarp;
+
+  if (threadIdx.x == 0) {
+    ptx::prefetch_tensor_map(&tm_x);
+    ptx::prefetch_tensor_map(&tm_g);
+    ptx::prefetch_tensor_map(&tm_u);
+    ptx::prefetch_tensor_map(&tm_y);
+    for (int s = 0; s < C::kStages; ++s) {
+      ptx::mbar_init(&full[s], 1);
+      ptx::mbar_init(&empty[s], 1);
+      ptx::mbar_init(&conv_full[s], kConvThreads / kWarp);
+    }
+    ptx::mbar_init(tmem_full, 1);
+    ptx::mbar_init(tmem_empty, 4);
+    ptx::mbar_init(drain, 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, C::kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t outstanding = 0, issue_parity = 0;
+      for (int tile = blockIdx.x; tile < p.n_tiles && !aborted(abort_flag); tile += gridDim.x) {
+        const int w0 = (tile % p.n_tiles_w) * kBM;
+        const int t0 = (tile / p.n_tiles_w) * BT;
+        for (int it = 0; it < p.num_kb; ++it) {
+          if (!ptx::mbar_wait(&empty[stage], phase ^ 1)) {
+            record_timeout(p.err, abort_flag);
+            break;
+          }
+          uint8_t *sx = smem + stage * C::kStageBytes + 2 * C::kABytes;
+          uint8_t *raw = sx + C::kXBytes;
+          const int k0 = it * C::kBKw;
+          ptx::mbar_expect_tx(&full[stage], C::kXBytes + 2 * C::kRawBytes);
+          ptx::tma_load_2d(sx, &tm_x, &full[stage], k0, t0);
+          ptx::tma_load_2d(raw, &tm_g, &full[stage], k0, w0);
+          ptx::tma_load_2d(raw + C::kRawBytes, &tm_u, &full[stage], k0, w0);
+          outstanding |= 1u << stage;
+          issue_parity = (issue_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (aborted(abort_flag)) {
+        for (int s = 0; s < C::kStages; ++s) {
+          if (outstanding & (1u << s)) ptx::mbar_wait(&full[s], (issue_parity >> s) & 1u, 200000000ull);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = ptx::make_idesc_f16(kBf16, kBM, BT, false, false);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (int tile = blockIdx.x; tile < p.n_tiles && !aborted(abort_flag);
+           tile += gridDim.x, ++local) {
+        if (!ptx::mbar_wait(tmem_empty, static_cast<uint32_t>(local & 1) ^ 1u)) {
+          record_timeout(p.err, abort_flag);
+          break;
+        }
+        ptx::tc_fence_after();
+        bool ok = true;
+        for (int it = 0; it < p.num_kb; ++it) {
+          if (!ptx::mbar_wait(&conv_full[stage], phase)) {
+            record_timeout(p.err, abort_flag);
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint32_t sg = ptx::smem_addr(smem + stage * C::kStageBytes);
+          const uint32_t su = sg + C::kABytes;
+          const uint32_t sx = sg + 2 * C::kABytes;
+          for (int ks = 0; ks < C::kBKw / kUmmaK; ++ks) {
+            const uint64_t bdesc = kmajor_desc(sx, C::kRowBytes, ks);
+            const uint32_t acc = (it > 0 || ks > 0) ? 1u : 0u;
+            ptx::mma_f16(tmem_base, kmajor_desc(sg, C::kRowBytes, ks), bdesc, idesc, acc);
+            ptx::mma_f16(tmem_base + BT, kmajor_desc(su, C::kRowBytes, ks), bdesc, idesc, acc);
+          }
+          ptx::mma_commit(&empty[stage]);
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        ptx::mma_commit(tmem_full);
+      }
+      if (aborted(abort_flag)) {
+        ptx::mma_commit(drain);
+        ptx::mbar_wait(drain, 0, 200000000ull);
+      }
+    }
+  } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) {
+    // ------------------------------------------------------------------ epilogue
+    const int quarter = warp % 4;
+    const int row = quarter * 32 + lane;
+    const bool elected = threadIdx.x == kEpiWarp0 * kWarp;
+    uint32_t slab = 0;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x, ++local) {
+      const int w0 = (tile % p.n_tiles_w) * kBM;
+      const int t0 = (tile / p.n_tiles_w) * BT;
+      // The four epilogue warps share named barriers, so they leave together.
+      const bool got = ptx::warp_wait(tmem_full, static_cast<uint32_t>(local & 1));
+      if (!ptx::named_bar_all(1, 4 * kWarp, got)) {
+        if (lane == 0) record_timeout(p.err, abort_flag);
+        break;
+      }
+      ptx::tc_fence_after();
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+#pragma unroll 1
+      for (int c = 0; c < BT / 32; ++c) {
+        uint32_t g[32], u[32];
+        ptx::tmem_ld_32x32b_x32(t_row + c * 32, g);
+        ptx::tmem_ld_32x32b_x32(t_row + BT + c * 32, u);
+        ptx::tmem_ld_wait();
+        // Stage a 32-token x 128-feature slab (token-major) and let the TMA
+        // engine store it; the slab buffer is double-buffered against the
+        // store still reading it.
+        if (elected) ptx::bulk_wait_read<1>();
+        ptx::named_bar_sync(1, 4 * kWarp);
+        uint16_t *stg = reinterpret_cast<uint16_t *>(staging + (slab & 1) * C::kSlabBytes);
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          // The projections' outputs in the activation dtype ...
+          const uint32_t gp = kBf16 ? ptx::pack_bf16x2(__uint_as_float(g[j]), __uint_as_float(g[j + 1]))
+                                    : ptx::pack_f16x2(__uint_as_float(g[j]), __uint_as_float(g[j + 1]));
+          const uint32_t up = kBf16 ? ptx::pack_bf16x2(__uint_as_float(u[j]), __uint_as_float(u[j + 1]))
+                                    : ptx::pack_f16x2(__uint_as_float(u[j]), __uint_as_float(u[j + 1]));
+          float g0, g1, u0, u1;
+          if constexpr (kBf16) {
+            g0 = __uint_as_float(gp << 16);
+            g1 = __uint_as_float(gp & 0xffff0000u);
+            u0 = __uint_as_float(up << 16);
+            u1 = __uint_as_float(up & 0xffff0000u);
+          } else {
+            const float2 gf = __half22float2(*reinterpret_cast<const __half2 *>(&gp));
+            const float2 uf = __half22float2(*reinterpret_cast<const __half2 *>(&up));
+            g0 = gf.x;
+            g1 = gf.y;
+            u0 = uf.x;
+            u1 = uf.y;
+          }
+          // ... then silu(g) * u in fp32, rounded once.
+          const float h0 = g0 / (1.0f + __expf(-g0)) * u0;
+          const float h1 = g1 / (1.0f + __expf(-g1)) * u1;
+          const uint32_t hp = kBf16 ? ptx::pack_bf16x2(h0, h1) : ptx::pack_f16x2(h0, h1);
+          stg[j * kBM + row] = static_cast<uint16_t>(hp & 0xffffu);
+          stg[(j + 1) * kBM + row] = static_cast<uint16_t>(hp >> 16);
+        }
+        ptx::fence_proxy_async_smem();
+        ptx::named_bar_sync(1, 4 * kWarp);
+        if (elected) {
+          ptx::tma_store_2d(&tm_y, stg, w0, t0 + c * 32);
+          ptx::bulk_commit();
+        }
+        ++slab;
+      }
+      ptx::tc_fence_before();
+      ptx::warp_arrive(tmem_empty);
+    }
+    if (elected) ptx::bulk_wait_all();  // stores finish reading shared memory before exit
+  } else if (warp >= kConvWarp0) {
+    // ------------------------------------------------------------------ converters
+    // Lane l of converter warp cw: row cw * 16 + l / 2, 16-code half l % 2 of
+    // the 32-code row, for the gate tile and then the up tile; writes 32
+    // bytes of each 64-byte swizzled bf16 row (logical 16-byte chunk c sits
+    // at c ^ ((row >> 1) & 3)).
+    const int cw = warp - kConvWarp0;
+    const int r = cw * 16 + lane / 2;
+    const int half = lane & 1;
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x) {
+      const int w0 = (tile % p.n_tiles_w) * kBM;
+      const int n = w0 + r;
+      const float *srow[2] = {
+          n < p.N ? p.g_scales + static_cast<int64_t>(n) * p.kb_per_row : nullptr,
+          n < p.N ? p.u_scales + static_cast<int64_t>(n) * p.kb_per_row : nullptr};
+      bool ok = true;
+      for (int it = 0; it < p.num_kb; ++it) {
+        float sc[2];
+#pragma unroll
+        for (int w = 0; w < 2; ++w) sc[w] = srow[w] != nullptr ? __ldg(srow[w] + it / 2) : 0.0f;
+        const bool got = ptx::mbar_wait(&full[stage], phase);
+        if (__any_sync(0xffffffffu, !got)) {
+          if (lane == 0) record_timeout(p.err, abort_flag);
+          ok = false;
+          break;
+        }
+        uint8_t *base = smem + stage * C::kStageBytes;
+        const uint8_t *raw = base + 2 * C::kABytes + C::kXBytes;
+#pragma unroll
+        for (int w = 0; w < 2; ++w) {
+          const uint4 codes =
+              *reinterpret_cast<const uint4 *>(raw + w * C::kRawBytes + r * C::kBKw + half * 16);
+          const uint32_t words[4] = {codes.x, codes.y, codes.z, codes.w};
+          const uint64_t sc2 = ptx::splat_f32x2(sc[w]);
+          uint32_t outw[8];
+#pragma unroll
+          for (int wd = 0; wd < 4; ++wd) {
+            const uint32_t uu = words[wd] ^ 0x80808080u;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const uint32_t b0 = __byte_perm(uu, 0x4B000000u, 0x7440u | (2 * h));
+              const uint32_t b1 = __byte_perm(uu, 0x4B000000u, 0x7440u | (2 * h + 1));
+              float lo, hi;
+              ptx::dequant_pair(b0, b1, sc2, lo, hi);
+              outw[2 * wd + h] = kBf16 ? ptx::pack_bf16x2(lo, hi) : ptx::pack_f16x2(lo, hi);
+            }
+          }
+          uint8_t *dst_row = base + w * C::kABytes + r * C::kRowBytes;
+          const int sw = (r >> 1) & 3;
+          *reinterpret_cast<uint4 *>(dst_row + (((2 * half) ^ sw) << 4)) =
+              make_uint4(outw[0], outw[1], outw[2], outw[3]);
+          *reinterpret_cast<uint4 *>(dst_row + (((2 * half + 1) ^ sw) << 4)) =
+              make_uint4(outw[4], outw[5], outw[6], outw[7]);
+        }
+        ptx::fence_proxy_async_smem();
+        ptx::warp_arrive(&conv_full[stage]);
+        if (++stage == C::kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!ok) break;
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side: tensor maps and launches.
 // ---------------------------------------------------------------------------
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
@@ -2521,6 +2848,35 @@ int run_merge_quantize(const void *w, const void *lora_a, const void *lora_b, in
   return check_launch();
 }
 
+template <bool kBf16>
+int run_w8_swiglu(const void *x, const int8_t *g_codes, const float *g_scales,
+                  const int8_t *u_codes, const float *u_scales, void *y, int64_t m, int64_t k,
+                  int64_t n, cudaStream_t stream) {
+  using C = SwigluCfg;
+  unsigned *err = device_error_word();
+  if (err == nullptr) return record_cuda_error(cudaGetLastError());
+  CUtensorMap tm_x, tm_g, tm_u, tm_y;
+  int st = CF_OK;
+  if ((st = make_map(&tm_x, x, 2, k, m, C::kBKw, C::BT, true))) return st;
+  if ((st = make_map(&tm_g, g_codes, 1, k, n, C::kBKw, kBM, false))) return st;
+  if ((st = make_map(&tm_u, u_codes, 1, k, n, C::kBKw, kBM, false))) return st;
+  if ((st = make_map(&tm_y, y, 2, n, m, kBM, 32, false))) return st;
+  SwigluParams p{};
+  p.M = static_cast<int>(m);
+  p.N = static_cast<int>(n);
+  p.num_kb = static_cast<int>(k / C::kBKw);
+  p.kb_per_row = static_cast<int>(k / kQuantBlockSize);
+  p.g_scales = g_scales;
+  p.u_scales = u_scales;
+  p.n_tiles_w = static_cast<int>((n + kBM - 1) / kBM);
+  p.n_tiles = p.n_tiles_w * static_cast<int>((m + C::BT - 1) / C::BT);
+  p.err = err;
+  if ((st = allow_dynamic_smem<w8_swiglu_kernel<kBf16>>(C::kSmemBytes))) return st;
+  const int grid = std::max(1, std::min(p.n_tiles, sm_count()));
+  w8_swiglu_kernel<kBf16><<<grid, C::kThreads, C::kSmemBytes, stream>>>(tm_x, tm_g, tm_u, tm_y, p);
+  return check_launch();
+}
+
 int validate_and_run(const LinearArgs &L, cf_stream_t stream) {
   if (L.m < 0 || L.k < 0 || L.n < 0 || L.r < 0) return CF_ERR_INVALID_ARGUMENT;
   if (L.m == 0 || L.n == 0) return CF_OK;
@@ -2873,4 +3229,29 @@ int cf_lora_merge_quantize_int8(const void *w, const void *lora_a, const void *l
                                              scales, s)
              : cfb::run_merge_quantize<false>(w, lora_a, lora_b, n, k, rank, scaling, codes,
                                               scales, s);
+}
+
+int cf_w8_swiglu_int8(const void *x, const int8_t *gate_codes, const float *gate_scales,
+                      const int8_t *up_codes, const float *up_scales, void *y, int64_t m,
+                      int64_t k, int64_t n, int dtype, cf_stream_t stream) {
+  if (m < 0 || k < 0 || n < 0) return CF_ERR_INVALID_ARGUMENT;
+  if (m == 0 || n == 0) return CF_OK;
+  if (x == nullptr || gate_codes == nullptr || gate_scales == nullptr || up_codes == nullptr ||
+      up_scales == nullptr || y == nullptr) {
+    return CF_ERR_INVALID_ARGUMENT;
+  }
+  if (dtype != CF_DTYPE_BF16 && dtype != CF_DTYPE_F16) return CF_ERR_UNSUPPORTED;
+  if (k == 0 || k % cfb::kQuantBlockSize != 0 || n % 8 != 0) return CF_ERR_UNSUPPORTED;
+  if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX) return CF_ERR_UNSUPPORTED;
+  for (const void *ptr : {x, static_cast<const void *>(gate_codes),
+                          static_cast<const void *>(up_codes), static_cast<const void *>(y)}) {
+    if (!cfb::aligned_to(ptr, 16)) return CF_ERR_MISALIGNED;
+  }
+  if (!cfb::aligned_to(gate_scales, 4) || !cfb::aligned_to(up_scales, 4)) return CF_ERR_MISALIGNED;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  return dtype == CF_DTYPE_BF16
+             ? cfb::run_w8_swiglu<true>(x, gate_codes, gate_scales, up_codes, up_scales, y, m, k,
+                                        n, s)
+             : cfb::run_w8_swiglu<false>(x, gate_codes, gate_scales, up_codes, up_scales, y, m,
+                                         k, n, s);
 }

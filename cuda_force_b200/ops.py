@@ -240,6 +240,52 @@ def lora_merge_quantize_int8(
     return codes, scales
 
 
+def w8_swiglu_int8(
+    x: torch.Tensor,
+    gate_codes: torch.Tensor,
+    gate_scales: torch.Tensor,
+    up_codes: torch.Tensor,
+    up_scales: torch.Tensor,
+) -> torch.Tensor:
+    """``swiglu(x @ Wg.T, x @ Wu.T)`` for block-INT8 gate and up weights, in one kernel.
+
+    ``gate_codes`` / ``up_codes`` are int8 ``[intermediate, hidden]`` (what
+    :func:`quantize_int8` returns for the nn.Linear weights) with their 1-D
+    float32 scales; ``x [..., hidden]`` is float16 or bfloat16. Matches
+    ``swiglu(gate(x), up(x))`` of the reference's transformer block
+    (examples/transformer_block.py:84-87) with the projections rounded to
+    x's dtype; only the activated ``[..., intermediate]`` output is written.
+    """
+    import ctypes
+
+    from cuda_force_b200 import _abi
+
+    if gate_codes.dim() != 2 or up_codes.shape != gate_codes.shape:
+        raise ValueError("gate_codes and up_codes must both be [intermediate, hidden], got "
+                         f"{tuple(gate_codes.shape)} and {tuple(up_codes.shape)}")
+    n, k = gate_codes.shape
+    if x.shape[-1] != k:
+        raise ValueError(f"x has {x.shape[-1]} input features but the weights expect {k}")
+    expected = n * k // QUANT_BLOCK_SIZE
+    if k % QUANT_BLOCK_SIZE or gate_scales.numel() != expected or up_scales.numel() != expected:
+        raise ValueError(f"expected {expected} block scales per weight and hidden a multiple of "
+                         f"{QUANT_BLOCK_SIZE}")
+    if x.dtype not in (torch.float16, torch.bfloat16):
+        raise ValueError("w8_swiglu_int8 takes float16 or bfloat16 activations")
+    _require("w8_swiglu_int8", x, gate_codes, gate_scales, up_codes, up_scales)
+    x2, lead = _flatten_tokens(x)
+    m = x2.shape[0]
+    y = torch.empty(m, n, dtype=x.dtype, device=x.device)
+    dtype = _abi.CF_DTYPE_BF16 if x.dtype == torch.bfloat16 else _abi.CF_DTYPE_F16
+    p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    gc, uc = gate_codes.contiguous(), up_codes.contiguous()
+    gs, us = gate_scales.contiguous().reshape(-1), up_scales.contiguous().reshape(-1)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)
+    _abi.check(_abi.load().cf_w8_swiglu_int8(p(x2), p(gc), p(gs), p(uc), p(us), p(y), m, k, n,
+                                             dtype, stream), "cf_w8_swiglu_int8")
+    return y.reshape(*lead, n)
+
+
 def quantization_error(x: torch.Tensor) -> torch.Tensor:
     """Maximum absolute round-trip error of int8 quantisation (<= scale / 2 per block)."""
     quantised, scales = quantize_int8(x)

@@ -217,6 +217,21 @@ CF_API int cf_lora_merge_quantize_int8(const void *w, const void *lora_a, const 
                                        int dtype, int8_t *codes, float *scales,
                                        cf_stream_t stream);
 
+/* The gate and up projections of a LLaMA MLP with SwiGLU fused:
+ *   y[m, n] = silu(g) * u,  g = x gate_W^T,  u = x up_W^T
+ * with block-INT8 weights (gate_codes / up_codes int8 [n, k], scales float
+ * [n * k / 64], as cf_quantize_int8 produces them from nn.Linear weights) and
+ * x, y of `dtype` (f16 or bf16). g and u are rounded to `dtype` as the two
+ * projections' outputs would be, silu(v) = v / (1 + exp(-v)) and the product
+ * are computed in fp32 and rounded once; only y is written. Replaces
+ * gate(x), up(x), swiglu(gate, up) of the reference's transformer block
+ * (examples/transformer_block.py:84-87; swiglu: cuda/src/activations.cu:68-76,
+ * python/cudaforge/ops.py:407-440). Requirements: k % 64 == 0, n % 8 == 0,
+ * pointers 16-byte aligned (scales 4). */
+CF_API int cf_w8_swiglu_int8(const void *x, const int8_t *gate_codes, const float *gate_scales,
+                             const int8_t *up_codes, const float *up_scales, void *y, int64_t m,
+                             int64_t k, int64_t n, int dtype, cf_stream_t stream);
+
 /* Allocation-free form of cf_lora_linear, for callers that cannot allocate the
  * workspace: hosts whose device memory is reserved up front by another
  * allocator, foreign-language hosts without a CUDA allocator, and loops that
