@@ -2070,7 +2070,7 @@ __global__ void __launch_bounds__(MergeCfg::kThreads, 1)
 // feature row f of both accumulators, so silu(g) * u needs no exchange; the
 // result goes out through the staged TMA-store path. Only h reaches memory.
 //   warp 0 TMA producer, warp 1 TMEM owner + MMA issuer, warps 4-7 epilogue,
-//   warps 8-15 converters.
+//   warps 8-23 converters.
 // ---------------------------------------------------------------------------
 struct SwigluCfg {
   static constexpr int BT = 256;                       // tokens per tile
@@ -2084,7 +2084,10 @@ struct SwigluCfg {
   static constexpr int kStages = 5;
   static constexpr int kSlabBytes = 32 * kBM * 2;      // 32 tokens x 128 features
   static constexpr int kStagingBytes = 2 * kSlabBytes;
-  static constexpr int kThreads = 512;
+  // Sixteen converter warps (warps 8-23), eight per weight tile: each stage
+  // carries two code tiles, so conversion is what bounds this kernel.
+  static constexpr int kConvWarps = 16;
+  static constexpr int kThreads = (kConvWarp0 + kConvWarps) * kWarp;  // 768
   static constexpr int kTmemCols = 512;                // g: 0-255, u: 256-511
   static constexpr size_t kSmemBytes =
       1024 + static_cast<size_t>(kStages) * kStageBytes + kStagingBytes + 256;
@@ -2135,7 +2138,7 @@ __global__ void __launch_bounds__(SwigluCfg::kThreads, 1)
     for (int s = 0; s < C::kStages; ++s) {
       ptx::mbar_init(&full[s], 1);
       ptx::mbar_init(&empty[s], 1);
-      ptx::mbar_init(&conv_full[s], kConvThreads / kWarp);
+      ptx::mbar_init(&conv_full[s], C::kConvWarps);
     }
     ptx::mbar_init(tmem_full, 1);
     ptx::mbar_init(tmem_empty, 4);
@@ -2252,18 +2255,20 @@ __global__ void __launch_bounds__(SwigluCfg::kThreads, 1)
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
 #pragma unroll 1
       for (int c = 0; c < BT / 32; ++c) {
-        uint32_t g[32], u[32];
-        ptx::tmem_ld_32x32b_x32(t_row + c * 32, g);
-        ptx::tmem_ld_32x32b_x32(t_row + BT + c * 32, u);
-        ptx::tmem_ld_wait();
         // Stage a 32-token x 128-feature slab (token-major) and let the TMA
         // engine store it; the slab buffer is double-buffered against the
         // store still reading it.
         if (elected) ptx::bulk_wait_read<1>();
         ptx::named_bar_sync(1, 4 * kWarp);
         uint16_t *stg = reinterpret_cast<uint16_t *>(staging + (slab & 1) * C::kSlabBytes);
+#pragma unroll 1
+        for (int hh = 0; hh < 2; ++hh) {  // 16 tokens at a time keeps registers low
+        uint32_t g[32], u[32];
+        ptx::tmem_ld_32x32b_x16(t_row + c * 32 + hh * 16, g);
+        ptx::tmem_ld_32x32b_x16(t_row + BT + c * 32 + hh * 16, u);
+        ptx::tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 32; j += 2) {
+        for (int j = 0; j < 16; j += 2) {
           // The projections' outputs in the activation dtype ...
           const uint32_t gp = kBf16 ? ptx::pack_bf16x2(__uint_as_float(g[j]), __uint_as_float(g[j + 1]))
                                     : ptx::pack_f16x2(__uint_as_float(g[j]), __uint_as_float(g[j + 1]));
@@ -2287,8 +2292,10 @@ __global__ void __launch_bounds__(SwigluCfg::kThreads, 1)
           const float h0 = g0 / (1.0f + __expf(-g0)) * u0;
           const float h1 = g1 / (1.0f + __expf(-g1)) * u1;
           const uint32_t hp = kBf16 ? ptx::pack_bf16x2(h0, h1) : ptx::pack_f16x2(h0, h1);
-          stg[j * kBM + row] = static_cast<uint16_t>(hp & 0xffffu);
-          stg[(j + 1) * kBM + row] = static_cast<uint16_t>(hp >> 16);
+          const int t = hh * 16 + j;
+          stg[t * kBM + row] = static_cast<uint16_t>(hp & 0xffffu);
+          stg[(t + 1) * kBM + row] = static_cast<uint16_t>(hp >> 16);
+        }
         }
         ptx::fence_proxy_async_smem();
         ptx::named_bar_sync(1, 4 * kWarp);
@@ -2304,26 +2311,25 @@ __global__ void __launch_bounds__(SwigluCfg::kThreads, 1)
     if (elected) ptx::bulk_wait_all();  // stores finish reading shared memory before exit
   } else if (warp >= kConvWarp0) {
     // ------------------------------------------------------------------ converters
-    // Lane l of converter warp cw: row cw * 16 + l / 2, 16-code half l % 2 of
-    // the 32-code row, for the gate tile and then the up tile; writes 32
-    // bytes of each 64-byte swizzled bf16 row (logical 16-byte chunk c sits
-    // at c ^ ((row >> 1) & 3)).
+    // Converter warp cw handles weight tile wt = cw / 8 (0 gate, 1 up); its
+    // lane l takes row (cw % 8) * 16 + l / 2, 16-code half l % 2 of the
+    // 32-code row, and writes 32 bytes of the 64-byte swizzled bf16 row
+    // (logical 16-byte chunk c sits at c ^ ((row >> 1) & 3)).
     const int cw = warp - kConvWarp0;
-    const int r = cw * 16 + lane / 2;
+    const int wt = cw / 8;
+    const int r = (cw % 8) * 16 + lane / 2;
     const int half = lane & 1;
     int stage = 0;
     uint32_t phase = 0;
     for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x) {
       const int w0 = (tile % p.n_tiles_w) * kBM;
       const int n = w0 + r;
-      const float *srow[2] = {
-          n < p.N ? p.g_scales + static_cast<int64_t>(n) * p.kb_per_row : nullptr,
-          n < p.N ? p.u_scales + static_cast<int64_t>(n) * p.kb_per_row : nullptr};
+      const float *srow =
+          n < p.N ? (wt == 0 ? p.g_scales : p.u_scales) + static_cast<int64_t>(n) * p.kb_per_row
+                  : nullptr;
       bool ok = true;
       for (int it = 0; it < p.num_kb; ++it) {
-        float sc[2];
-#pragma unroll
-        for (int w = 0; w < 2; ++w) sc[w] = srow[w] != nullptr ? __ldg(srow[w] + it / 2) : 0.0f;
+        const float sc = srow != nullptr ? __ldg(srow + it / 2) : 0.0f;
         const bool got = ptx::mbar_wait(&full[stage], phase);
         if (__any_sync(0xffffffffu, !got)) {
           if (lane == 0) record_timeout(p.err, abort_flag);
@@ -2332,12 +2338,12 @@ __global__ void __launch_bounds__(SwigluCfg::kThreads, 1)
         }
         uint8_t *base = smem + stage * C::kStageBytes;
         const uint8_t *raw = base + 2 * C::kABytes + C::kXBytes;
-#pragma unroll
-        for (int w = 0; w < 2; ++w) {
+        {
+          const int w = wt;
           const uint4 codes =
               *reinterpret_cast<const uint4 *>(raw + w * C::kRawBytes + r * C::kBKw + half * 16);
           const uint32_t words[4] = {codes.x, codes.y, codes.z, codes.w};
-          const uint64_t sc2 = ptx::splat_f32x2(sc[w]);
+          const uint64_t sc2 = ptx::splat_f32x2(sc);
           uint32_t outw[8];
 #pragma unroll
           for (int wd = 0; wd < 4; ++wd) {
