@@ -2055,9 +2055,9 @@ __global__ void __launch_bounds__(MergeCfg::kThreads, 1)
 
 // ---------------------------------------------------------------------------
 // W8 gate and up projections of a LLaMA MLP with the SwiGLU fused into the
-// epilogue (SURVEY row "SwiGLU after the up-projection"; the reference's
-// examples/transformer_block.py:70-89 computes swiglu(gate(x), up(x)), and its
-// cuda/src/activations.cu:19-21, 68-76 defines silu(x) = x / (1 + exp(-x))):
+// epilogue (the reference's examples/transformer_block.py:70-89 computes
+// swiglu(gate(x), up(x)), and its cuda/src/activations.cu:19-21, 68-76
+// defines silu(x) = x / (1 + exp(-x))):
 //   h[t, f] = silu(g) * u,  g = round(x Wg^T)[t, f],  u = round(x Wu^T)[t, f]
 // with g and u rounded to the activation dtype as the two projections' outputs
 // would be, and h computed in fp32 and rounded once.
