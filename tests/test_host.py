@@ -109,6 +109,58 @@ def test_lora_abi_validates_shapes_and_workspace():
                               _abi.CF_DTYPE_BF16, f, ws, None) == _abi.CF_OK      # empty
 
 
+def test_newer_entry_points_validate_before_touching_the_device():
+    # Every rejected call returns before any CUDA call, so this runs on a CPU
+    # host; a call that passed validation would need a GPU and is not made.
+    lib = _abi.load()
+    f = ctypes.c_void_p(0x1000)
+    odd = ctypes.c_void_p(0x1004)
+    # fp32 matmul: k and n in whole 16-byte rows, 16-byte alignment, layouts
+    assert lib.cf_matmul_f32(f, f, 0, f, 64, 64, 66, 1, None) == _abi.CF_ERR_UNSUPPORTED
+    assert lib.cf_matmul_f32(f, f, 0, f, 64, 62, 64, 1, None) == _abi.CF_ERR_UNSUPPORTED
+    assert lib.cf_matmul_f32(odd, f, 0, f, 64, 64, 64, 1, None) == _abi.CF_ERR_MISALIGNED
+    assert lib.cf_matmul_f32(f, f, 7, f, 64, 64, 64, 1, None) == _abi.CF_ERR_INVALID_ARGUMENT
+    assert lib.cf_matmul_f32(f, f, 0, f, 0, 64, 64, 1, None) == _abi.CF_OK    # empty
+    # merge + quantise: 16-bit dtypes, whole 64-element blocks, ranks 16/32/64
+    merge = lambda n, k, r, dt, w=f: lib.cf_lora_merge_quantize_int8(  # noqa: E731
+        w, f, f, n, k, r, 2.0, dt, f, f, None)
+    assert merge(64, 100, 16, _abi.CF_DTYPE_BF16) == _abi.CF_ERR_UNSUPPORTED
+    assert merge(64, 128, 24, _abi.CF_DTYPE_BF16) == _abi.CF_ERR_UNSUPPORTED
+    assert merge(64, 128, 16, _abi.CF_DTYPE_F32) == _abi.CF_ERR_UNSUPPORTED
+    assert merge(64, 128, 16, _abi.CF_DTYPE_BF16, odd) == _abi.CF_ERR_MISALIGNED
+    assert merge(-1, 128, 16, _abi.CF_DTYPE_BF16) == _abi.CF_ERR_INVALID_ARGUMENT
+    assert merge(0, 128, 16, _abi.CF_DTYPE_BF16) == _abi.CF_OK
+    # W8 gate/up + SwiGLU: 16-bit activations, k % 64, n % 8, alignment
+    swiglu = lambda m, k, n, dt, x=f: lib.cf_w8_swiglu_int8(  # noqa: E731
+        x, f, f, f, f, f, m, k, n, dt, None)
+    assert swiglu(32, 100, 128, _abi.CF_DTYPE_BF16) == _abi.CF_ERR_UNSUPPORTED
+    assert swiglu(32, 128, 100, _abi.CF_DTYPE_BF16) == _abi.CF_ERR_UNSUPPORTED
+    assert swiglu(32, 128, 128, _abi.CF_DTYPE_F32) == _abi.CF_ERR_UNSUPPORTED
+    assert swiglu(32, 128, 128, _abi.CF_DTYPE_BF16, odd) == _abi.CF_ERR_MISALIGNED
+    assert lib.cf_w8_swiglu_int8(f, None, f, f, f, f, 32, 128, 128, _abi.CF_DTYPE_BF16,
+                                 None) == _abi.CF_ERR_INVALID_ARGUMENT
+    assert swiglu(0, 128, 128, _abi.CF_DTYPE_BF16) == _abi.CF_OK
+
+
+def test_python_wrappers_validate_shapes_on_the_host():
+    w = torch.zeros(64, 100, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="multiple of 64"):
+        cf.lora_merge_quantize_int8(w, torch.zeros(4, 100, dtype=torch.bfloat16),
+                                    torch.zeros(64, 4, dtype=torch.bfloat16), 1.0)
+    with pytest.raises(ValueError, match="lora_b must be"):
+        cf.lora_merge_quantize_int8(torch.zeros(64, 128, dtype=torch.bfloat16),
+                                    torch.zeros(4, 128, dtype=torch.bfloat16),
+                                    torch.zeros(64, 5, dtype=torch.bfloat16), 1.0)
+    codes = torch.zeros(128, 256, dtype=torch.int8)
+    scales = torch.ones(128 * 256 // 64)
+    with pytest.raises(ValueError, match="input features"):
+        cf.w8_swiglu_int8(torch.zeros(2, 128, dtype=torch.bfloat16), codes, scales, codes, scales)
+    with pytest.raises(ValueError, match="float32"):
+        cf.matmul_f32(torch.zeros(4, 8, dtype=torch.bfloat16), torch.zeros(8, 4))
+    with pytest.raises(ValueError, match=r"\[m, k\] and b \[k, n\]"):
+        cf.matmul_f32(torch.zeros(4, 8), torch.zeros(9, 4))
+
+
 def test_dispatcher_schemas_match_the_reference():
     # Byte-identical to reference cpp/src/bindings.cpp:344,352-353.
     expected = {
