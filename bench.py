@@ -6,7 +6,7 @@
 Multi-GPU: launched by torchrun (one rank per GPU, NCCL); RANK / LOCAL_RANK /
 WORLD_SIZE come from the environment. Rank 0 prints one JSON line.
 
-Default workload ``llama7b_stack_quant`` = BASELINE config 2: block-INT8
+Default workload ``llama7b_stack_quant`` = benchmark config 2: block-INT8
 quantisation of a Llama-2-7B-shaped bf16 weight stack (32 layers x [4 x
 4096x4096, 2 x 11008x4096, 4096x11008], N(0, 0.02) with 0.1% of entries x20),
 block 64 along the input dimension, layers sharded across ranks with no
@@ -14,7 +14,7 @@ communication ("strong" scaling: the stack is fixed, each rank quantises
 32/N layers). Metric: aggregate algorithmic GB/s = 3.0625 B/element (2 B bf16
 read, 1 B code + 4/64 B scale written) x elements / max-over-ranks time.
 
-Other workloads (``--workload``) time the remaining BASELINE configs for the
+Other workloads (``--workload``) time the remaining benchmark configs for the
 design notes; the driver's default line is config 2.
 
 Timing rules: W >= 3 warm-up steps; the timed region is K steps bracketed by a
@@ -173,7 +173,7 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------
-# Workload: BASELINE config 2 (Llama-2-7B stack, bf16, layer-sharded quantise)
+# Workload: benchmark config 2 (Llama-2-7B stack, bf16, layer-sharded quantise)
 # ---------------------------------------------------------------------------
 LLAMA7B_LAYER = [(4096, 4096)] * 4 + [(11008, 4096)] * 2 + [(4096, 11008)]
 LLAMA7B_LAYERS = 32
@@ -212,7 +212,7 @@ class LlamaStackQuant:
 
     def config(self) -> dict:
         return {
-            "workload": "BASELINE config 2: Llama-2-7B bf16 weight stack block-INT8 quantise",
+            "workload": "benchmark config 2: Llama-2-7B bf16 weight stack block-INT8 quantise",
             "layers": self.n_layers,
             "layer_shapes": [list(s) for s in LLAMA7B_LAYER],
             "block": 64,
@@ -343,7 +343,7 @@ def reference_quantize_fn():
 
 
 class Config1Quant:
-    """fp32 [4096, 4096] N(0,1) block-INT8 quantise (or dequantise)."""
+    """benchmark config 1: fp32 [4096, 4096] N(0,1) block-INT8 quantise (or dequantise)."""
 
     name = "config1_quant_f32"
     unit = "GB/s"
@@ -361,10 +361,10 @@ class Config1Quant:
         self.kernel = "dequantize_vec_kernel" if self.dequant else "quantize_tma_kernel<f32>"
 
     def config(self) -> dict:
-        return {"workload": (f"BASELINE config 1: fp32 [4096,4096] N(0,1) block-64 "
+        return {"workload": (f"benchmark config 1: fp32 [4096,4096] N(0,1) block-64 "
                              f"{'dequantise' if self.dequant else 'quantise'}")
                 if self.rows == 4096 else
-                f"config 1 kernel at [{self.rows},4096] fp32 (size study, not a BASELINE config)",
+                f"config 1 kernel at [{self.rows},4096] fp32 (size study, not a benchmark config)",
                 "block": 64, "bytes_per_element": 4 + 1 + 4 / 64,
                 "l2": "flushed between steps (256 MiB write outside the timed events)",
                 "parallelism": f"{self.dist.world} independent replica(s)"}
@@ -473,7 +473,7 @@ def timed_e2e(wl, one_step, steps: int, h2d: int, d2h: int, api: str) -> dict:
 
 
 class LoraLinear:
-    """BASELINE config 3 (bf16 LoRA linear) and config 4 (W8 + LoRA, decode / prefill)."""
+    """benchmark config 3 (bf16 LoRA linear) and config 4 (W8 + LoRA, decode / prefill)."""
 
     name = "lora_bf16_8192x4096x4096"
     unit = "TFLOP/s"
@@ -615,7 +615,7 @@ class LoraLinear:
 
 
 class W8Decode(LoraLinear):
-    """BASELINE config 4 decode: W8 + LoRA, x [32, 4096], W [11008, 4096] int8."""
+    """benchmark config 4 decode: W8 + LoRA, x [32, 4096], W [11008, 4096] int8."""
 
     name = "w8_lora_decode_32x4096x11008"
     unit = "GB/s"
@@ -626,7 +626,7 @@ class W8Decode(LoraLinear):
 
 
 class W8Prefill(LoraLinear):
-    """BASELINE config 4 prefill: W8 + LoRA, x [4096, 4096], W [11008, 4096] int8."""
+    """benchmark config 4 prefill: W8 + LoRA, x [4096, 4096], W [11008, 4096] int8."""
 
     name = "w8_lora_prefill_4096x4096x11008"
     m, k, n, r = 4096, 4096, 11008, 16
@@ -635,7 +635,7 @@ class W8Prefill(LoraLinear):
 
 
 class LoraF32(LoraLinear):
-    """fp32 LoRA linear (the reference's own CUDA dtype), BASELINE config 3 shapes."""
+    """fp32 LoRA linear (the reference's own CUDA dtype), benchmark config 3 shapes."""
 
     name = "lora_f32_8192x4096x4096"
     main_kernel = "lora_f32_kernel (three tf32 products)"
@@ -909,7 +909,7 @@ class W8SwiGLU:
 
 
 class W8ColumnSharded:
-    """column-sharded W8 + LoRA on a Llama-70B MLP shape + NCCL all-gather."""
+    """benchmark config 5: column-sharded W8 + LoRA on a Llama-70B MLP shape + NCCL all-gather."""
 
     name = "w8_lora_70b_colshard_16384x8192x28672"
     unit = "TFLOP/s"
@@ -1227,7 +1227,7 @@ def main() -> None:
     parser.add_argument("--workload", choices=sorted(WORKLOADS), default=LlamaStackQuant.name)
     parser.add_argument("--e2e-steps", type=int, default=2)
     parser.add_argument("--layers", type=int, default=LLAMA7B_LAYERS,
-                        help="stack depth (default 32 = BASELINE config 2; smaller only "
+                        help="stack depth (default 32 = benchmark config 2; smaller only "
                              "for profiling captures)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--elements", type=int, default=0,

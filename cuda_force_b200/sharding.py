@@ -1,8 +1,8 @@
 """Multi-GPU layouts of the hot path (one process per GPU, torch.distributed).
 
-* Layer-sharded quantisation: independent layers are dealt
+* Layer-sharded quantisation (benchmark config 2): independent layers are dealt
   round-robin to ranks; no communication.
-* Column-sharded W8 + LoRA linear: rank g owns output
+* Column-sharded W8 + LoRA linear (benchmark config 5): rank g owns output
   features [g*N/G, (g+1)*N/G) — its rows of the int8 weight and their scales,
   and the matching columns of the adapter's B — while x and A are replicated.
   Each rank computes its slice y_g = x W_g^T + scale (x A) B_g, and the slices
@@ -11,7 +11,7 @@
 
 The reference has no multi-GPU path for these ops (its only NCCL use is a DDP
 training example, examples/distributed_train.py:82); the sharding follows the
-north-star configuration, not reference code.
+benchmark configuration, not reference code.
 """
 
 from __future__ import annotations

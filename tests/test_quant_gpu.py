@@ -2,7 +2,7 @@
 
 Bit-exact against the golden fixtures (generated from the reference) and the
 oracle, through both the C ABI (ctypes, raw pointers) and the dispatcher ops;
-size-independent properties at BASELINE sizes; edge cases the reference tests
+size-independent properties at the benchmark sizes; edge cases the reference tests
 (tests/python/test_ops.py:164-228, tests/cuda/test_quantization.cu:55-158).
 """
 
@@ -138,7 +138,7 @@ def test_misaligned_views_take_the_scalar_path_correctly(offset, cuda_device):
 
 def test_round_trip_bound_and_range_at_config1_size(cuda_device):
     # Size-independent properties (reference test_ops.py:174-187,
-    # test_quantization.cu:62-121) at BASELINE config 1's size.
+    # test_quantization.cu:62-121) at benchmark config 1's size.
     g = torch.Generator(device=cuda_device).manual_seed(11)
     x = torch.randn(4096, 4096, device=cuda_device, generator=g)
     codes, scales = cf.quantize_int8(x)
@@ -179,7 +179,7 @@ def test_grouped_quantisation_equals_single_calls(cuda_device):
 
 
 def test_llama_layer_bf16_matches_oracle_bit_exact(cuda_device):
-    # One Llama-2-7B layer of BASELINE config 2 (7 projections, N(0,0.02),
+    # One Llama-2-7B layer of benchmark config 2 (7 projections, N(0,0.02),
     # 0.1% outliers x20, bf16), grouped launch, checked block for block.
     g = torch.Generator(device=cuda_device).manual_seed(1234)
     shapes = [(4096, 4096)] * 4 + [(11008, 4096)] * 2 + [(4096, 11008)]

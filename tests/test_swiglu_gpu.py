@@ -4,7 +4,7 @@ Oracle: the reference's transformer-block composition on the CPU
 (examples/transformer_block.py:84-87): g = x @ dequantize(Wg).T and
 u = x @ dequantize(Wu).T rounded to x's dtype, then silu(g) * u with
 silu(v) = v / (1 + exp(-v)) (cuda/src/activations.cu:19-21) in fp32, rounded
-once. Bar: max|h - ref| / max|ref| <= 1e-2, inside BASELINE's 2e-2: the two
+once. Bar: max|h - ref| / max|ref| <= 1e-2, inside the path's 2e-2 tolerance: the two
 products accumulate in fp32 in a different order, which can move g or u by one
 ulp of the dtype before h is rounded again (measured up to ~1.5 bf16 ulps of
 the largest output, 6.6e-3).
