@@ -808,6 +808,100 @@ class MergeQuant:
                 f"quantize_int8")
 
 
+class ResidualRMSNorm:
+    """Residual add + RMSNorm before a LLaMA-7B projection (fused_residual_rmsnorm)."""
+
+    name = "residual_rmsnorm_16384x4096_bf16"
+    unit = "GB/s"
+    bound = "hbm"
+    scaling = "weak"
+    flush_l2 = True
+    rows, cols, eps = 16384, 4096, 1e-6
+    kernel = "residual_rmsnorm_vec_kernel<bf16, bf16, 2>"
+    dtype = "bf16 (fp32 sum of squares)"
+    metric = "residual add + RMSNorm GB/s (x, residual [16384,4096] bf16)"
+
+    def __init__(self, dist: Dist, _layers: int = 0):
+        self.dist = dist
+
+    def bytes(self) -> float:
+        # x and residual read, normalised and residual_out written; weight once
+        return self.rows * self.cols * 2 * 4 + self.cols * 2
+
+    def config(self) -> dict:
+        return {"workload": self.__doc__.strip() + f" [{self.name}]", "rows": self.rows,
+                "cols": self.cols, "eps": self.eps,
+                "values": "x, residual N(0,1); weight 1 + N(0,0.1)",
+                "l2": "flushed between steps (256 MiB write outside the timed events)",
+                "parallelism": f"{self.dist.world} independent replica(s)"}
+
+    def setup(self) -> None:
+        from cuda_force_b200 import _abi
+
+        dev = self.dist.device
+        g = torch.Generator(device=dev).manual_seed(11)
+        shape = (self.rows, self.cols)
+        self.x = torch.randn(shape, device=dev, generator=g).to(torch.bfloat16)
+        self.r = torch.randn(shape, device=dev, generator=g).to(torch.bfloat16)
+        self.w = (1 + 0.1 * torch.randn(self.cols, device=dev, generator=g)).to(torch.bfloat16)
+        self.out = torch.empty_like(self.x)
+        self.summed = torch.empty_like(self.x)
+        self.lib = _abi.load()
+        self.work_per_step = self.bytes()
+        self.launches_per_step = 1
+
+    def step(self, stream) -> None:
+        from cuda_force_b200 import _abi
+
+        st = self.lib.cf_fused_residual_rmsnorm(
+            self.x.data_ptr(), self.r.data_ptr(), self.w.data_ptr(), _abi.CF_DTYPE_BF16,
+            self.out.data_ptr(), self.summed.data_ptr(), self.rows, self.cols, self.eps,
+            _abi.CF_DTYPE_BF16, stream.cuda_stream)
+        _abi.check(st, self.name)
+
+    def verify(self) -> None:
+        summed = self.x + self.r
+        assert torch.equal(self.summed, summed), f"{self.name}: residual_out differs"
+        f = summed.float()
+        ref = (f * torch.rsqrt(f.pow(2).mean(-1, keepdim=True) + self.eps) * self.w.float())
+        err = ((self.out.float() - ref).abs() / ref.abs().clamp_min(1e-30)).max().item()
+        assert err <= 2.0 ** -7, f"{self.name}: normalised error {err}"
+
+    def e2e(self, steps: int) -> dict:
+        import cuda_force_b200 as cf
+
+        dev = self.dist.device
+        hx, hr = self.x.cpu().pin_memory(), self.r.cpu().pin_memory()
+        ho, hs = torch.empty_like(hx).pin_memory(), torch.empty_like(hx).pin_memory()
+
+        def one():
+            x = hx.to(dev, non_blocking=True)
+            r = hr.to(dev, non_blocking=True)
+            out, summed = cf.fused_residual_rmsnorm(x, r, self.w, self.eps)
+            ho.copy_(out, non_blocking=True)
+            hs.copy_(summed, non_blocking=True)
+
+        return timed_e2e(self, one, steps, 2 * hx.numel() * 2, 2 * ho.numel() * 2,
+                         "cuda_force_b200.fused_residual_rmsnorm (weight resident, x and "
+                         "residual in, normalised and residual_out out)")
+
+    def cpu_sample(self):
+        from oracle import build_ref
+
+        rows = 2048
+        x, r, w = self.x[:rows].cpu(), self.r[:rows].cpu(), self.w.cpu()
+        if build_ref.load():
+            fn = lambda: torch.ops.cudaforge_ref.fused_residual_rmsnorm(x, r, w, self.eps)  # noqa: E731
+            kind = "reference"
+        else:
+            from oracle import norm_ref
+
+            fn = lambda: norm_ref.fused_residual_rmsnorm(x, r, w, self.eps)  # noqa: E731
+            kind = "port"
+        return (fn, self.work_per_step * rows / self.rows, kind,
+                f"{rows} of {self.rows} rows through the reference's CPU fused_residual_rmsnorm")
+
+
 class W8SwiGLU:
     """LLaMA MLP gate + up projections with block-INT8 weights and SwiGLU fused."""
 
@@ -1061,7 +1155,7 @@ class W8ColumnSharded:
 
 WORKLOADS = {w.name: w for w in (LlamaStackQuant, Config1Quant, Config1Dequant, LoraLinear,
                                 W8Decode, W8Prefill, W8ColumnSharded, LoraF32, MergeQuant,
-                                W8SwiGLU)}
+                                W8SwiGLU, ResidualRMSNorm)}
 
 
 # ---------------------------------------------------------------------------

@@ -10,6 +10,7 @@ from cuda_force_b200.ops import (
     QUANT_BLOCK_SIZE,
     backend_report,
     dequantize_int8,
+    fused_residual_rmsnorm,
     kernel_supports,
     lora_linear,
     lora_linear_int8,
@@ -19,6 +20,7 @@ from cuda_force_b200.ops import (
     quantize_dequantize,
     quantize_int8,
     quantize_int8_many,
+    rmsnorm,
     w8_swiglu_int8,
 )
 
@@ -31,6 +33,7 @@ __all__ = [
     "__version__",
     "backend_report",
     "dequantize_int8",
+    "fused_residual_rmsnorm",
     "kernel_supports",
     "lora_linear",
     "lora_linear_int8",
@@ -40,5 +43,6 @@ __all__ = [
     "quantize_dequantize",
     "quantize_int8",
     "quantize_int8_many",
+    "rmsnorm",
     "w8_swiglu_int8",
 ]

@@ -70,6 +70,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "cf_matmul_f32": (_int, [_p, _p, _int, _p, _i64, _i64, _i64, _int, _p]),
     "cf_w8_swiglu_int8": (_int, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p]),
+    "cf_fused_residual_rmsnorm": (
+        _int, [_p, _p, _p, _int, _p, _p, _i64, _i64, ctypes.c_float, _int, _p]),
     "cf_lora_merge_quantize_int8": (
         _int, [_p, _p, _p, _i64, _i64, _i64, ctypes.c_float, _int, _p, _p, _p]),
     "cf_lora_linear_noalloc": (

@@ -25,7 +25,7 @@ INCLUDE = ROOT / "include"
 LIB = PKG / "libcudaforge_b200.so"
 SHIM = PKG / "_C.so"
 
-CUDA_SOURCES = ["abi.cu", "quant.cu", "lora_gemm.cu"]
+CUDA_SOURCES = ["abi.cu", "quant.cu", "lora_gemm.cu", "norm.cu"]
 HEADERS = ["quant_math.cuh", "cf_common.cuh", "ptx.cuh"]
 
 NVCC_FLAGS = [

@@ -268,6 +268,57 @@ at::Tensor lora_linear_int8_cuda(const at::Tensor &x, const at::Tensor &w_codes,
   return y;
 }
 
+// Reference shapes (cpp/src/bindings.cpp:65-80, 129-151): 2-D rows x cols,
+// weight [cols]. Any float dtype here (the reference kernels are fp32 only);
+// the weight is of x's dtype or float32, as the reference composition's
+// weight.float() allows. Outputs: normalised (and the rounded sum).
+void check_norm_args(const at::Tensor &x, const at::Tensor &weight, const char *xname) {
+  check_cuda(x, xname);
+  check_cuda(weight, "weight");
+  TORCH_CHECK(x.dim() == 2, xname, " must be 2-D, got ", x.dim(), " dimensions");
+  check_contiguous(x, xname);
+  check_contiguous(weight, "weight");
+  TORCH_CHECK(weight.dim() == 1 && weight.size(0) == x.size(1), "weight must be 1-D of length ",
+              x.size(1), ", got ", weight.sizes());
+  TORCH_CHECK(weight.scalar_type() == x.scalar_type() || weight.scalar_type() == at::kFloat,
+              "weight must be float32 or of ", xname, "'s dtype");
+  TORCH_CHECK(weight.device() == x.device(), "weight must be on ", xname, "'s device");
+}
+
+at::Tensor rmsnorm_cuda(const at::Tensor &input, const at::Tensor &weight, double eps) {
+  check_norm_args(input, weight, "input");
+  const int dtype = dtype_code(input, "input");
+  const c10::cuda::CUDAGuard guard(input.device());
+  at::Tensor out = at::empty_like(input);
+  check_status(cf_fused_residual_rmsnorm(input.data_ptr(), nullptr, weight.data_ptr(),
+                                         dtype_code(weight, "weight"), out.data_ptr(), nullptr,
+                                         input.size(0), input.size(1), static_cast<float>(eps),
+                                         dtype, current_stream()),
+               "rmsnorm");
+  return out;
+}
+
+std::vector<at::Tensor> fused_residual_rmsnorm_cuda(const at::Tensor &x, const at::Tensor &residual,
+                                                    const at::Tensor &weight, double eps) {
+  check_norm_args(x, weight, "x");
+  check_cuda(residual, "residual");
+  check_contiguous(residual, "residual");
+  TORCH_CHECK(x.sizes() == residual.sizes(), "x and residual must have the same shape, got ",
+              x.sizes(), " and ", residual.sizes());
+  TORCH_CHECK(residual.scalar_type() == x.scalar_type(), "x and residual must share one dtype");
+  TORCH_CHECK(residual.device() == x.device(), "residual must be on x's device");
+  const int dtype = dtype_code(x, "x");
+  const c10::cuda::CUDAGuard guard(x.device());
+  at::Tensor out = at::empty_like(x);
+  at::Tensor summed = at::empty_like(x);
+  check_status(cf_fused_residual_rmsnorm(x.data_ptr(), residual.data_ptr(), weight.data_ptr(),
+                                         dtype_code(weight, "weight"), out.data_ptr(),
+                                         summed.data_ptr(), x.size(0), x.size(1),
+                                         static_cast<float>(eps), dtype, current_stream()),
+               "fused_residual_rmsnorm");
+  return {out, summed};
+}
+
 }  // namespace
 
 TORCH_LIBRARY(cudaforge, m) {
@@ -275,6 +326,11 @@ TORCH_LIBRARY(cudaforge, m) {
   m.def("lora_linear(Tensor x, Tensor w, Tensor a, Tensor b, float scale) -> Tensor");
   m.def("quantize_int8(Tensor input) -> Tensor[]");
   m.def("dequantize_int8(Tensor quantised, Tensor scales) -> Tensor");
+  // Byte-identical to the reference (cpp/src/bindings.cpp:343, 349-351).
+  m.def("rmsnorm(Tensor input, Tensor weight, float eps) -> Tensor");
+  m.def(
+      "fused_residual_rmsnorm(Tensor x, Tensor residual, Tensor weight, float eps) "
+      "-> Tensor[]");
   // Additive.
   m.def(
       "lora_linear_int8(Tensor x, Tensor w_codes, Tensor w_scales, Tensor a, Tensor b, "
@@ -285,7 +341,8 @@ TORCH_LIBRARY(cudaforge, m) {
 
 TORCH_LIBRARY_IMPL(cudaforge, Autograd, m) {
   for (const char *name : {"lora_linear", "quantize_int8", "dequantize_int8", "lora_linear_int8",
-                           "quantize_dequantize", "quantize_int8_many"}) {
+                           "quantize_dequantize", "quantize_int8_many", "rmsnorm",
+                           "fused_residual_rmsnorm"}) {
     m.impl(name, torch::autograd::autogradNotImplementedFallback());
   }
 }
@@ -297,4 +354,6 @@ TORCH_LIBRARY_IMPL(cudaforge, CUDA, m) {
   m.impl("lora_linear_int8", &lora_linear_int8_cuda);
   m.impl("quantize_dequantize", &quantize_dequantize_cuda);
   m.impl("quantize_int8_many", &quantize_int8_many_cuda);
+  m.impl("rmsnorm", &rmsnorm_cuda);
+  m.impl("fused_residual_rmsnorm", &fused_residual_rmsnorm_cuda);
 }

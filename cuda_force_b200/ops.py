@@ -19,6 +19,9 @@ three differences that are deliberate:
   the reference's layout or as the transpose of a contiguous tensor (the
   nn.Linear / ``training/lora.py`` storage), without copying.
 
+``rmsnorm`` and ``fused_residual_rmsnorm`` (ops.py:248-275, :335-382) keep
+the reference's names, arguments and messages and take all three dtypes.
+
 Additive ops: ``lora_linear_int8`` (W as block-INT8 codes + scales),
 ``quantize_dequantize`` (fake quantisation) and ``quantize_int8_many``.
 """
@@ -147,6 +150,54 @@ def quantize_int8_many(tensors: list[torch.Tensor]) -> list[tuple[torch.Tensor, 
     _require("quantize_int8_many", *tensors)
     flat = torch.ops.cudaforge.quantize_int8_many([t.contiguous() for t in tensors])
     return [(flat[2 * i], flat[2 * i + 1]) for i in range(len(tensors))]
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """Root-mean-square normalisation over the last dimension.
+
+    ``x * rsqrt(mean(x^2) + eps) * weight`` in fp32, rounded once to x's dtype
+    (reference ops.py:164-171, :248-275). ``x`` is ``[..., hidden]``; ``weight``
+    is ``[hidden]`` of x's dtype or float32.
+    """
+    if weight.ndim != 1:
+        raise ValueError(f"weight must be 1-D, got shape {tuple(weight.shape)}")
+    if x.shape[-1] != weight.shape[0]:
+        raise ValueError(
+            f"weight length {weight.shape[0]} does not match the last dimension "
+            f"of x, which is {x.shape[-1]}"
+        )
+    if x.numel() == 0:
+        return x.clone()
+    _require("rmsnorm", x, weight)
+    rows = x.contiguous().view(-1, x.shape[-1])
+    return torch.ops.cudaforge.rmsnorm(rows, weight.contiguous(), float(eps)).view(x.shape)
+
+
+def fused_residual_rmsnorm(
+    x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Residual add followed by RMSNorm, in one pass over the rows.
+
+    Returns ``(normalised, residual_out)`` with ``residual_out = x + residual``
+    rounded to x's dtype and ``normalised = rmsnorm(residual_out, weight, eps)``
+    (reference ops.py:188-192, :335-382). ``x`` and ``residual`` share a shape
+    ``[..., hidden]`` and dtype; ``weight`` is ``[hidden]``.
+    """
+    if x.shape != residual.shape:
+        raise ValueError(
+            f"x and residual must have the same shape, got {tuple(x.shape)} "
+            f"and {tuple(residual.shape)}"
+        )
+    if weight.ndim != 1 or weight.shape[0] != x.shape[-1]:
+        raise ValueError(f"weight must be 1-D of length {x.shape[-1]}, got {tuple(weight.shape)}")
+    if x.numel() == 0:
+        return x.clone(), residual.clone()
+    _require("fused_residual_rmsnorm", x, residual, weight)
+    hidden = x.shape[-1]
+    normalised, summed = torch.ops.cudaforge.fused_residual_rmsnorm(
+        x.contiguous().view(-1, hidden), residual.contiguous().view(-1, hidden),
+        weight.contiguous(), float(eps))
+    return normalised.view(x.shape), summed.view(x.shape)
 
 
 def matmul_f32(a: torch.Tensor, b: torch.Tensor, precise: bool = True) -> torch.Tensor:

@@ -232,6 +232,23 @@ CF_API int cf_w8_swiglu_int8(const void *x, const int8_t *gate_codes, const floa
                              const int8_t *up_codes, const float *up_scales, void *y, int64_t m,
                              int64_t k, int64_t n, int dtype, cf_stream_t stream);
 
+/* Residual add + RMSNorm over rows of length cols (rows x cols, contiguous):
+ *   residual_out = x + residual                 (rounded to dtype)
+ *   output = residual_out * rsqrt(mean(residual_out^2) + eps) * weight
+ * (fp32 arithmetic, rounded once to dtype). Replaces the reference's
+ * fused_residual_rmsnorm (cpp/src/bindings.cpp:129-151,
+ * cuda/include/cudaforge/fused_norm.cuh; semantics python/cudaforge/ops.py:
+ * 164-171, 188-192), which runs fp32 only; here dtype is f32, bf16 or f16 and
+ * weight [cols] is of dtype or f32 (weight_dtype). residual and residual_out
+ * both NULL give the reference's rmsnorm (cpp/src/bindings.cpp:65-80): output =
+ * x * rsqrt(mean(x^2) + eps) * weight. output may alias x and residual_out may
+ * alias residual. Any alignment works; 16-byte aligned pointers and rows of a
+ * whole number of 16-byte chunks take the vector path. */
+CF_API int cf_fused_residual_rmsnorm(const void *x, const void *residual, const void *weight,
+                                     int weight_dtype, void *output, void *residual_out,
+                                     int64_t rows, int64_t cols, float eps, int dtype,
+                                     cf_stream_t stream);
+
 /* Allocation-free form of cf_lora_linear, for callers that cannot allocate the
  * workspace: hosts whose device memory is reserved up front by another
  * allocator, foreign-language hosts without a CUDA allocator, and loops that

@@ -11,6 +11,8 @@ use it, and only as the checker or the timed CPU baseline.
   ``_build/``), a second independent checker used on large inputs.
 * ``linear_ref`` — fp32/fp64 restatement of the LoRA linear
   (python/cudaforge/ops.py:178-185, cpp/src/bindings.cpp:255-258).
+* ``norm_ref``   — torch restatement of RMSNorm and residual add + RMSNorm
+  (python/cudaforge/ops.py:164-171, 188-192, cpp/src/bindings.cpp:238-271).
 * ``build_ref``  — compiles the reference's own CPU operators
   (cpp/src/bindings.cpp) into ``_ref/`` as ``torch.ops.cudaforge_ref.*``.
 

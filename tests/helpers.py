@@ -35,6 +35,24 @@ def golden_cases() -> dict[str, dict[str, np.ndarray | str]]:
     return cases
 
 
+def norm_cases() -> dict[str, dict]:
+    """Residual-add + RMSNorm fixtures as torch tensors (CPU), with eps and dtypes."""
+    data = np.load(GOLDEN / "norm_cases.npz")
+    meta = json.loads(str(data["__meta__"]))
+    cases = {}
+    for name, m in meta.items():
+        tag, wtag = m["dtype"], m["weight_dtype"]
+        cases[name] = {
+            "dtype": DTYPE_TAG_TO_TORCH[tag],
+            "eps": m["eps"],
+            "x": numpy_to_torch(tag, data[f"{name}/x"]),
+            "residual": numpy_to_torch(tag, data[f"{name}/residual"]),
+            "weight": numpy_to_torch(wtag, data[f"{name}/weight"]),
+            **{k: numpy_to_torch(tag, data[f"{name}/{k}"]) for k in ("normalised", "summed", "plain")},
+        }
+    return cases
+
+
 def golden_hashes() -> dict[str, dict]:
     return json.loads((GOLDEN / "quant_hashes.json").read_text())
 

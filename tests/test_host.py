@@ -140,6 +140,19 @@ def test_newer_entry_points_validate_before_touching_the_device():
     assert lib.cf_w8_swiglu_int8(f, None, f, f, f, f, 32, 128, 128, _abi.CF_DTYPE_BF16,
                                  None) == _abi.CF_ERR_INVALID_ARGUMENT
     assert swiglu(0, 128, 128, _abi.CF_DTYPE_BF16) == _abi.CF_OK
+    # residual add + RMSNorm: sizes, dtypes, residual / residual_out together
+    norm = lambda rows, cols, dt, wdt, r=f, ro=f, x=f: lib.cf_fused_residual_rmsnorm(  # noqa: E731
+        x, r, f, wdt, f, ro, rows, cols, 1e-6, dt, None)
+    bf16 = _abi.CF_DTYPE_BF16
+    assert norm(-1, 64, bf16, bf16) == _abi.CF_ERR_INVALID_ARGUMENT
+    assert norm(4, -1, bf16, bf16) == _abi.CF_ERR_INVALID_ARGUMENT
+    assert norm(4, 64, 7, 7) == _abi.CF_ERR_UNSUPPORTED
+    assert norm(4, 64, bf16, _abi.CF_DTYPE_F16) == _abi.CF_ERR_UNSUPPORTED
+    assert norm(4, 64, bf16, bf16, ro=None) == _abi.CF_ERR_INVALID_ARGUMENT
+    assert norm(4, 64, bf16, bf16, x=None) == _abi.CF_ERR_INVALID_ARGUMENT
+    assert norm(1 << 40, 1 << 20, bf16, bf16) == _abi.CF_ERR_INVALID_ARGUMENT
+    assert norm(0, 64, bf16, bf16) == _abi.CF_OK
+    assert norm(4, 0, bf16, bf16) == _abi.CF_OK
 
 
 def test_python_wrappers_validate_shapes_on_the_host():
@@ -159,14 +172,29 @@ def test_python_wrappers_validate_shapes_on_the_host():
         cf.matmul_f32(torch.zeros(4, 8, dtype=torch.bfloat16), torch.zeros(8, 4))
     with pytest.raises(ValueError, match=r"\[m, k\] and b \[k, n\]"):
         cf.matmul_f32(torch.zeros(4, 8), torch.zeros(9, 4))
+    # rmsnorm / fused_residual_rmsnorm: the reference's messages (ops.py:260-266, :361-367)
+    with pytest.raises(ValueError, match="weight must be 1-D"):
+        cf.rmsnorm(torch.zeros(2, 8), torch.zeros(2, 8))
+    with pytest.raises(ValueError, match="does not match the last dimension"):
+        cf.rmsnorm(torch.zeros(2, 8), torch.zeros(9))
+    with pytest.raises(ValueError, match="same shape"):
+        cf.fused_residual_rmsnorm(torch.zeros(2, 8), torch.zeros(3, 8), torch.zeros(8))
+    with pytest.raises(ValueError, match="1-D of length 8"):
+        cf.fused_residual_rmsnorm(torch.zeros(2, 8), torch.zeros(2, 8), torch.zeros(7))
+    empty = torch.zeros(0, 8)
+    assert cf.rmsnorm(empty, torch.ones(8)).shape == (0, 8)
+    assert [t.shape for t in cf.fused_residual_rmsnorm(empty, empty, torch.ones(8))] == [(0, 8)] * 2
 
 
 def test_dispatcher_schemas_match_the_reference():
-    # Byte-identical to reference cpp/src/bindings.cpp:344,352-353.
+    # Byte-identical to reference cpp/src/bindings.cpp:343-344,349-353.
     expected = {
         "lora_linear": "cudaforge::lora_linear(Tensor x, Tensor w, Tensor a, Tensor b, float scale) -> Tensor",
         "quantize_int8": "cudaforge::quantize_int8(Tensor input) -> Tensor[]",
         "dequantize_int8": "cudaforge::dequantize_int8(Tensor quantised, Tensor scales) -> Tensor",
+        "rmsnorm": "cudaforge::rmsnorm(Tensor input, Tensor weight, float eps) -> Tensor",
+        "fused_residual_rmsnorm": ("cudaforge::fused_residual_rmsnorm(Tensor x, Tensor residual, "
+                                   "Tensor weight, float eps) -> Tensor[]"),
     }
     for name, schema in expected.items():
         assert str(getattr(torch.ops.cudaforge, name).default._schema) == schema

@@ -10,8 +10,8 @@ import numpy as np
 import pytest
 import torch
 
-from oracle import linear_ref, quant_ref
-from tests.helpers import golden_cases, golden_hashes, regenerate, sha
+from oracle import linear_ref, norm_ref, quant_ref
+from tests.helpers import golden_cases, norm_cases, golden_hashes, regenerate, sha
 
 CASES = golden_cases()
 
@@ -82,3 +82,15 @@ def test_linear_oracle_int8_uses_dequantised_weight():
                                          torch.from_numpy(scales))
     assert wt.shape == (128, 32)
     assert (wt.t() - w).abs().max().item() <= scales.max() / 2 + 1e-9
+
+
+@pytest.mark.parametrize("name", sorted(norm_cases()))
+def test_norm_oracle_matches_reference_fixture(name):
+    # Bit for bit: the fixture came from the reference's composition and its
+    # compiled CPU operators (which agreed bit for bit when it was made).
+    case = norm_cases()[name]
+    normalised, summed = norm_ref.fused_residual_rmsnorm(case["x"], case["residual"],
+                                                         case["weight"], case["eps"])
+    plain = norm_ref.rmsnorm(case["x"], case["weight"], case["eps"])
+    for got, key in ((normalised, "normalised"), (summed, "summed"), (plain, "plain")):
+        assert torch.equal(got, case[key]), key
