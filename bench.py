@@ -53,6 +53,37 @@ def load_peaks() -> tuple[dict, str]:
     return dict(FALLBACK_PEAKS), "fallback"
 
 
+def size_matched_copy(nbytes: float, device, flush, steps: int = 10) -> dict | None:
+    """A plain torch copy that moves the same bytes as one step, timed like the step.
+
+    Half of ``nbytes`` is read and half written, with the same L2 flush before
+    each launch and CUDA events around it: the best a copy kernel reaches at
+    this size, where launch and ramp-up latency weigh on a short launch.
+    """
+    half = int(nbytes // 2) // 16 * 16
+    if half <= 0 or nbytes > 4e9:
+        return None
+    src = torch.empty(half, dtype=torch.uint8, device=device).fill_(1)
+    dst = torch.empty_like(src)
+    for _ in range(3):
+        dst.copy_(src)
+    times = []
+    for i in range(steps):
+        if flush is not None:
+            flush.fill_(i & 0xFF)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        dst.copy_(src)
+        end.record()
+        end.synchronize()
+        times.append(start.elapsed_time(end))
+    ms = statistics.median(times)
+    del src, dst
+    return {"gbs": round(2 * half / (ms * 1e-3) / 1e9, 1), "us": round(ms * 1e3, 2),
+            "what": f"torch copy_ of {2 * half / 1e6:.1f} MB (half read, half written), same "
+                    f"L2 flush, median of {steps}"}
+
+
 def load_traffic() -> dict:
     path = ROOT / "profiles" / "traffic.json"
     return json.loads(path.read_text()) if path.exists() else {}
@@ -1222,6 +1253,7 @@ def run_ours(args, dist: Dist) -> dict | None:
     traffic_info = load_traffic().get(wl.name)
     traffic = traffic_info.get("dram_bytes_per_step") if traffic_info else None
 
+    copy_ref = size_matched_copy(wl.work_per_step, dist.device, flush) if wl.bound == "hbm" else None
     e2e = wl.e2e(max(1, min(args.steps, args.e2e_steps)))
 
     cpu = None
@@ -1255,6 +1287,7 @@ def run_ours(args, dist: Dist) -> dict | None:
             "traffic": traffic,
             "algorithmic_per_launch_step": wl.work_per_step,
             "launches_per_step": wl.launches_per_step,
+            **({"size_matched_copy": copy_ref} if copy_ref else {}),
         },
         "e2e": e2e,
         "gpu_launches": wl.launches_per_step * args.steps,
