@@ -269,9 +269,10 @@ at::Tensor lora_linear_int8_cuda(const at::Tensor &x, const at::Tensor &w_codes,
 }
 
 // Reference shapes (cpp/src/bindings.cpp:65-80, 129-151): 2-D rows x cols,
-// weight [cols]. Any float dtype here (the reference kernels are fp32 only);
-// the weight is of x's dtype or float32, as the reference composition's
-// weight.float() allows. Outputs: normalised (and the rounded sum).
+// weight [cols]. Any float dtype here (the reference kernels are fp32 only).
+// The kernels read the weight in x's dtype or in float32; a weight of another
+// float dtype is widened to float32 first, which is exactly the reference
+// composition's weight.float(). Outputs: normalised (and the rounded sum).
 void check_norm_args(const at::Tensor &x, const at::Tensor &weight, const char *xname) {
   check_cuda(x, xname);
   check_cuda(weight, "weight");
@@ -280,18 +281,23 @@ void check_norm_args(const at::Tensor &x, const at::Tensor &weight, const char *
   check_contiguous(weight, "weight");
   TORCH_CHECK(weight.dim() == 1 && weight.size(0) == x.size(1), "weight must be 1-D of length ",
               x.size(1), ", got ", weight.sizes());
-  TORCH_CHECK(weight.scalar_type() == x.scalar_type() || weight.scalar_type() == at::kFloat,
-              "weight must be float32 or of ", xname, "'s dtype");
+  dtype_code(weight, "weight");
   TORCH_CHECK(weight.device() == x.device(), "weight must be on ", xname, "'s device");
+}
+
+at::Tensor kernel_weight(const at::Tensor &weight, const at::Tensor &x) {
+  if (weight.scalar_type() == x.scalar_type() || weight.scalar_type() == at::kFloat) return weight;
+  return weight.to(at::kFloat);
 }
 
 at::Tensor rmsnorm_cuda(const at::Tensor &input, const at::Tensor &weight, double eps) {
   check_norm_args(input, weight, "input");
   const int dtype = dtype_code(input, "input");
   const c10::cuda::CUDAGuard guard(input.device());
+  const at::Tensor w = kernel_weight(weight, input);
   at::Tensor out = at::empty_like(input);
-  check_status(cf_fused_residual_rmsnorm(input.data_ptr(), nullptr, weight.data_ptr(),
-                                         dtype_code(weight, "weight"), out.data_ptr(), nullptr,
+  check_status(cf_fused_residual_rmsnorm(input.data_ptr(), nullptr, w.data_ptr(),
+                                         dtype_code(w, "weight"), out.data_ptr(), nullptr,
                                          input.size(0), input.size(1), static_cast<float>(eps),
                                          dtype, current_stream()),
                "rmsnorm");
@@ -309,10 +315,11 @@ std::vector<at::Tensor> fused_residual_rmsnorm_cuda(const at::Tensor &x, const a
   TORCH_CHECK(residual.device() == x.device(), "residual must be on x's device");
   const int dtype = dtype_code(x, "x");
   const c10::cuda::CUDAGuard guard(x.device());
+  const at::Tensor w = kernel_weight(weight, x);
   at::Tensor out = at::empty_like(x);
   at::Tensor summed = at::empty_like(x);
-  check_status(cf_fused_residual_rmsnorm(x.data_ptr(), residual.data_ptr(), weight.data_ptr(),
-                                         dtype_code(weight, "weight"), out.data_ptr(),
+  check_status(cf_fused_residual_rmsnorm(x.data_ptr(), residual.data_ptr(), w.data_ptr(),
+                                         dtype_code(w, "weight"), out.data_ptr(),
                                          summed.data_ptr(), x.size(0), x.size(1),
                                          static_cast<float>(eps), dtype, current_stream()),
                "fused_residual_rmsnorm");

@@ -157,7 +157,7 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.T
 
     ``x * rsqrt(mean(x^2) + eps) * weight`` in fp32, rounded once to x's dtype
     (reference ops.py:164-171, :248-275). ``x`` is ``[..., hidden]``; ``weight``
-    is ``[hidden]`` of x's dtype or float32.
+    is ``[hidden]`` of any float dtype (read as float32, like the reference).
     """
     if weight.ndim != 1:
         raise ValueError(f"weight must be 1-D, got shape {tuple(weight.shape)}")

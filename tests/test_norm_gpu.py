@@ -140,3 +140,19 @@ def test_torch_op_matches_reference_schema_outputs(cuda_device):
     assert bits_equal(out[1], ref_sum)
     assert_one_step(out[0], ref_norm)
     assert_one_step(torch.ops.cudaforge.rmsnorm(x, w, 1e-6), norm_ref.rmsnorm(x, w, 1e-6))
+
+
+@pytest.mark.parametrize(("dtype", "wdtype"), [
+    (torch.float32, torch.bfloat16),
+    (torch.bfloat16, torch.float16),
+])
+def test_norm_weight_of_another_dtype_is_widened(dtype, wdtype, cuda_device):
+    # The reference composition multiplies by weight.float() whatever its dtype.
+    x = torch.randn(19, 768, device=cuda_device).to(dtype)
+    r = torch.randn_like(x)
+    w = (1 + 0.1 * torch.randn(768, device=cuda_device)).to(wdtype)
+    normalised, summed = cf.fused_residual_rmsnorm(x, r, w)
+    ref_norm, ref_sum = norm_ref.fused_residual_rmsnorm(x, r, w, 1e-6)
+    assert bits_equal(summed, ref_sum)
+    assert_one_step(normalised, ref_norm)
+    assert_one_step(cf.rmsnorm(x, w), norm_ref.rmsnorm(x, w, 1e-6))
