@@ -93,7 +93,10 @@ def build_shim(force: bool = False) -> Path:
     deps = [src, INCLUDE / "cudaforge_b200.h", LIB, Path(__file__)]
     if not force and not _stale(SHIM, deps):
         return SHIM
-    include_dirs = cpp_extension.include_paths() + [str(_cuda_home() / "include"), str(INCLUDE)]
+    import sysconfig
+
+    include_dirs = cpp_extension.include_paths() + [
+        str(_cuda_home() / "include"), str(INCLUDE), sysconfig.get_paths()["include"]]
     torch_lib = Path(torch.__file__).resolve().parent / "lib"
     abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
     tmp = SHIM.with_suffix(".so.tmp")

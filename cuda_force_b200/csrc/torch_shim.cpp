@@ -1,15 +1,27 @@
-// PyTorch dispatcher shim over the C ABI.
+// PyTorch dispatcher shim over the C ABI, loadable as the reference's
+// `cudaforge._C` extension module.
 //
-// Registers the reference's operator schemas in the `cudaforge` namespace
-// (reference cpp/src/bindings.cpp:342-355), byte-identical for the three
-// hot-path ops, plus three additive ops. Only the CUDA key has kernels: there
-// is deliberately no CPU implementation, so a CPU tensor fails loudly in the
-// dispatcher instead of taking a silent host path. The Autograd key raises
+// Registers all ten of the reference's operator schemas in the `cudaforge`
+// namespace, byte-identical (reference cpp/src/bindings.cpp:342-355), plus
+// additive ops. For the five on the accelerated path (quantize_int8,
+// dequantize_int8, lora_linear, rmsnorm, fused_residual_rmsnorm) the CUDA key
+// runs this build's sm_100a kernels through the C ABI; the other five keep the
+// reference's semantics as ATen compositions (see below). The Autograd key raises
 // (autogradNotImplementedFallback), as the reference does (bindings.cpp:369-377).
 //
-// Each impl validates like the reference's CUDA impl (TORCH_CHECK messages that
-// name the operand), allocates its outputs on the input's device, and launches
-// on PyTorch's current stream.
+// CPU tensors: the reference's extension registers ATen CPU kernels for its
+// schemas (bindings.cpp:379-390), and its Python wrapper sends CPU tensors to
+// them (python/cudaforge/ops.py:150-152). The five reference schemas keep that
+// contract here with ATen compositions of the reference semantics, so callers
+// of the reference that pass host tensors still work. The dispatcher selects
+// the kernel by the tensors' device: a CUDA tensor never reaches these, and
+// this package's own Python API refuses host tensors before dispatching.
+//
+// Each CUDA impl validates like the reference's CUDA impl (TORCH_CHECK
+// messages that name the operand), allocates its outputs on the input's
+// device, and launches on PyTorch's current stream.
+#include <Python.h>
+
 #include <ATen/ATen.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
@@ -326,18 +338,100 @@ std::vector<at::Tensor> fused_residual_rmsnorm_cuda(const at::Tensor &x, const a
   return {out, summed};
 }
 
+// ---- host tensors: the reference semantics (python/cudaforge/ops.py:164-240)
+
+std::vector<at::Tensor> quantize_int8_host(const at::Tensor &input) {
+  at::Tensor flat = input.reshape({-1}).to(at::kFloat);
+  const int64_t count = flat.numel();
+  const int64_t pad = cf_quant_scale_count(count) * CF_QUANT_BLOCK_SIZE - count;
+  if (pad > 0) flat = at::constant_pad_nd(flat, {0, pad});
+  const at::Tensor blocks = flat.view({-1, CF_QUANT_BLOCK_SIZE});
+  at::Tensor scales = blocks.abs().amax(1) / 127.0;
+  scales = at::where(scales > 0, scales, at::ones_like(scales));
+  const at::Tensor codes = at::clamp(at::round(blocks / scales.unsqueeze(1)), -127, 127);
+  return {codes.reshape({-1}).narrow(0, 0, count).to(at::kChar).view(input.sizes()), scales};
+}
+
+at::Tensor dequantize_int8_host(const at::Tensor &quantised, const at::Tensor &scales) {
+  const int64_t count = quantised.numel();
+  TORCH_CHECK(scales.numel() == cf_quant_scale_count(count), "expected ",
+              cf_quant_scale_count(count), " block scales, got ", scales.numel());
+  const int64_t pad = scales.numel() * CF_QUANT_BLOCK_SIZE - count;
+  at::Tensor flat = quantised.reshape({-1}).to(at::kFloat);
+  if (pad > 0) flat = at::constant_pad_nd(flat, {0, pad});
+  const at::Tensor values = flat.view({-1, CF_QUANT_BLOCK_SIZE}) * scales.to(at::kFloat).unsqueeze(1);
+  return values.reshape({-1}).narrow(0, 0, count).view(quantised.sizes());
+}
+
+at::Tensor lora_linear_host(const at::Tensor &x, const at::Tensor &w, const at::Tensor &a,
+                            const at::Tensor &b, double scale) {
+  return at::matmul(x, w) + scale * at::matmul(at::matmul(x, a), b);
+}
+
+at::Tensor rmsnorm_host(const at::Tensor &input, const at::Tensor &weight, double eps) {
+  TORCH_CHECK(input.dim() == 2, "input must be 2-D, got ", input.dim(), " dimensions");
+  TORCH_CHECK(weight.size(0) == input.size(1), "weight length ", weight.size(0),
+              " does not match the input's last dimension ", input.size(1));
+  const at::Tensor f = input.to(at::kFloat);
+  const at::Tensor norm = f * at::rsqrt(f.pow(2).mean({-1}, /*keepdim=*/true) + eps);
+  return (norm * weight.to(at::kFloat)).to(input.scalar_type());
+}
+
+std::vector<at::Tensor> fused_residual_rmsnorm_host(const at::Tensor &x,
+                                                    const at::Tensor &residual,
+                                                    const at::Tensor &weight, double eps) {
+  TORCH_CHECK(x.sizes() == residual.sizes(), "x and residual must have the same shape, got ",
+              x.sizes(), " and ", residual.sizes());
+  const at::Tensor summed = x + residual;
+  return {rmsnorm_host(summed, weight, eps), summed};
+}
+
+// ---- the reference's other operators (not on the accelerated path)
+//
+// softmax, sum, silu, gelu and swiglu keep their schemas registered so the
+// reference package behaves the same with this extension installed
+// (python/cudaforge/ops.py probes each op by name and calls it for host and
+// device tensors alike). They are ATen compositions of the reference semantics
+// (cpp/src/bindings.cpp:250-295) on whichever device the tensors live.
+
+at::Tensor softmax_any(const at::Tensor &input) {
+  TORCH_CHECK(input.dim() == 2, "input must be 2-D, got ", input.dim(), " dimensions");
+  return at::softmax(input, -1);
+}
+
+at::Tensor sum_any(const at::Tensor &input) { return input.sum(); }
+
+at::Tensor silu_any(const at::Tensor &input) { return at::silu(input); }
+
+at::Tensor gelu_any(const at::Tensor &input) { return at::gelu(input, "tanh"); }
+
+at::Tensor swiglu_any(const at::Tensor &gate, const at::Tensor &up) {
+  TORCH_CHECK(gate.sizes() == up.sizes(), "gate and up must have the same shape, got ",
+              gate.sizes(), " and ", up.sizes());
+  const auto t = gate.scalar_type();
+  if (t != at::kHalf && t != at::kBFloat16) return at::silu(gate) * up;
+  // 16-bit inputs are computed in fp32 and rounded once.
+  return (at::silu(gate.to(at::kFloat)) * up.to(at::kFloat)).to(t);
+}
+
 }  // namespace
 
 TORCH_LIBRARY(cudaforge, m) {
-  // Byte-identical to the reference (cpp/src/bindings.cpp:344, 352-353).
+  // Byte-identical to the reference (cpp/src/bindings.cpp:345, 353-354).
   m.def("lora_linear(Tensor x, Tensor w, Tensor a, Tensor b, float scale) -> Tensor");
   m.def("quantize_int8(Tensor input) -> Tensor[]");
   m.def("dequantize_int8(Tensor quantised, Tensor scales) -> Tensor");
-  // Byte-identical to the reference (cpp/src/bindings.cpp:343, 349-351).
+  // Byte-identical to the reference (cpp/src/bindings.cpp:343, 350-352).
   m.def("rmsnorm(Tensor input, Tensor weight, float eps) -> Tensor");
   m.def(
       "fused_residual_rmsnorm(Tensor x, Tensor residual, Tensor weight, float eps) "
       "-> Tensor[]");
+  // The reference's remaining schemas (cpp/src/bindings.cpp:344, 346-349), byte-identical.
+  m.def("softmax(Tensor input) -> Tensor");
+  m.def("sum(Tensor input) -> Tensor");
+  m.def("silu(Tensor input) -> Tensor");
+  m.def("gelu(Tensor input) -> Tensor");
+  m.def("swiglu(Tensor gate, Tensor up) -> Tensor");
   // Additive.
   m.def(
       "lora_linear_int8(Tensor x, Tensor w_codes, Tensor w_scales, Tensor a, Tensor b, "
@@ -349,7 +443,8 @@ TORCH_LIBRARY(cudaforge, m) {
 TORCH_LIBRARY_IMPL(cudaforge, Autograd, m) {
   for (const char *name : {"lora_linear", "quantize_int8", "dequantize_int8", "lora_linear_int8",
                            "quantize_dequantize", "quantize_int8_many", "rmsnorm",
-                           "fused_residual_rmsnorm"}) {
+                           "fused_residual_rmsnorm", "softmax", "sum", "silu", "gelu",
+                           "swiglu"}) {
     m.impl(name, torch::autograd::autogradNotImplementedFallback());
   }
 }
@@ -364,3 +459,40 @@ TORCH_LIBRARY_IMPL(cudaforge, CUDA, m) {
   m.impl("rmsnorm", &rmsnorm_cuda);
   m.impl("fused_residual_rmsnorm", &fused_residual_rmsnorm_cuda);
 }
+
+TORCH_LIBRARY_IMPL(cudaforge, CompositeExplicitAutograd, m) {
+  m.impl("softmax", &softmax_any);
+  m.impl("sum", &sum_any);
+  m.impl("silu", &silu_any);
+  m.impl("gelu", &gelu_any);
+  m.impl("swiglu", &swiglu_any);
+}
+
+TORCH_LIBRARY_IMPL(cudaforge, CPU, m) {
+  m.impl("quantize_int8", &quantize_int8_host);
+  m.impl("dequantize_int8", &dequantize_int8_host);
+  m.impl("lora_linear", &lora_linear_host);
+  m.impl("rmsnorm", &rmsnorm_host);
+  m.impl("fused_residual_rmsnorm", &fused_residual_rmsnorm_host);
+}
+
+// `from cudaforge import _C` (python/cudaforge/ops.py:44-58) imports this file
+// as a Python extension module; loading it runs the registrations above.
+// cuda_kernels_available() answers as the reference's does (bindings.cpp:
+// 331-337): this build always has its CUDA kernels.
+namespace {
+
+PyObject *cuda_kernels_available(PyObject *, PyObject *) { Py_RETURN_TRUE; }
+
+PyMethodDef kModuleMethods[] = {
+    {"cuda_kernels_available", cuda_kernels_available, METH_NOARGS,
+     "True: the operators have sm_100a CUDA kernels."},
+    {nullptr, nullptr, 0, nullptr}};
+
+PyModuleDef kModuleDef = {PyModuleDef_HEAD_INIT, "_C",
+                          "cudaforge operators on sm_100a kernels (C-ABI shim)", -1,
+                          kModuleMethods};
+
+}  // namespace
+
+PyMODINIT_FUNC PyInit__C(void) { return PyModule_Create(&kModuleDef); }

@@ -9,12 +9,14 @@ import ctypes
 import re
 from pathlib import Path
 
+import numpy as np
 import pytest
 import torch
 
 import cuda_force_b200 as cf
 from cuda_force_b200 import _abi
 from cuda_force_b200 import ops
+from tests.helpers import golden_cases, norm_cases, numpy_to_torch
 
 ROOT = Path(__file__).resolve().parents[1]
 HEADER = ROOT / "include" / "cudaforge_b200.h"
@@ -187,24 +189,90 @@ def test_python_wrappers_validate_shapes_on_the_host():
 
 
 def test_dispatcher_schemas_match_the_reference():
-    # Byte-identical to reference cpp/src/bindings.cpp:343-344,349-353.
+    # All ten, byte-identical to reference cpp/src/bindings.cpp:342-355.
     expected = {
-        "lora_linear": "cudaforge::lora_linear(Tensor x, Tensor w, Tensor a, Tensor b, float scale) -> Tensor",
-        "quantize_int8": "cudaforge::quantize_int8(Tensor input) -> Tensor[]",
-        "dequantize_int8": "cudaforge::dequantize_int8(Tensor quantised, Tensor scales) -> Tensor",
         "rmsnorm": "cudaforge::rmsnorm(Tensor input, Tensor weight, float eps) -> Tensor",
+        "softmax": "cudaforge::softmax(Tensor input) -> Tensor",
+        "lora_linear": "cudaforge::lora_linear(Tensor x, Tensor w, Tensor a, Tensor b, float scale) -> Tensor",
+        "sum": "cudaforge::sum(Tensor input) -> Tensor",
+        "silu": "cudaforge::silu(Tensor input) -> Tensor",
+        "gelu": "cudaforge::gelu(Tensor input) -> Tensor",
+        "swiglu": "cudaforge::swiglu(Tensor gate, Tensor up) -> Tensor",
         "fused_residual_rmsnorm": ("cudaforge::fused_residual_rmsnorm(Tensor x, Tensor residual, "
                                    "Tensor weight, float eps) -> Tensor[]"),
+        "quantize_int8": "cudaforge::quantize_int8(Tensor input) -> Tensor[]",
+        "dequantize_int8": "cudaforge::dequantize_int8(Tensor quantised, Tensor scales) -> Tensor",
     }
     for name, schema in expected.items():
         assert str(getattr(torch.ops.cudaforge, name).default._schema) == schema
 
 
+def test_reference_side_operators_keep_their_semantics():
+    # softmax / sum / silu / gelu / swiglu are not accelerated here; they stay
+    # registered as compositions of the reference semantics (bindings.cpp:250-295).
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(4, 33, generator=g)
+    assert torch.equal(torch.ops.cudaforge.softmax(x), torch.softmax(x, -1))
+    assert torch.equal(torch.ops.cudaforge.sum(x), x.sum())
+    assert torch.equal(torch.ops.cudaforge.silu(x), torch.nn.functional.silu(x))
+    assert torch.equal(torch.ops.cudaforge.gelu(x), torch.nn.functional.gelu(x, approximate="tanh"))
+    gate, up = x.bfloat16(), torch.randn(4, 33, generator=g).bfloat16()
+    ref = (torch.nn.functional.silu(gate.float()) * up.float()).bfloat16()
+    assert torch.equal(torch.ops.cudaforge.swiglu(gate, up), ref)
+    with pytest.raises(RuntimeError, match="derivative for cudaforge::silu is not implemented"):
+        torch.ops.cudaforge.silu(x.requires_grad_()).sum().backward()
+
+
 def test_cpu_tensors_fail_loudly():
+    # This package's API never computes on the host.
     with pytest.raises(RuntimeError, match="CUDA"):
         cf.quantize_int8(torch.randn(128))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        cf.fused_residual_rmsnorm(torch.randn(2, 8), torch.randn(2, 8), torch.ones(8))
+    # Additive ops have no host kernel in the dispatcher either.
     with pytest.raises((RuntimeError, NotImplementedError)):
-        torch.ops.cudaforge.quantize_int8(torch.randn(128))
+        torch.ops.cudaforge.quantize_dequantize(torch.randn(128))
+
+
+def test_extension_imports_as_the_reference_module():
+    # python/cudaforge/ops.py:44-58 imports cudaforge._C and asks it whether
+    # CUDA kernels were compiled in.
+    import importlib
+
+    mod = importlib.import_module("cuda_force_b200._C")
+    assert mod.cuda_kernels_available() is True
+
+
+@pytest.mark.parametrize("name", sorted(golden_cases()))
+def test_dispatcher_host_kernels_match_reference_fixture(name):
+    # Reference callers may pass host tensors to the registered ops
+    # (python/cudaforge/ops.py:150-152); the host kernels keep the reference's
+    # results bit for bit.
+    case = golden_cases()[name]
+    x = numpy_to_torch(case["dtype"], case["input"])
+    codes, scales = torch.ops.cudaforge.quantize_int8(x)
+    assert np.array_equal(codes.reshape(-1).numpy(), case["codes"])
+    assert np.array_equal(scales.numpy().view(np.int32), case["scales"].view(np.int32))
+    deq = torch.ops.cudaforge.dequantize_int8(codes, scales)
+    assert np.array_equal(deq.reshape(-1).numpy(), case["deq"], equal_nan=True)
+
+
+@pytest.mark.parametrize("name", sorted(norm_cases()))
+def test_dispatcher_host_norm_matches_reference_fixture(name):
+    case = norm_cases()[name]
+    normalised, summed = torch.ops.cudaforge.fused_residual_rmsnorm(
+        case["x"], case["residual"], case["weight"], case["eps"])
+    assert torch.equal(normalised, case["normalised"]) and torch.equal(summed, case["summed"])
+    plain = torch.ops.cudaforge.rmsnorm(case["x"], case["weight"], case["eps"])
+    assert torch.equal(plain, case["plain"])
+
+
+def test_dispatcher_host_lora_linear_is_the_reference_composition():
+    g = torch.Generator().manual_seed(3)
+    x, w = torch.randn(7, 129, generator=g), torch.randn(129, 65, generator=g)
+    a, b = torch.randn(129, 3, generator=g), torch.randn(3, 65, generator=g)
+    y = torch.ops.cudaforge.lora_linear(x, w, a, b, 0.5)
+    assert torch.equal(y, x @ w + 0.5 * ((x @ a) @ b))
 
 
 @pytest.mark.parametrize(
