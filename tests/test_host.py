@@ -313,3 +313,19 @@ def test_autograd_inputs_are_rejected():
     x = torch.randn(4, 64, requires_grad=True)
     with pytest.raises(RuntimeError):
         cf.quantize_int8(x)
+
+
+def test_header_is_plain_c_and_links_from_c(tmp_path):
+    # A cgo / JNI / FFI binding sees the header as C: it must compile as
+    # pedantic C99 and link against the library with no C++ runtime in sight.
+    import subprocess
+
+    root = Path(__file__).resolve().parents[1]
+    exe = tmp_path / "abi_from_c"
+    lib_dir = root / "cuda_force_b200"
+    subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-Werror", "-pedantic",
+                    f"-I{root / 'include'}", str(root / "tests" / "native" / "abi_from_c.c"),
+                    "-o", str(exe), f"-L{lib_dir}", "-l:libcudaforge_b200.so",
+                    f"-Wl,-rpath,{lib_dir}"], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0 and out.stdout.strip() == "ok", out.stdout + out.stderr
