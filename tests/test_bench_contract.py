@@ -1,0 +1,57 @@
+"""bench.py's workload definitions, checked on the CPU.
+
+The roofline fractions and values are algorithmic work ÷ time, so the work per
+step must be the figure the benchmark configs define: bytes for the HBM-bound
+workloads, FLOPs for the tensor-bound ones. Each workload must also carry every
+field the JSON line reports.
+"""
+
+from __future__ import annotations
+
+import pytest
+
+import bench
+
+
+@pytest.fixture(scope="module")
+def dist():
+    return bench.Dist(1)
+
+
+def test_llama_stack_bytes(dist):
+    wl = bench.LlamaStackQuant(dist)
+    assert wl.elems_per_layer * bench.LLAMA7B_LAYERS == 6_476_005_376
+    assert bench.BYTES_PER_ELEM_BF16_QUANT * wl.elems_per_layer * 32 == 19_832_766_464
+
+
+def test_config1_bytes():
+    assert (4 + 1 + 4 / 64) * bench.CONFIG1_ROWS * 4096 == 84_934_656
+
+
+def test_linear_work(dist):
+    assert bench.LoraLinear(dist).flops() == 277_025_390_592
+    assert bench.W8Decode(dist).bytes() == 49_356_800
+    assert bench.W8Prefill(dist).flops() == 371_346_898_944
+    # 2MNK + 2·M·r·(K+N) for the 70B MLP shape: 7.774 TFLOP per call in total
+    assert bench.W8ColumnSharded(dist).flops() == pytest.approx(7.7739e12, rel=1e-4)
+
+
+def test_new_workload_bytes(dist):
+    assert bench.ResidualRMSNorm(dist).bytes() == 16384 * 4096 * 8 + 4096 * 2
+    assert bench.MergeQuant(dist).bytes() == 11008 * 4096 * (2 + 1 + 4 / 64) + 2 * 16 * (11008 + 4096)
+
+
+@pytest.mark.parametrize("name", sorted(bench.WORKLOADS))
+def test_every_workload_reports_the_contract_fields(name, dist):
+    wl = bench.WORKLOADS[name](dist, bench.LLAMA7B_LAYERS)
+    assert wl.name == name
+    assert wl.unit in ("GB/s", "TFLOP/s")
+    assert wl.bound in ("hbm", "tensor")
+    assert (wl.bound == "hbm") == (wl.unit == "GB/s")
+    assert wl.scaling in ("weak", "strong")
+    assert isinstance(wl.flush_l2, bool)
+    for field in ("metric", "dtype", "kernel"):
+        assert isinstance(getattr(wl, field), str) and getattr(wl, field)
+    cfg = wl.config()
+    assert isinstance(cfg.get("workload"), str) and cfg["workload"]
+    assert "l2" in cfg or not wl.flush_l2
