@@ -236,9 +236,9 @@ class LlamaStackQuant:
     def __init__(self, dist: Dist, n_layers: int = LLAMA7B_LAYERS):
         self.dist = dist
         self.n_layers = n_layers
-        from cuda_force_b200.sharding import layer_shard
-
-        self.layers = layer_shard(n_layers, dist.rank, dist.world)
+        # layers l with l % world == rank (cuda_force_b200.sharding.layer_shard), computed here
+        # so that building the workload imports nothing of the package (the reference arm).
+        self.layers = list(range(dist.rank, n_layers, dist.world))
         self.elems_per_layer = sum(a * b for a, b in LLAMA7B_LAYER)
 
     def config(self) -> dict:
@@ -253,10 +253,16 @@ class LlamaStackQuant:
             "l2": "inputs larger than L2 (each step streams the rank's whole stack)",
         }
 
-    def setup(self) -> None:
-        from cuda_force_b200 import _abi
-
+    def setup(self, reference: bool = False) -> None:
         dev = self.dist.device
+        if reference:
+            # the reference arm samples one 4096x4096 projection of layer 0
+            self.inputs = [llama_layer_weights(0, dev)[0].cpu()]
+            return
+        from cuda_force_b200 import _abi
+        from cuda_force_b200.sharding import layer_shard
+
+        assert layer_shard(self.n_layers, self.dist.rank, self.dist.world) == self.layers
         self.lib = _abi.load()
         self.inputs, self.codes, self.scales = [], [], []
         for layer in self.layers:
@@ -373,6 +379,33 @@ def reference_quantize_fn():
                                          if x.dtype == torch.bfloat16 else x.numpy())), "port"
 
 
+def quantize_weight(w: torch.Tensor, reference: bool = False):
+    """Block-INT8 codes and scales of a weight: this package's kernel, or, for the
+    reference arm, the reference's CPU operator (bit-identical output)."""
+    if not reference:
+        import cuda_force_b200 as cf
+
+        return cf.quantize_int8(w)
+    fn, _kind = reference_quantize_fn()
+    out = fn(w.cpu())
+    if isinstance(out[0], torch.Tensor):
+        return out[0].reshape(w.shape), out[1]
+    codes, scales = out
+    return torch.from_numpy(codes).reshape(w.shape), torch.from_numpy(scales)
+
+
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+
+    return platform.processor() or "unknown"
+
+
 class Config1Quant:
     """benchmark config 1: fp32 [4096, 4096] N(0,1) block-INT8 quantise (or dequantise)."""
 
@@ -400,13 +433,16 @@ class Config1Quant:
                 "l2": "flushed between steps (256 MiB write outside the timed events)",
                 "parallelism": f"{self.dist.world} independent replica(s)"}
 
-    def setup(self) -> None:
-        from cuda_force_b200 import _abi
-
+    def setup(self, reference: bool = False) -> None:
         dev = self.dist.device
-        self.lib = _abi.load()
         g = torch.Generator(device=dev).manual_seed(1)
         self.x = torch.randn(self.rows, 4096, device=dev, generator=g)
+        self.work_per_step = (4 + 1 + 4 / 64) * self.x.numel()
+        if reference:
+            return
+        from cuda_force_b200 import _abi
+
+        self.lib = _abi.load()
         self.codes = torch.empty(self.rows, 4096, dtype=torch.int8, device=dev)
         self.scales = torch.empty(self.rows * 64, device=dev)
         self.out = torch.empty(self.rows, 4096, device=dev)
@@ -538,21 +574,22 @@ class LoraLinear:
                 "l2": "flushed between steps (256 MiB write outside the timed events)",
                 "parallelism": f"{self.dist.world} independent replica(s)"}
 
-    def setup(self) -> None:
-        import cuda_force_b200 as cf
-
+    def setup(self, reference: bool = False) -> None:
         dev = self.dist.device
         g = torch.Generator(device=dev).manual_seed(3)
         self.x = (torch.randn(self.m, self.k, device=dev, generator=g) * self.x_std).to(torch.bfloat16)
         w = (torch.randn(self.n, self.k, device=dev, generator=g) * self.w_std).to(torch.bfloat16)
         self.a = (torch.randn(self.k, self.r, device=dev, generator=g) * self.ab_std).to(torch.bfloat16)
         self.b = (torch.randn(self.r, self.n, device=dev, generator=g) * self.ab_std).to(torch.bfloat16)
+        self.scale = self.alpha / self.r
+        self.work_per_step = self.bytes() if self.unit == "GB/s" else self.flops()
         if self.int8:
-            self.codes, self.scales = cf.quantize_int8(w)
+            self.codes, self.scales = quantize_weight(w, reference)
             self.w = None
         else:
             self.w = w
-        self.scale = self.alpha / self.r
+        if reference:
+            return
         from cuda_force_b200 import _abi
 
         self.lib = _abi.load()
@@ -689,9 +726,7 @@ class LoraF32(LoraLinear):
         c["weight"] = "fp32 [out, in] (passed as W.t(), K-major)"
         return c
 
-    def setup(self) -> None:
-        from cuda_force_b200 import _abi
-
+    def setup(self, reference: bool = False) -> None:
         dev = self.dist.device
         g = torch.Generator(device=dev).manual_seed(3)
         self.x = torch.randn(self.m, self.k, device=dev, generator=g) * self.x_std
@@ -699,6 +734,11 @@ class LoraF32(LoraLinear):
         self.a = torch.randn(self.k, self.r, device=dev, generator=g) * self.ab_std
         self.b = torch.randn(self.r, self.n, device=dev, generator=g) * self.ab_std
         self.scale = self.alpha / self.r
+        self.work_per_step = self.flops()
+        if reference:
+            return
+        from cuda_force_b200 import _abi
+
         self.lib = _abi.load()
         self.y = torch.empty(self.m, self.n, dtype=torch.float32, device=dev)
         self.ws_bytes = self.lib.cf_lora_linear_workspace_bytes(self.m, self.r)
@@ -767,14 +807,17 @@ class MergeQuant:
                 "l2": "flushed between steps (256 MiB write outside the timed events)",
                 "parallelism": f"{self.dist.world} independent replica(s)"}
 
-    def setup(self) -> None:
-        from cuda_force_b200 import _abi
-
+    def setup(self, reference: bool = False) -> None:
         dev = self.dist.device
         g = torch.Generator(device=dev).manual_seed(9)
         self.w = (torch.randn(self.n, self.k, device=dev, generator=g) * 0.02).to(torch.bfloat16)
         self.a = (torch.randn(self.r, self.k, device=dev, generator=g) * 0.05).to(torch.bfloat16)
         self.b = (torch.randn(self.n, self.r, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+        self.work_per_step = self.bytes()
+        if reference:
+            return
+        from cuda_force_b200 import _abi
+
         self.codes = torch.empty(self.n, self.k, dtype=torch.int8, device=dev)
         self.scales = torch.empty(self.n * self.k // 64, dtype=torch.float32, device=dev)
         self.lib = _abi.load()
@@ -866,15 +909,18 @@ class ResidualRMSNorm:
                 "l2": "flushed between steps (256 MiB write outside the timed events)",
                 "parallelism": f"{self.dist.world} independent replica(s)"}
 
-    def setup(self) -> None:
-        from cuda_force_b200 import _abi
-
+    def setup(self, reference: bool = False) -> None:
         dev = self.dist.device
         g = torch.Generator(device=dev).manual_seed(11)
         shape = (self.rows, self.cols)
         self.x = torch.randn(shape, device=dev, generator=g).to(torch.bfloat16)
         self.r = torch.randn(shape, device=dev, generator=g).to(torch.bfloat16)
         self.w = (1 + 0.1 * torch.randn(self.cols, device=dev, generator=g)).to(torch.bfloat16)
+        self.work_per_step = self.bytes()
+        if reference:
+            return
+        from cuda_force_b200 import _abi
+
         self.out = torch.empty_like(self.x)
         self.summed = torch.empty_like(self.x)
         self.lib = _abi.load()
@@ -959,18 +1005,20 @@ class W8SwiGLU:
                 "l2": "flushed between steps (256 MiB write outside the timed events)",
                 "parallelism": f"{self.dist.world} independent replica(s)"}
 
-    def setup(self) -> None:
-        import cuda_force_b200 as cf
-        from cuda_force_b200 import _abi
-
+    def setup(self, reference: bool = False) -> None:
         dev = self.dist.device
         g = torch.Generator(device=dev).manual_seed(11)
         self.x = torch.randn(self.m, self.k, device=dev, generator=g).to(torch.bfloat16)
         wg = (torch.randn(self.n, self.k, device=dev, generator=g) * 0.02).to(torch.bfloat16)
         wu = (torch.randn(self.n, self.k, device=dev, generator=g) * 0.02).to(torch.bfloat16)
-        self.gc, self.gs = cf.quantize_int8(wg)
-        self.uc, self.us = cf.quantize_int8(wu)
+        self.gc, self.gs = quantize_weight(wg, reference)
+        self.uc, self.us = quantize_weight(wu, reference)
         del wg, wu
+        self.work_per_step = self.flops()
+        if reference:
+            return
+        from cuda_force_b200 import _abi
+
         self.y = torch.empty(self.m, self.n, dtype=torch.bfloat16, device=dev)
         self.lib = _abi.load()
         self.work_per_step = self.flops()
@@ -1047,9 +1095,12 @@ class W8ColumnSharded:
     dtype = "bf16 x int8->bf16 (fp32 acc)"
     metric = ("W8+LoRA column-sharded linear TFLOP/s (x [16384,8192], W [28672,8192] int8, "
               "r 64, all-gather of y)")
+    comm = None  # None = the --comm flag; "fused", "ce" or "nccl"
 
     def __init__(self, dist: Dist, _layers: int = 0):
         self.dist = dist
+        if self.comm is None:
+            self.comm = COMM_MODE
 
     def flops(self) -> float:
         return 2.0 * self.m * self.n * self.k + 2.0 * self.m * self.r * (self.k + self.n)
@@ -1061,39 +1112,45 @@ class W8ColumnSharded:
                 "parallelism": f"column-sharded over {g} GPU(s): {self.n // g} output features "
                                f"per rank, x and A replicated; all-gather of y "
                                + ("fused into the GEMM epilogue (TMA stores into every rank's "
-                                  "symmetric-memory y)" if COMM_MODE == "fused" and g > 1 else
+                                  "symmetric-memory y)" if self.comm == "fused" and g > 1 else
                                   "by the copy engines, one stream per peer, each row group "
                                   "pushed as soon as the kernel's counter says it is done "
-                                  "(symmetric-memory y)" if COMM_MODE == "ce" and g > 1 else
+                                  "(symmetric-memory y)" if self.comm == "ce" and g > 1 else
                                   f"by NCCL in {self.chunks} row chunks on a side stream"),
-                "output": ("y [M, N] on every rank" if COMM_MODE != "nccl" and g > 1 else
+                "output": ("y [M, N] on every rank" if self.comm != "nccl" and g > 1 else
                            "rank-major [G, rows, N/G] per chunk (no relayout copy)"),
                 "values": "x N(0,1), W N(0,0.015), A and B N(0,0.01); W and B seeded per rank",
                 "l2": "inputs larger than L2 (x 268 MB, W codes 235 MB / G)"}
 
-    def setup(self) -> None:
-        import cuda_force_b200 as cf
-        from cuda_force_b200.sharding import column_slice
+    def _slice(self, rank: int, reference: bool = False):
+        """The int8 codes, scales and B columns that ``rank`` owns, regenerated from its seed."""
+        from_cols = self.n // self.dist.world
+        dev = self.dist.device
+        gw = torch.Generator(device=dev).manual_seed(7 + rank)
+        w = (torch.randn(from_cols, self.k, device=dev, generator=gw) * 0.015).to(torch.bfloat16)
+        codes, scales = quantize_weight(w, reference)
+        del w
+        b = (torch.randn(self.r, from_cols, device=dev, generator=gw) * 0.01).to(torch.bfloat16)
+        return codes, scales, b
 
+    def setup(self, reference: bool = False) -> None:
         dev = self.dist.device
         g = torch.Generator(device=dev).manual_seed(5)
         self.x = torch.randn(self.m, self.k, device=dev, generator=g).to(torch.bfloat16)
         self.a = (torch.randn(self.k, self.r, device=dev, generator=g) * 0.01).to(torch.bfloat16)
-        cols = column_slice(self.n, self.dist.rank, self.dist.world)
-        width = cols.stop - cols.start
-        gw = torch.Generator(device=dev).manual_seed(7 + self.dist.rank)
-        w = (torch.randn(width, self.k, device=dev, generator=gw) * 0.015).to(torch.bfloat16)
-        self.codes, self.scales = cf.quantize_int8(w)
-        del w
-        self.b = (torch.randn(self.r, width, device=dev, generator=gw) * 0.01).to(torch.bfloat16)
+        if reference:
+            self.x = self.x[:256].cpu()  # the CPU sample's rows only
+        self.codes, self.scales, self.b = self._slice(self.dist.rank, reference)
         self.scale = self.alpha / self.r
         self.work_per_step = self.flops() / self.dist.world
         self.last = None
         self.fused = None
-        if self.dist.world > 1 and COMM_MODE in ("fused", "ce"):
+        if reference:
+            return
+        if self.dist.world > 1 and self.comm in ("fused", "ce"):
             from cuda_force_b200.sharding import FusedGatherLinear
 
-            mode = "ce" if COMM_MODE == "ce" else "kernel"
+            mode = "ce" if self.comm == "ce" else "kernel"
             self.fused = FusedGatherLinear(self.m, self.n, torch.bfloat16, dev, mode=mode)
             self.kernel = ("w8_wide_kernel with the all-gather fused into the epilogue "
                            "(TMA stores to every rank over NVLink) + down_proj_kernel<64>"
@@ -1114,25 +1171,77 @@ class W8ColumnSharded:
         self.last = sharded_lora_linear_int8(self.x, self.codes, self.scales, self.a, self.b,
                                              self.scale, group=group, chunks=self.chunks)
 
+    def gathered_rows(self, rows: list[int], owner: int) -> torch.Tensor:
+        """Rows ``rows`` of the columns that rank ``owner`` computed, read from this rank's
+        gathered output."""
+        width = self.codes.shape[0]
+        if self.fused is not None:
+            return self.last[rows][:, owner * width:(owner + 1) * width]
+        chunk_rows = -(-self.m // (self.chunks if self.dist.world > 1 else 1))
+        return torch.stack([self.last[r // chunk_rows][owner, r % chunk_rows] for r in rows])
+
     def verify(self) -> None:
+        """Every rank's column slice of the gathered output, on sampled rows, against the oracle:
+        the peer slices (written over NVLink by the peers) are rebuilt here from their seeds."""
         from oracle import linear_ref
 
         torch.cuda.synchronize(self.dist.device)
-        w_t = linear_ref.dequantized_weight_t(self.codes, self.scales)
         rows = torch.randperm(self.m, generator=torch.Generator().manual_seed(0))[:64].tolist()
         rows.sort()
-        if self.fused is not None:
-            width = self.codes.shape[0]
-            got = self.last[rows][:, self.dist.rank * width:(self.dist.rank + 1) * width]
-            peer = (self.dist.rank + 1) % self.dist.world
-            assert torch.isfinite(self.last[:, peer * width:(peer + 1) * width].float()).all()
-        else:
-            chunk_rows = -(-self.m // (self.chunks if self.dist.world > 1 else 1))
-            got = torch.stack([self.last[r // chunk_rows][self.dist.rank, r % chunk_rows]
-                               for r in rows])
-        ref = linear_ref.lora_linear(self.x[rows], w_t, self.a, self.b, self.scale)
-        err = linear_ref.max_rel_error(got, ref)
-        assert err <= 2e-2, f"{self.name}: max relative error {err}"
+        for owner in range(self.dist.world):
+            if owner == self.dist.rank:
+                codes, scales, b = self.codes, self.scales, self.b
+            else:
+                codes, scales, b = self._slice(owner)
+            w_t = linear_ref.dequantized_weight_t(codes, scales)
+            ref = linear_ref.lora_linear(self.x[rows], w_t, self.a, b, self.scale)
+            err = linear_ref.max_rel_error(self.gathered_rows(rows, owner), ref)
+            if not err <= 2e-2:
+                raise SystemExit(f"{self.name}: rank {self.dist.rank}'s copy of rank {owner}'s "
+                                 f"columns has max relative error {err}")
+
+    def exchange_record(self, step_ms: float, steps: int) -> dict | None:
+        """Bytes each rank sends per step, and the exchange time: the step minus the same
+        rank's compute alone (this rank's columns into a local y, no exchange)."""
+        if self.dist.world < 2:
+            return None
+        from cuda_force_b200 import _abi
+
+        lib = _abi.load()
+        width = self.codes.shape[0]
+        y = torch.empty(self.m, width, dtype=torch.bfloat16, device=self.dist.device)
+        ws_bytes = lib.cf_lora_linear_workspace_bytes(self.m, self.r)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=self.dist.device)
+        stream = torch.cuda.current_stream(self.dist.device)
+
+        def local():
+            _abi.check(lib.cf_lora_linear_int8(
+                self.x.data_ptr(), self.codes.data_ptr(), self.scales.data_ptr(),
+                self.a.data_ptr(), _abi.CF_LAYOUT_REF, self.b.data_ptr(), _abi.CF_LAYOUT_REF,
+                y.data_ptr(), self.m, self.k, width, self.r, self.scale, _abi.CF_DTYPE_BF16,
+                ws.data_ptr(), ws_bytes, stream.cuda_stream), "local compute")
+
+        for _ in range(3):
+            local()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(self.dist.device)
+        start.record(stream)
+        for _ in range(steps):
+            local()
+        end.record(stream)
+        end.synchronize()
+        local_ms = self.dist.max(start.elapsed_time(end) / steps)
+        sent = (self.dist.world - 1) * self.m * width * 2
+        exchange_ms = max(step_ms - local_ms, 0.0)
+        return {"bytes_sent_per_rank_per_step": sent,
+                "step_ms": round(step_ms, 4),
+                "compute_only_ms": round(local_ms, 4),
+                "exchange_ms": round(exchange_ms, 4),
+                "compute_only_tflops_per_gpu": round(self.work_per_step / local_ms / 1e9, 1),
+                "nvlink_gbs_over_step": round(sent / step_ms / 1e6, 1),
+                "exchange_efficiency": round(local_ms / step_ms, 4),
+                "how": "compute_only = this rank's columns into a local y (same kernels, no "
+                       "exchange), CUDA events, max over ranks; exchange = step - compute_only"}
 
     def e2e(self, steps: int) -> dict:
         dev = self.dist.device
@@ -1184,8 +1293,16 @@ class W8ColumnSharded:
             f"CPU dequantize_int8 + lora_linear (W dequantised every call)")
 
 
+class W8ColumnShardedNccl(W8ColumnSharded):
+    """benchmark config 5 with the output all-gather done by NCCL (the unfused baseline)."""
+
+    name = "w8_lora_70b_colshard_16384x8192x28672_nccl"
+    comm = "nccl"
+
+
 WORKLOADS = {w.name: w for w in (LlamaStackQuant, Config1Quant, Config1Dequant, LoraLinear,
-                                W8Decode, W8Prefill, W8ColumnSharded, LoraF32, MergeQuant,
+                                W8Decode, W8Prefill, W8ColumnSharded, W8ColumnShardedNccl,
+                                LoraF32, MergeQuant,
                                 W8SwiGLU, ResidualRMSNorm)}
 
 
@@ -1203,8 +1320,15 @@ def time_cpu(fn, min_seconds: float = 10.0, max_calls: int = 50) -> float:
     return statistics.median(times)
 
 
-def run_ours(args, dist: Dist) -> dict | None:
-    wl = WORKLOADS[args.workload](dist, args.layers)
+# The benchmark configs reported beside the headline (config 2) in the same JSON line.
+PER_CONFIG = ["config1_quant_f32", "config1_dequant_f32", "lora_bf16_8192x4096x4096",
+              "w8_lora_decode_32x4096x11008", "w8_lora_prefill_4096x4096x11008",
+              "w8_lora_70b_colshard_16384x8192x28672"]
+PER_CONFIG_MULTI = ["w8_lora_70b_colshard_16384x8192x28672_nccl"]
+
+
+def measure(wl, args, dist: Dist, cpu_seconds: float) -> dict:
+    """Times K steps of one workload under the bench rules and returns its report fields."""
     torch.cuda.set_device(dist.device)
     wl.setup()
     stream = torch.cuda.Stream(device=dist.device)
@@ -1254,27 +1378,24 @@ def run_ours(args, dist: Dist) -> dict | None:
     traffic = traffic_info.get("dram_bytes_per_step") if traffic_info else None
 
     copy_ref = size_matched_copy(wl.work_per_step, dist.device, flush) if wl.bound == "hbm" else None
+    exchange = (wl.exchange_record(total_ms / args.steps, args.steps)
+                if hasattr(wl, "exchange_record") else None)
     e2e = wl.e2e(max(1, min(args.steps, args.e2e_steps)))
 
     cpu = None
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
         fn, work, kind, sample = wl.cpu_sample()
-        t = time_cpu(fn)
+        t = time_cpu(fn, min_seconds=cpu_seconds)
         cpu = {"value": work / t / scale, "unit": wl.unit, "cores": torch.get_num_threads(),
-               "kind": kind, "sample": sample + ", median of >=3 calls over ~10 s"}
+               "cpu_model": cpu_model(), "kind": kind,
+               "sample": sample + f", median of >=3 calls over ~{cpu_seconds:g} s"}
     result = {
         "metric": wl.metric,
         "value": round(value, 3),
         "unit": wl.unit,
-        "n_gpus": dist.world,
-        "steps": args.steps,
-        "warmup": args.warmup,
         "ms_per_step": round(total_ms / args.steps, 5),
-        "higher_is_better": True,
         "scaling": wl.scaling,
-        "vs_baseline": None,
         "dtype": wl.dtype,
-        "data": "synthetic (seeded on device)",
         "config": wl.config(),
         "roofline": {
             "bound": wl.bound,
@@ -1294,55 +1415,124 @@ def run_ours(args, dist: Dist) -> dict | None:
         "clocks": clocks.summary(),
         "cpu_baseline": cpu,
     }
+    if dist.world > 1:
+        result["per_gpu"] = round(value / dist.world, 3)
+    if exchange is not None:
+        result["comm"] = exchange
+    return result
+
+
+def release(wl) -> None:
+    """Drops a workload's device tensors before the next one is set up."""
+    for name in list(vars(wl)):
+        if name != "dist":
+            delattr(wl, name)
+    if torch.cuda.is_available():
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+
+
+def run_ours(args, dist: Dist) -> dict | None:
+    wl = WORKLOADS[args.workload](dist, args.layers)
+    head = measure(wl, args, dist, cpu_seconds=10.0)
+    release(wl)
+    result = {
+        "metric": head.pop("metric"),
+        "value": head.pop("value"),
+        "unit": head.pop("unit"),
+        "n_gpus": dist.world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": head.pop("ms_per_step"),
+        "higher_is_better": True,
+        "scaling": head.pop("scaling"),
+        "vs_baseline": None,
+        "dtype": head.pop("dtype"),
+        "data": "synthetic (seeded on device)",
+        **head,
+    }
+    if args.per_config and args.workload == LlamaStackQuant.name:
+        names = PER_CONFIG + (PER_CONFIG_MULTI if dist.world > 1 else [])
+        per = {}
+        launches = result["gpu_launches"]
+        for name in names:
+            sub = WORKLOADS[name](dist, args.layers)
+            per[name] = measure(sub, args, dist, cpu_seconds=3.0)
+            launches += per[name]["gpu_launches"]
+            release(sub)
+        result["per_config"] = per
+        result["gpu_launches_all_configs"] = launches
     return result if dist.rank == 0 else None
 
 
-def run_reference(args, dist: Dist) -> dict | None:
-    """The reference's own CPU implementation of the path on this host's cores."""
-    if dist.rank != 0:
-        return None
-    torch.cuda.set_device(dist.device)
-    torch.set_num_threads(os.cpu_count() or 1)
-    wl = WORKLOADS[args.workload](dist, args.layers)
-    if isinstance(wl, LlamaStackQuant):
-        # generate only the sampled projection (layer 0), not the whole stack
-        x = llama_layer_weights(0, dist.device)[0].cpu()
-        qfn, kind = reference_quantize_fn()
-        fn = lambda: qfn(x)  # noqa: E731
-        work = BYTES_PER_ELEM_BF16_QUANT * x.numel()
-        sample = "one 4096x4096 bf16 projection of layer 0 per step"
-    else:
-        wl.setup()
-        fn, work, kind, sample = wl.cpu_sample()
+def reference_entry(wl, args, dist: Dist, steps: int, warmup: int) -> dict:
+    """The reference's own CPU implementation of one workload, timed on this host's cores."""
+    wl.setup(reference=True)
+    fn, work, kind, sample = wl.cpu_sample()
     scale = 1e9 if wl.unit == "GB/s" else 1e12
-    for _ in range(max(1, args.warmup)):
+    for _ in range(max(1, warmup)):
         fn()
     times = []
-    for _ in range(args.steps):
+    for _ in range(steps):
         t0 = time.perf_counter()
         fn()
         times.append(time.perf_counter() - t0)
     value = work * len(times) / sum(times) / scale
     return {
-        "impl": "reference",
         "metric": wl.metric,
         "value": round(value, 6),
         "unit": wl.unit,
+        "ms_per_step": round(1e3 * sum(times) / len(times), 3),
+        "steps": steps,
+        "config": {**wl.config(), "reference_sample": sample},
+        "cpu_baseline": {"value": round(value, 6), "unit": wl.unit,
+                         "cores": torch.get_num_threads(), "cpu_model": cpu_model(),
+                         "kind": kind, "sample": sample},
+        "e2e": {"value": round(value, 6), "unit": wl.unit, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def run_reference(args, dist: Dist) -> dict | None:
+    """The reference's own CPU implementation of the path on this host's cores.
+
+    Nothing of this package is imported on this arm: inputs come from torch's
+    generators and the reference's compiled CPU operators quantise the weights.
+    """
+    if dist.rank != 0:
+        return None
+    torch.cuda.set_device(dist.device)
+    torch.set_num_threads(os.cpu_count() or 1)
+    wl = WORKLOADS[args.workload](dist, args.layers)
+    head = reference_entry(wl, args, dist, args.steps, args.warmup)
+    result = {
+        "impl": "reference",
+        "metric": head["metric"],
+        "value": head["value"],
+        "unit": head["unit"],
         "n_gpus": dist.world,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": round(1e3 * sum(times) / len(times), 3),
+        "ms_per_step": head["ms_per_step"],
         "higher_is_better": True,
         "scaling": wl.scaling,
         "vs_baseline": None,
         "dtype": wl.dtype,
         "data": "synthetic (seeded)",
-        "config": {**wl.config(), "reference_sample": sample},
-        "cpu_baseline": {"value": round(value, 6), "unit": wl.unit,
-                         "cores": torch.get_num_threads(), "kind": kind, "sample": sample},
-        "e2e": {"value": round(value, 6), "unit": wl.unit, "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
+        "config": head["config"],
+        "cpu_baseline": head["cpu_baseline"],
+        "e2e": head["e2e"],
     }
+    if args.per_config and args.workload == LlamaStackQuant.name:
+        # bounded samples: a few calls each, so the whole arm stays within minutes
+        per = {}
+        for name in PER_CONFIG:
+            sub = WORKLOADS[name](dist, args.layers)
+            per[name] = reference_entry(sub, args, dist, min(args.steps, 5), 1)
+            release(sub)
+        result["per_config"] = per
+    assert "cuda_force_b200" not in sys.modules, "the reference arm imported this package"
+    return result
 
 
 def main() -> None:
@@ -1357,6 +1547,9 @@ def main() -> None:
                         help="stack depth (default 32 = benchmark config 2; smaller only "
                              "for profiling captures)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-per-config", dest="per_config", action="store_false",
+                        help="report the headline workload only (default: the headline config "
+                             "2 line also carries configs 1, 3, 4 and 5 under per_config)")
     parser.add_argument("--elements", type=int, default=0,
                         help="config 1 workloads: tensor size (default 4096*4096)")
     parser.add_argument("--comm", choices=["fused", "ce", "nccl"], default="fused",

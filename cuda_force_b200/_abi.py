@@ -81,6 +81,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "cf_status_string": (ctypes.c_char_p, [_int]),
     "cf_last_cuda_error": (_int, []),
     "cf_device_status": (_int, []),
+    "cf_debug_expire_wait": (_int, [ctypes.c_uint64, ctypes.c_void_p]),
     "cf_build_info": (ctypes.c_char_p, []),
 }
 

@@ -4,6 +4,7 @@
 #include <cstdio>
 
 #include "cf_common.cuh"
+#include "ptx.cuh"
 
 // Device-side error word. Kernels with bounded waits OR a DeviceError code
 // into it and return instead of spinning forever; cf_device_status() reads and
@@ -56,6 +57,20 @@ unsigned *device_error_word() {
   return static_cast<unsigned *>(addr);
 }
 
+// Test hook of the bounded-wait path: one warp waits on an mbarrier that
+// nothing arrives on, with the same bounded wait the product kernels use, and
+// records the expiry in the error word exactly as they do.
+__global__ void expire_wait_kernel(uint64_t limit_ns, unsigned *error_word) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(&bar, 1);
+    ptx::fence_mbar_init();
+  }
+  __syncwarp();
+  const bool ok = ptx::warp_wait(&bar, 0, limit_ns);
+  if (!ok && threadIdx.x == 0) atomicOr(error_word, kDevErrTimeout);
+}
+
 }  // namespace cfb
 
 extern "C" {
@@ -85,6 +100,15 @@ int cf_device_status(void) {
   const unsigned zero = 0u;
   CFB_TRY_CUDA(cudaMemcpy(word, &zero, sizeof(zero), cudaMemcpyHostToDevice));
   return CF_ERR_DEVICE_TIMEOUT;
+}
+
+int cf_debug_expire_wait(uint64_t limit_ns, cf_stream_t stream) {
+  if (limit_ns < 1000000ull || limit_ns > 2000000000ull) return CF_ERR_INVALID_ARGUMENT;
+  unsigned *word = cfb::device_error_word();
+  if (word == nullptr) return cfb::record_cuda_error(cudaGetLastError());
+  cfb::expire_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(limit_ns, word);
+  CFB_TRY_CUDA(cudaGetLastError());
+  return CF_OK;
 }
 
 const char *cf_build_info(void) {

@@ -254,8 +254,10 @@ CF_API int cf_fused_residual_rmsnorm(const void *x, const void *residual, const 
  * allocator, foreign-language hosts without a CUDA allocator, and loops that
  * must not pay cudaMalloc's device synchronisation. No counterpart in the
  * reference. The workspace is a 4 MiB device array inside the library, held by
- * every GPU that loads it until exit: m * rank * 2 bytes (rounded up to 256)
- * must fit, else CF_ERR_WORKSPACE and nothing is launched. Calls on one device
+ * every GPU that loads it until exit: m * rank * 2 bytes for bf16/f16 calls
+ * (m <= 131072 at rank 16) or m * rank * 4 bytes for fp32 calls (m <= 65536 at
+ * rank 16), rounded up to 256, must fit, else CF_ERR_WORKSPACE and nothing is
+ * launched. Calls on one device
  * share the array; calls that overlap on the GPU race on it. The first call on
  * a device looks up the array's address (make it before any stream capture).
  * Same arguments and semantics as cf_lora_linear otherwise. */
@@ -276,6 +278,15 @@ CF_API int cf_last_cuda_error(void);
  * kernel whose bounded wait gave up). Synchronises with the device. Returns
  * CF_OK or CF_ERR_DEVICE_TIMEOUT (CF_ERR_CUDA if the read itself fails). */
 CF_API int cf_device_status(void);
+
+/* Test hook for the bounded-wait path (no counterpart in the reference; its
+ * closest is the sticky / non-sticky split of CudaError::is_sticky,
+ * cuda/include/cudaforge/cuda_error.cuh:15-41). Launches one warp that waits
+ * on a barrier nothing arrives on, with the bounded wait every kernel here
+ * uses, limited to limit_ns (1 ms .. 2 s, else CF_ERR_INVALID_ARGUMENT). The
+ * wait runs out, the kernel records CF_ERR_DEVICE_TIMEOUT in the device error
+ * word and returns: nothing faults, and the context stays usable. */
+CF_API int cf_debug_expire_wait(uint64_t limit_ns, cf_stream_t stream);
 
 /* Build information: "sm_100a" architecture tag and version string. */
 CF_API const char *cf_build_info(void);

@@ -55,3 +55,40 @@ def test_every_workload_reports_the_contract_fields(name, dist):
     cfg = wl.config()
     assert isinstance(cfg.get("workload"), str) and cfg["workload"]
     assert "l2" in cfg or not wl.flush_l2
+
+
+def test_reference_arm_imports_nothing_of_the_package(tmp_path):
+    # bench.py --impl reference must time the reference's CPU path only: no module of this
+    # package may load in that process (its native libraries would show as loaded). Run on
+    # the CPU here, with the device redirected to the host.
+    import json
+    import subprocess
+    import sys
+
+    script = tmp_path / "ref_arm.py"
+    script.write_text(
+        "import sys, torch\n"
+        f"sys.path.insert(0, {str(bench.ROOT)!r})\n"
+        "sys.argv = ['bench.py', '--impl', 'reference', '--steps', '2', '--warmup', '3',\n"
+        "            '--workload', 'config1_quant_f32']\n"
+        "import bench\n"
+        "bench.Dist.device = property(lambda self: torch.device('cpu'))\n"
+        "torch.cuda.set_device = lambda d: None\n"
+        "bench.main()\n"
+        "assert 'cuda_force_b200' not in sys.modules\n")
+    out = subprocess.run([sys.executable, str(script)], capture_output=True, text=True,
+                         timeout=600)
+    assert out.returncode == 0, out.stderr[-2000:]
+    line = json.loads(out.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference"
+    assert line["cpu_baseline"]["cores"] >= 1 and line["cpu_baseline"]["cpu_model"]
+    assert line["e2e"]["h2d_bytes_per_step"] == 0
+
+
+def test_headline_line_lists_every_benchmark_config():
+    # configs 1 (quantise, dequantise), 3, 4 (decode, prefill) and 5 ride in the config 2 line
+    assert set(bench.PER_CONFIG) == {
+        "config1_quant_f32", "config1_dequant_f32", "lora_bf16_8192x4096x4096",
+        "w8_lora_decode_32x4096x11008", "w8_lora_prefill_4096x4096x11008",
+        "w8_lora_70b_colshard_16384x8192x28672"}
+    assert all(name in bench.WORKLOADS for name in bench.PER_CONFIG + bench.PER_CONFIG_MULTI)

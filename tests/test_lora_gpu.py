@@ -364,3 +364,37 @@ def test_matmul_f32(m, k, n, b_t, cuda_device):
     # one tf32 product: operands rounded to 10 explicit mantissa bits
     assert (tf32 - ref).abs().max() <= 5e-3 * ref.abs().max()
     assert (tf32 - ref).abs().max() > (precise - ref).abs().max()
+
+
+@pytest.mark.parametrize("mode", ["kernel", "ce"])
+def test_config5_per_rank_shape_into_eight_destinations(mode, cuda_device):
+    # Benchmark config 5 at 8 GPUs, one rank's share: K 8192, rank 64, 28672 / 8 = 3584 output
+    # features at column offset 3 * 3584 of y [M, 28672], pushed into 8 copies of y (on one GPU
+    # here, standing in for the 8 ranks' symmetric buffers). Every copy must hold exactly the
+    # single-destination product in this rank's columns and nothing outside them.
+    m, k, n, rank, n_dest, ldy = 2048, 8192, 3584, 64, 8, 28672
+    col0 = 3 * n
+    x, codes, scales, a, b = _w8_case(m, k, n, rank, cuda_device, seed=55)
+    dests = [torch.full((m, ldy), 7.0, dtype=torch.bfloat16, device=cuda_device)
+             for _ in range(n_dest)]
+    ptrs = (ctypes.c_void_p * n_dest)(*[t.data_ptr() for t in dests])
+    lib = _abi.load()
+    s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    if mode == "ce":
+        fn, ws_bytes = (lib.cf_lora_linear_int8_allgather_ce,
+                        lib.cf_lora_linear_int8_allgather_ce_workspace_bytes(m, rank))
+    else:
+        fn, ws_bytes = lib.cf_lora_linear_int8_allgather, lib.cf_lora_linear_workspace_bytes(m, rank)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=cuda_device)
+    _abi.check(fn(p(x), p(codes), p(scales), p(a), _abi.CF_LAYOUT_REF, p(b), _abi.CF_LAYOUT_REF,
+                  n_dest, ptrs, 3, ldy, col0, m, k, n, rank, 2.0, _abi.CF_DTYPE_BF16, p(ws),
+                  ws_bytes, s), mode)
+    torch.cuda.synchronize()
+    assert lib.cf_device_status() == _abi.CF_OK
+    y = cf.lora_linear_int8(x, codes, scales, a, b, 2.0)
+    for d in dests:
+        assert torch.equal(d[:, col0:col0 + n], y)
+        assert (d[:, :col0] == 7.0).all() and (d[:, col0 + n:] == 7.0).all()
+    w_t = linear_ref.dequantized_weight_t(codes, scales)
+    assert sampled_rows_error(y, x, w_t, a, b, 2.0, rows=128) <= TIGHT

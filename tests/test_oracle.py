@@ -94,3 +94,37 @@ def test_norm_oracle_matches_reference_fixture(name):
     plain = norm_ref.rmsnorm(case["x"], case["weight"], case["eps"])
     for got, key in ((normalised, "normalised"), (summed, "summed"), (plain, "plain")):
         assert torch.equal(got, case[key]), key
+
+
+@pytest.mark.parametrize(("m", "k", "n", "r", "int8"), [
+    (256, 4096, 4096, 16, False),     # benchmark config 3, 256 of its 8192 rows
+    (32, 4096, 11008, 16, True),      # benchmark config 4 decode
+    (256, 4096, 11008, 16, True),     # benchmark config 4 prefill, 256 of its 4096 rows
+    (7, 129, 65, 3, False),           # the reference's own ragged test shape
+])
+def test_linear_oracle_matches_the_compiled_reference(m, k, n, r, int8):
+    # oracle/linear_ref against the reference's own compiled CPU operators
+    # (cpp/src/bindings.cpp:255-258 lora_linear_cpu, :320-329 dequantize_int8_cpu), on the
+    # same bf16-valued inputs upcast to fp32, the dtype the reference's operator takes.
+    from oracle import build_ref
+
+    if not build_ref.load():
+        pytest.skip("the reference's CPU operators are not built (oracle/_ref)")
+    g = torch.Generator().manual_seed(m * 7 + k + n)
+    x = torch.randn(m, k, generator=g).bfloat16()
+    w = (torch.randn(n, k, generator=g) * 0.02).bfloat16()
+    a = (torch.randn(k, r, generator=g) * 0.01).bfloat16()
+    b = (torch.randn(r, n, generator=g) * 0.01).bfloat16()
+    if int8:
+        codes, scales = torch.ops.cudaforge_ref.quantize_int8(w.float())
+        codes = codes.reshape(n, k)
+        ours = linear_ref.lora_linear_int8(x, codes, scales, a, b, 2.0)
+        w_t = torch.ops.cudaforge_ref.dequantize_int8(codes, scales).reshape(n, k).t()
+    else:
+        ours = linear_ref.lora_linear(x, w.t(), a, b, 2.0)
+        w_t = w.float().t()
+    ref = torch.ops.cudaforge_ref.lora_linear(x.float(), w_t.contiguous(), a.float(),
+                                              b.float(), 2.0)
+    # Both are fp32 ATen compositions of the same formula; only the GEMM blocking of a
+    # contiguous versus a transposed operand may differ.
+    assert linear_ref.max_rel_error(ours, ref) <= 1e-6

@@ -212,3 +212,23 @@ def test_count_above_two_to_the_31(cuda_device):
         assert scales[b].item() == ref_s[0]
     del x, codes, scales
     torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("size", [1, 63, 64, 65, 128, 1000, 4096 * 4096])
+def test_quantization_error_is_within_half_a_step(dtype, size, cuda_device):
+    # reference python/cudaforge/ops.py:479-488 (quantization_error) and the bound its tests
+    # hold it to (tests/python/test_ops.py:174-181, 225-229): the round trip errs by at most
+    # half the largest block scale, and the helper equals a manual round trip. Here both sides
+    # are also checked against the oracle's dequantised values, bit for bit.
+    g = torch.Generator().manual_seed(size)
+    x = (torch.randn(size, generator=g) * 5.0).to(dtype)
+    xd = x.to(cuda_device)
+    err = cf.quantization_error(xd)
+    codes, scales = cf.quantize_int8(xd)
+    manual = (xd.float() - cf.dequantize_int8(codes, scales)).abs().max()
+    assert torch.equal(err, manual)
+    assert err.item() <= scales.max().item() / 2 + 1e-6
+    ref_codes, ref_scales = quant_ref.quantize(torch_to_numpy_input(x))
+    ref = torch.from_numpy(quant_ref.dequantize(ref_codes, ref_scales))
+    assert err.item() == (x.float() - ref).abs().max().item()
