@@ -41,7 +41,9 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 CONFIG1_ROWS = 4096  # rows of 4096 fp32 for the config 1 workloads (--elements)
-COMM_MODE = "fused"  # config 5 all-gather: "fused" (peer stores), "ce" (copy engines) or "nccl"
+# config 5 all-gather: "mc" (NVLink multicast stores), "fused" (one peer store per rank),
+# "ce" (copy engines), "nccl", or "auto" (mc where the GPUs support multicast, else fused)
+COMM_MODE = "auto"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 BYTES_PER_ELEM_BF16_QUANT = 2 + 1 + 4 / 64
 
@@ -1081,6 +1083,14 @@ class W8SwiGLU:
                 f"swiglu")
 
 
+def _multicast_ok(dist: Dist) -> bool:
+    if not torch.cuda.is_available():
+        return False
+    from cuda_force_b200.sharding import FusedGatherLinear
+
+    return FusedGatherLinear.has_multicast(dist.device)
+
+
 class W8ColumnSharded:
     """benchmark config 5: column-sharded W8 + LoRA on a Llama-70B MLP shape + NCCL all-gather."""
 
@@ -1101,6 +1111,8 @@ class W8ColumnSharded:
         self.dist = dist
         if self.comm is None:
             self.comm = COMM_MODE
+        if self.comm == "auto":
+            self.comm = "mc" if dist.world > 1 and _multicast_ok(dist) else "fused"
 
     def flops(self) -> float:
         return 2.0 * self.m * self.n * self.k + 2.0 * self.m * self.r * (self.k + self.n)
@@ -1111,7 +1123,11 @@ class W8ColumnSharded:
                 "rank": self.r, "alpha": self.alpha, "weight": "block-64 int8 codes + fp32 scales",
                 "parallelism": f"column-sharded over {g} GPU(s): {self.n // g} output features "
                                f"per rank, x and A replicated; all-gather of y "
-                               + ("fused into the GEMM epilogue (TMA stores into every rank's "
+                               + ("fused into the GEMM epilogue: each 16-byte piece written "
+                                  "once through y's NVLink multicast address (multimem.st), "
+                                  "the switch delivers it to every rank" if self.comm == "mc"
+                                  and g > 1 else
+                                  "fused into the GEMM epilogue (TMA stores into every rank's "
                                   "symmetric-memory y)" if self.comm == "fused" and g > 1 else
                                   "by the copy engines, one stream per peer, each row group "
                                   "pushed as soon as the kernel's counter says it is done "
@@ -1147,12 +1163,15 @@ class W8ColumnSharded:
         self.fused = None
         if reference:
             return
-        if self.dist.world > 1 and self.comm in ("fused", "ce"):
+        if self.dist.world > 1 and self.comm in ("fused", "ce", "mc"):
             from cuda_force_b200.sharding import FusedGatherLinear
 
-            mode = "ce" if self.comm == "ce" else "kernel"
+            mode = {"ce": "ce", "mc": "mc"}.get(self.comm, "kernel")
             self.fused = FusedGatherLinear(self.m, self.n, torch.bfloat16, dev, mode=mode)
             self.kernel = ("w8_wide_kernel with the all-gather fused into the epilogue "
+                           "(multimem stores to y's NVLink multicast address) + "
+                           "down_proj_kernel<64>" if mode == "mc" else
+                           "w8_wide_kernel with the all-gather fused into the epilogue "
                            "(TMA stores to every rank over NVLink) + down_proj_kernel<64>"
                            if mode == "kernel" else
                            "w8_wide_kernel (local y + row-group counters) + down_proj_kernel<64>; "
@@ -1300,8 +1319,16 @@ class W8ColumnShardedNccl(W8ColumnSharded):
     comm = "nccl"
 
 
+class W8ColumnShardedPeer(W8ColumnSharded):
+    """benchmark config 5 with the all-gather fused as one TMA store per peer (no multicast)."""
+
+    name = "w8_lora_70b_colshard_16384x8192x28672_peer"
+    comm = "fused"
+
+
 WORKLOADS = {w.name: w for w in (LlamaStackQuant, Config1Quant, Config1Dequant, LoraLinear,
                                 W8Decode, W8Prefill, W8ColumnSharded, W8ColumnShardedNccl,
+                                W8ColumnShardedPeer,
                                 LoraF32, MergeQuant,
                                 W8SwiGLU, ResidualRMSNorm)}
 
@@ -1324,7 +1351,8 @@ def time_cpu(fn, min_seconds: float = 10.0, max_calls: int = 50) -> float:
 PER_CONFIG = ["config1_quant_f32", "config1_dequant_f32", "lora_bf16_8192x4096x4096",
               "w8_lora_decode_32x4096x11008", "w8_lora_prefill_4096x4096x11008",
               "w8_lora_70b_colshard_16384x8192x28672"]
-PER_CONFIG_MULTI = ["w8_lora_70b_colshard_16384x8192x28672_nccl"]
+PER_CONFIG_MULTI = ["w8_lora_70b_colshard_16384x8192x28672_nccl",
+                    "w8_lora_70b_colshard_16384x8192x28672_peer"]
 
 
 def measure(wl, args, dist: Dist, cpu_seconds: float) -> dict:
@@ -1552,9 +1580,11 @@ def main() -> None:
                              "2 line also carries configs 1, 3, 4 and 5 under per_config)")
     parser.add_argument("--elements", type=int, default=0,
                         help="config 1 workloads: tensor size (default 4096*4096)")
-    parser.add_argument("--comm", choices=["fused", "ce", "nccl"], default="fused",
-                        help="config 5 all-gather: fused into the kernel, on the copy "
-                             "engines behind per-row-group counters, or NCCL")
+    parser.add_argument("--comm", choices=["auto", "mc", "fused", "ce", "nccl"], default="auto",
+                        help="config 5 all-gather: multimem stores through y's NVLink "
+                             "multicast address, one TMA store per peer, the copy engines "
+                             "behind per-row-group counters, or NCCL (auto: mc where the "
+                             "GPUs support multicast, else fused)")
     args = parser.parse_args()
     global COMM_MODE, CONFIG1_ROWS
     COMM_MODE = args.comm

@@ -62,6 +62,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_p, _p, _p, _p, _int, _p, _int, _int, ctypes.POINTER(_p), _int, _i64, _i64, _i64, _i64,
          _i64, _i64, ctypes.c_float, _int, _p, ctypes.c_size_t, _p],
     ),
+    "cf_lora_linear_int8_allgather_mc": (
+        _int,
+        [_p, _p, _p, _p, _int, _p, _int, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64,
+         ctypes.c_float, _int, _p, ctypes.c_size_t, _p],
+    ),
     "cf_lora_linear_int8_allgather_ce_workspace_bytes": (ctypes.c_size_t, [_i64, _i64]),
     "cf_lora_linear_int8_allgather_ce": (
         _int,

@@ -584,11 +584,16 @@ struct W8Params {
   int extra_b_mn;    // B stored [rank, N] (N contiguous)
   const float *w_scales;
   int kb_per_row;    // scales per row (K / 64)
+  int scale_tma;     // scales arrive by TMA with each stage (kb_per_row % 4 == 0)
   int ldo;           // row stride of every destination (elements)
   int out_col0;      // first column of this call's features in the destination
   int n_outs;        // destinations written by the epilogue
   int self_out;      // index of the destination on this GPU (stored first)
   void *outs[kMaxOuts];
+  // Multicast address of the destination (all ranks' y bound to one NVLink
+  // multicast object); when set, the epilogue writes every slab once with
+  // multimem stores instead of one TMA store per destination.
+  void *mc_out;
   int n_tiles_w;
   int n_tiles;
   unsigned *err;
@@ -641,10 +646,15 @@ struct DecCfg {
   // converted slots, so the converters run two k-blocks ahead of the MMA's
   // commit instead of one (3 % faster than 4 + 2 at x [32, 4096], W [11008, 4096]).
   static constexpr int kRawStages = BT <= 32 ? 3 : 2;
-  static constexpr int kXStages = BT <= 32 ? 3 : (BT <= 64 ? 3 : 2);
+  static constexpr int kXStages = BT <= 64 ? 2 : 2;
   static constexpr int kConvSlots = BT <= 64 ? 3 : 2;
+  // Each raw stage also carries the tile's scales: 128 rows x 4 k-blocks of
+  // fp32 (a 16-byte TMA row; the stage's two k-blocks sit inside it), so no
+  // converter waits on a global load of its scale.
+  static constexpr int kScaleBytes = kBM * 4 * 4;  // 2 KB
   static constexpr int kRawOff = 0;
-  static constexpr int kXOff = kRawOff + kRawStages * kRawBytes;
+  static constexpr int kScaleOff = kRawOff + kRawStages * kRawBytes;
+  static constexpr int kXOff = kScaleOff + kRawStages * kScaleBytes;
   static constexpr int kConvOff = kXOff + kXStages * kXBytes;
   static constexpr int kRingBytes = kConvOff + kConvSlots * kConvBytes;
   static constexpr int kPartialBytes = kBM * BT * 4;  // aliases the spent rings
@@ -666,6 +676,7 @@ struct DecParams {
   int splits;        // cluster size
   int rank;          // adapter rank (16, 32 or 64)
   int b_mn;          // b stored [rank, N] (N contiguous: MN-major A operand)
+  int scale_tma;     // scales arrive by TMA with the codes (num_kb % 4 == 0)
   const float *w_scales;
   uint16_t *out;     // y [M, N]
   unsigned *err;
@@ -676,12 +687,14 @@ __global__ void __launch_bounds__(DecCfg<BT>::kThreads, DecCfg<BT>::kMinBlocks)
     w8_decode_kernel(const __grid_constant__ CUtensorMap tm_x,
                      const __grid_constant__ CUtensorMap tm_codes,
                      const __grid_constant__ CUtensorMap tm_p,
-                     const __grid_constant__ CUtensorMap tm_bt, const DecParams p) {
+                     const __grid_constant__ CUtensorMap tm_bt,
+                     const __grid_constant__ CUtensorMap tm_scales, const DecParams p) {
   using C = DecCfg<BT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t *raw_ring = smem + C::kRawOff;
+  const float *scale_ring = reinterpret_cast<const float *>(smem + C::kScaleOff);
   uint8_t *x_ring = smem + C::kXOff;
   uint8_t *conv = smem + C::kConvOff;
   float *partial = reinterpret_cast<float *>(smem);
@@ -714,6 +727,7 @@ __global__ void __launch_bounds__(DecCfg<BT>::kThreads, DecCfg<BT>::kMinBlocks)
     ptx::prefetch_tensor_map(&tm_x);
     ptx::prefetch_tensor_map(&tm_p);
     ptx::prefetch_tensor_map(&tm_bt);
+    if (p.scale_tma) ptx::prefetch_tensor_map(&tm_scales);
     for (int s = 0; s < C::kRawStages; ++s) {
       ptx::mbar_init(&raw_full[s], 1);
       ptx::mbar_init(&raw_empty[s], kConvWarps);
@@ -760,8 +774,14 @@ __global__ void __launch_bounds__(DecCfg<BT>::kThreads, DecCfg<BT>::kMinBlocks)
         if (codes) {
           uint8_t *dst = raw_ring + stage * C::kRawBytes;
           if (main) {
-            ptx::mbar_expect_tx(&full[stage], C::kRawBytes);
-            ptx::tma_load_2d(dst, &tm_codes, &full[stage], (kb0 + it * C::kRawKb) * kBK, w0);
+            const int kb = kb0 + it * C::kRawKb;
+            ptx::mbar_expect_tx(&full[stage], C::kRawBytes + (p.scale_tma ? C::kScaleBytes : 0));
+            ptx::tma_load_2d(dst, &tm_codes, &full[stage], kb * kBK, w0);
+            if (p.scale_tma) {
+              // scales [N, num_kb]: the aligned group of four k-blocks holding kb, kb + 1
+              ptx::tma_load_2d(smem + C::kScaleOff + stage * C::kScaleBytes,
+                               &tm_scales, &full[stage], kb & ~3, w0);
+            }
           } else {
             // The tile's B^T slice: [128 features, rank] as the A operand.
             ptx::mbar_expect_tx(&full[stage], kBM * p.rank * 2);
@@ -874,7 +894,8 @@ __global__ void __launch_bounds__(DecCfg<BT>::kThreads, DecCfg<BT>::kMinBlocks)
 #pragma unroll
     for (int g = 0; g < kGroups; ++g) {
       const int n = w0 + (cw + g * kConvWarps) * 8 + sub_row;
-      srow[g] = n < p.N ? p.w_scales + static_cast<int64_t>(n) * p.num_kb + kb0 : nullptr;
+      srow[g] = n < p.N && !p.scale_tma
+                    ? p.w_scales + static_cast<int64_t>(n) * p.num_kb + kb0 : nullptr;
 #pragma unroll
       for (int a = 0; a < kScaleAhead; ++a) {
         sq[g][a] = (srow[g] != nullptr && a < nkb) ? __ldg(srow[g] + a) : 0.0f;
@@ -909,7 +930,10 @@ __global__ void __launch_bounds__(DecCfg<BT>::kThreads, DecCfg<BT>::kMinBlocks)
         const int r = (cw + g * kConvWarps) * 8 + sub_row;
         const uint32_t words[4] = {codes[g].x, codes[g].y, codes[g].z, codes[g].w};
         uint32_t outw[8];
-        const uint64_t sc2 = ptx::splat_f32x2(sq[g][0]);
+        const float sc = p.scale_tma ? scale_ring[rs * (C::kScaleBytes / 4) + r * 4 +
+                                                  ((kb0 + it) & 3)]
+                                     : sq[g][0];
+        const uint64_t sc2 = ptx::splat_f32x2(sc);
 #pragma unroll
         for (int wd = 0; wd < 4; ++wd) {
           const uint32_t u = words[wd] ^ 0x80808080u;
@@ -945,12 +969,14 @@ __global__ void __launch_bounds__(DecCfg<BT>::kThreads, DecCfg<BT>::kMinBlocks)
         c = 0;
         c_phase ^= 1;
       }
+      if (!p.scale_tma) {
 #pragma unroll
-      for (int g = 0; g < kGroups; ++g) {
+        for (int g = 0; g < kGroups; ++g) {
 #pragma unroll
-        for (int a = 0; a + 1 < kScaleAhead; ++a) sq[g][a] = sq[g][a + 1];
-        const int kb = it + kScaleAhead;
-        sq[g][kScaleAhead - 1] = (srow[g] != nullptr && kb < nkb) ? __ldg(srow[g] + kb) : 0.0f;
+          for (int a = 0; a + 1 < kScaleAhead; ++a) sq[g][a] = sq[g][a + 1];
+          const int kb = it + kScaleAhead;
+          sq[g][kScaleAhead - 1] = (srow[g] != nullptr && kb < nkb) ? __ldg(srow[g] + kb) : 0.0f;
+        }
       }
     }
   }
@@ -1064,7 +1090,10 @@ struct W8WideCfg {
   static constexpr int kXHalf = 256 * kRowBytes;       // 16 KB
   static constexpr int kXBytes = 2 * kXHalf;           // 32 KB
   static constexpr int kRawBytes = kBM * kBKw;         // 4 KB
-  static constexpr int kStageBytes = kABytes + kXBytes + kRawBytes;  // 44 KB
+  // The stage's scales: 128 rows x the aligned group of four 64-element
+  // blocks that holds its k-block (one 16-byte TMA row per feature).
+  static constexpr int kScaleBytes = kBM * 4 * 4;      // 2 KB
+  static constexpr int kStageBytes = kABytes + kXBytes + kRawBytes + kScaleBytes;  // 46 KB
   static constexpr int kStages = kTmaStore ? 4 : 5;
   static constexpr int kSlabBytes = 32 * kBM * 2;      // 32 tokens x 128 features, 8 KB
   static constexpr int kStagingBytes = kTmaStore ? 2 * kSlabBytes : 0;
@@ -1087,6 +1116,7 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore>::kThreads, 1)
                    const __grid_constant__ CUtensorMap tm_codes,
                    const __grid_constant__ CUtensorMap tm_p,
                    const __grid_constant__ CUtensorMap tm_bt,
+                   const __grid_constant__ CUtensorMap tm_scales,
                    const __grid_constant__ OutMaps out_maps, const W8Params p) {
   using C = W8WideCfg<kTmaStore>;
   constexpr int BT = C::BT;
@@ -1154,10 +1184,15 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore>::kThreads, 1)
           uint8_t *sx = sa + C::kABytes;
           if (it < p.num_kb) {
             const int k0 = it * C::kBKw;
-            ptx::mbar_expect_tx(&full[stage], C::kXBytes + C::kRawBytes);
+            ptx::mbar_expect_tx(&full[stage], C::kXBytes + C::kRawBytes +
+                                                  (p.scale_tma ? C::kScaleBytes : 0));
             ptx::tma_load_2d(sx, &tm_x, &full[stage], k0, t0);
             ptx::tma_load_2d(sx + C::kXHalf, &tm_x, &full[stage], k0, t0 + 256);
             ptx::tma_load_2d(sx + C::kXBytes, &tm_codes, &full[stage], k0, w0);
+            if (p.scale_tma) {
+              ptx::tma_load_2d(sx + C::kXBytes + C::kRawBytes, &tm_scales, &full[stage],
+                               (it / 2) & ~3, w0);
+            }
           } else {
             if (!dep_ready) {  // P comes from the down-projection launched just before
               ptx::grid_dep_wait();
@@ -1292,7 +1327,26 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore>::kThreads, 1)
           }
           ptx::fence_proxy_async_smem();
           ptx::named_bar_sync(1, 4 * kWarp);
-          if (elected) {
+          if (p.mc_out != nullptr) {
+            // One multicast write per 16 bytes reaches every rank's copy: the
+            // 128 epilogue threads each send 4 of the slab's 512 chunks
+            // (token j, 8 features). The slab buffer is reused two slabs
+            // later, after every thread has passed the next barrier.
+            const int epi = threadIdx.x - kEpiWarp0 * kWarp;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int q = epi + i * 128;
+              const int j = q >> 4;
+              const int f8 = (q & 15) * 8;
+              const int t = t0 + c * 32 + j;
+              if (t < p.M) {
+                const uint4 v = *reinterpret_cast<const uint4 *>(stg + j * kBM + f8);
+                uint16_t *dst = static_cast<uint16_t *>(p.mc_out) +
+                                static_cast<int64_t>(t) * p.ldo + p.out_col0 + w0 + f8;
+                ptx::multimem_st_v4(dst, v);
+              }
+            }
+          } else if (elected) {
             // The local copy first, then the peers (NVLink).
             ptx::tma_store_2d(&out_maps.map[p.self_out], stg, p.out_col0 + w0, t0 + c * 32);
             for (int d = 0; d < p.n_outs; ++d) {
@@ -1330,6 +1384,7 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore>::kThreads, 1)
     if constexpr (kTmaStore) {
       // Stores must finish reading shared memory before the CTA exits.
       if (threadIdx.x == kEpiWarp0 * kWarp) ptx::bulk_wait_all();
+      if (p.mc_out != nullptr) __threadfence_system();
     }
   } else if (warp >= kConvWarp0) {
     // ------------------------------------------------------------------ converters
@@ -1344,7 +1399,8 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore>::kThreads, 1)
     for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x) {
       const int w0 = (tile % p.n_tiles_w) * kBM;
       const int n = w0 + r;
-      const float *srow = n < p.N ? p.w_scales + static_cast<int64_t>(n) * p.kb_per_row : nullptr;
+      const float *srow = n < p.N && !p.scale_tma
+                              ? p.w_scales + static_cast<int64_t>(n) * p.kb_per_row : nullptr;
       float s_cur = srow != nullptr ? __ldg(srow) : 0.0f;
       bool ok = true;
       for (int it = 0; it < num_iters; ++it) {
@@ -1359,6 +1415,9 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore>::kThreads, 1)
           }
           uint8_t *sa = smem + stage * C::kStageBytes;
           const uint8_t *raw = sa + C::kABytes + C::kXBytes;
+          if (p.scale_tma) {
+            s_cur = reinterpret_cast<const float *>(raw + C::kRawBytes)[r * 4 + ((it / 2) & 3)];
+          }
           const uint4 codes = *reinterpret_cast<const uint4 *>(raw + r * C::kBKw + half * 16);
           const uint32_t words[4] = {codes.x, codes.y, codes.z, codes.w};
           const uint64_t sc2 = ptx::splat_f32x2(s_cur);
@@ -2498,6 +2557,7 @@ struct LinearArgs {
   int64_t ldy = 0;
   int64_t col0 = 0;
   int self_dest = 0;  // index in dest of this GPU's own copy
+  void *mc = nullptr;  // multicast address of the destination (multimem epilogue)
   // Row-group completion counters for a copy-engine all-gather (wide kernel).
   unsigned *done = nullptr;
   int rb_per_group = 1;
@@ -2575,6 +2635,13 @@ int launch_w8_decode(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
   p.w_scales = L.w_scales;
   p.out = static_cast<uint16_t *>(L.y);
   p.err = err;
+  CUtensorMap tm_scales;
+  std::memset(&tm_scales, 0, sizeof(tm_scales));
+  // scales as an fp32 [N, num_kb] matrix in boxes of 4 x 128: needs 16-byte rows
+  p.scale_tma = (p.num_kb % 4 == 0 && aligned_to(L.w_scales, 16)) ? 1 : 0;
+  if (p.scale_tma) {
+    if ((st = make_map(&tm_scales, L.w_scales, 4, p.num_kb, L.n, 4, kBM, false))) return st;
+  }
   const int n_tiles = static_cast<int>((L.n + kBM - 1) / kBM);
   // Largest K split (cluster size <= 8) that keeps the whole grid resident.
   const int slots = sm_count() * C::kMinBlocks;
@@ -2603,7 +2670,7 @@ int launch_w8_decode(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
   set_programmatic_dependency(attr[1]);
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  CFB_TRY_CUDA(cudaLaunchKernelEx(&cfg, kernel, tm_x, tm_codes, tm_p, tm_bt, p));
+  CFB_TRY_CUDA(cudaLaunchKernelEx(&cfg, kernel, tm_x, tm_codes, tm_p, tm_bt, tm_scales, p));
   return check_launch();
 }
 
@@ -2631,6 +2698,12 @@ int launch_w8_wide(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
   p.rank = r;
   p.w_scales = L.w_scales;
   p.kb_per_row = static_cast<int>(L.k / kBK);
+  CUtensorMap tm_scales;
+  std::memset(&tm_scales, 0, sizeof(tm_scales));
+  p.scale_tma = (p.kb_per_row % 4 == 0 && aligned_to(L.w_scales, 16)) ? 1 : 0;
+  if (p.scale_tma) {
+    if ((st = make_map(&tm_scales, L.w_scales, 4, p.kb_per_row, L.n, 4, kBM, false))) return st;
+  }
   OutMaps out_maps;
   std::memset(&out_maps, 0, sizeof(out_maps));
   if (L.n_dest > 0) {
@@ -2654,6 +2727,7 @@ int launch_w8_wide(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
   p.n_tiles = p.n_tiles_w * static_cast<int>((L.m + C::BT - 1) / C::BT);
   p.err = err;
   p.done = kTmaStore ? L.done : nullptr;
+  p.mc_out = kTmaStore ? L.mc : nullptr;
   p.rb_per_group = L.rb_per_group;
   p.n_groups = L.n_groups;
   auto kernel = w8_wide_kernel<kBf16, kTmaStore>;
@@ -2668,7 +2742,7 @@ int launch_w8_wide(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
   set_programmatic_dependency(attr[0]);
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  CFB_TRY_CUDA(cudaLaunchKernelEx(&cfg, kernel, tm_x, tm_codes, tm_p, tm_bt, out_maps, p));
+  CFB_TRY_CUDA(cudaLaunchKernelEx(&cfg, kernel, tm_x, tm_codes, tm_p, tm_bt, tm_scales, out_maps, p));
   return check_launch();
 }
 
@@ -3038,6 +3112,29 @@ int cf_lora_linear_int8_allgather(const void *x, const int8_t *w_codes, const fl
   L.self_dest = self_dest;
   L.ldy = ldy;
   L.col0 = col0;
+  if (w_scales != nullptr && !cfb::aligned_to(w_scales, 4)) return CF_ERR_MISALIGNED;
+  return cfb::validate_and_run(L, stream);
+}
+
+int cf_lora_linear_int8_allgather_mc(const void *x, const int8_t *w_codes, const float *w_scales,
+                                     const void *a, int a_layout, const void *b, int b_layout,
+                                     void *y_local, void *y_multicast, int64_t ldy, int64_t col0,
+                                     int64_t m, int64_t k, int64_t n, int64_t rank, float scale,
+                                     int dtype, void *workspace, size_t workspace_bytes,
+                                     cf_stream_t stream) {
+  if (y_local == nullptr || y_multicast == nullptr) return CF_ERR_INVALID_ARGUMENT;
+  if (!cfb::aligned_to(y_local, 16) || !cfb::aligned_to(y_multicast, 16)) return CF_ERR_MISALIGNED;
+  if (ldy <= 0 || col0 < 0 || col0 + n > ldy) return CF_ERR_INVALID_ARGUMENT;
+  if (ldy % 8 != 0 || col0 % 8 != 0 || ldy > INT32_MAX || n % 128 != 0) return CF_ERR_UNSUPPORTED;
+  void *const dest[1] = {y_local};
+  cfb::LinearArgs L{x, w_codes, CF_LAYOUT_T, w_scales, a, a_layout, b, b_layout,
+                    y_local, m, k, n, rank, scale, dtype, workspace, workspace_bytes, true};
+  L.n_dest = 1;
+  L.dest = dest;
+  L.self_dest = 0;
+  L.ldy = ldy;
+  L.col0 = col0;
+  L.mc = y_multicast;
   if (w_scales != nullptr && !cfb::aligned_to(w_scales, 4)) return CF_ERR_MISALIGNED;
   return cfb::validate_and_run(L, stream);
 }

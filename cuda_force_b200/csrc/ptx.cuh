@@ -170,6 +170,16 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void 
       : "memory");
 }
 
+// 16-byte store to a multicast (NVLink SHARP) address: the switch writes it
+// into every GPU's memory bound to the multicast object. A plain register
+// store; no TMA, no cluster multicast.
+__device__ __forceinline__ void multimem_st_v4(void *mc_addr, uint4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(
+                   reinterpret_cast<uint64_t>(mc_addr)),
+               "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tensor_map(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

@@ -109,6 +109,12 @@ class FusedGatherLinear:
     so the exchange overlaps the GEMM tile by tile and no relayout is needed.
     A device-side barrier after the launch orders the ranks before y is read.
 
+    ``mode="mc"`` writes through the buffer's NVLink multicast address
+    (``cf_lora_linear_int8_allgather_mc``): each 16-byte piece of this rank's
+    columns leaves the GPU once and the switch delivers it to every rank's
+    copy, instead of one store per peer. It needs multicast support
+    (``has_multicast``).
+
     ``mode="ce"`` moves the exchange to the copy engines
     (``cf_lora_linear_int8_allgather_ce``): the kernel writes only the local
     copy of y and counts finished tiles per row group, and one copy stream per
@@ -117,7 +123,7 @@ class FusedGatherLinear:
 
     def __init__(self, m: int, n: int, dtype: torch.dtype, device: torch.device,
                  group: dist.ProcessGroup | None = None, mode: str = "kernel"):
-        if mode not in ("kernel", "ce"):
+        if mode not in ("kernel", "ce", "mc"):
             raise ValueError(f"unknown exchange mode {mode!r}")
         self.mode = mode
         import torch.distributed._symmetric_memory as symm_mem
@@ -133,6 +139,25 @@ class FusedGatherLinear:
 
         self._dest = (ctypes.c_void_p * self.world)(*[t.data_ptr() for t in peers])
         self.m, self.n = m, n
+        self.mc = 0
+        if mode == "mc":
+            if not self.has_multicast(device):
+                raise RuntimeError("NVLink multicast is not available for this group")
+            local = peers[self.rank].data_ptr()
+            assert local == self.y.data_ptr()
+            # the multicast mapping covers the allocation the way each rank's
+            # unicast mapping does, so y sits at the same offset in both
+            self.mc = self.handle.multicast_ptr + (local - self.handle.buffer_ptrs[self.rank])
+
+    @staticmethod
+    def has_multicast(device: torch.device) -> bool:
+        from torch._C._distributed_c10d import _SymmetricMemory
+
+        try:
+            return bool(_SymmetricMemory.has_multicast_support(
+                torch._C._autograd.DeviceType.CUDA, device.index))
+        except Exception:  # noqa: BLE001 - treated as unsupported
+            return False
 
     def __call__(self, x, w_codes, w_scales, lora_a, lora_b, scale: float) -> torch.Tensor:
         import ctypes
@@ -151,7 +176,14 @@ class FusedGatherLinear:
         dtype = _abi.CF_DTYPE_BF16 if x.dtype == torch.bfloat16 else _abi.CF_DTYPE_F16
         stream = ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)
         p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
-        if self.mode == "ce":
+        if self.mode == "mc":
+            ws_bytes = lib.cf_lora_linear_workspace_bytes(m, r)
+            ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
+            _abi.check(lib.cf_lora_linear_int8_allgather_mc(
+                p(x), p(w_codes), p(w_scales), p(lora_a), a_layout, p(lora_b), b_layout,
+                p(self.y), ctypes.c_void_p(self.mc), self.n, self.rank * width, m, k, width, r,
+                float(scale), dtype, p(ws), ws_bytes, stream), "cf_lora_linear_int8_allgather_mc")
+        elif self.mode == "ce":
             ws_bytes = lib.cf_lora_linear_int8_allgather_ce_workspace_bytes(m, r)
             ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
             _abi.check(lib.cf_lora_linear_int8_allgather_ce(

@@ -175,6 +175,25 @@ CF_API int cf_lora_linear_int8_allgather(const void *x, const int8_t *w_codes,
                                          float scale, int dtype, void *workspace,
                                          size_t workspace_bytes, cf_stream_t stream);
 
+/* cf_lora_linear_int8_allgather with the exchange done by NVLink SHARP
+ * multicast (no counterpart in the reference, which has no multi-GPU path for
+ * this op; it stands in for the NCCL all-gather of the column-sharded linear).
+ * y_multicast is the multicast address of a [m, ldy] buffer that every rank
+ * has bound to one multicast object (y_local is this GPU's own copy of it):
+ * each 16-byte piece of this call's columns [col0, col0 + n) is written once
+ * with a multimem store, and the switch delivers it to every rank's copy, so
+ * each rank sends its slice over NVLink once instead of once per peer. The
+ * caller orders the ranks afterwards (a barrier) before reading y. Same
+ * shape rules as cf_lora_linear_int8_allgather (n a multiple of 128, ldy and
+ * col0 multiples of 8). */
+CF_API int cf_lora_linear_int8_allgather_mc(const void *x, const int8_t *w_codes,
+                                            const float *w_scales, const void *a, int a_layout,
+                                            const void *b, int b_layout, void *y_local,
+                                            void *y_multicast, int64_t ldy, int64_t col0,
+                                            int64_t m, int64_t k, int64_t n, int64_t rank,
+                                            float scale, int dtype, void *workspace,
+                                            size_t workspace_bytes, cf_stream_t stream);
+
 /* Workspace bytes of cf_lora_linear_int8_allgather_ce: the down-projection
  * workspace of cf_lora_linear_workspace_bytes plus 256 bytes of row-group
  * counters. */

@@ -25,13 +25,29 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 OUT_DIR = HERE / "_ref"
 OUT = OUT_DIR / "cudaforge_ref_cpu.so"
-REFERENCE = Path(os.environ.get("CUDAFORGE_REFERENCE", "/root/reference"))
+
+
+def reference_root() -> Path | None:
+    """The reference checkout: ``$CUDAFORGE_REFERENCE``, else BASELINE.json's
+    ``reference_path``; None when neither names one."""
+    env = os.environ.get("CUDAFORGE_REFERENCE")
+    if env:
+        return Path(env)
+    baseline = HERE.parent / "BASELINE.json"
+    if baseline.exists():
+        import json
+
+        path = json.loads(baseline.read_text()).get("reference_path")
+        if path:
+            return Path(path)
+    return None
 
 
 def build(force: bool = False) -> Path | None:
     """Builds the library if the reference tree is present; returns its path or None."""
-    src = REFERENCE / "cpp" / "src" / "bindings.cpp"
-    if not src.exists():
+    root = reference_root()
+    src = root / "cpp" / "src" / "bindings.cpp" if root is not None else None
+    if src is None or not src.exists():
         return OUT if OUT.exists() else None
     if OUT.exists() and not force and OUT.stat().st_mtime > src.stat().st_mtime:
         return OUT
@@ -42,8 +58,8 @@ def build(force: bool = False) -> Path | None:
     torch_lib = Path(torch.__file__).resolve().parent / "lib"
     includes = cpp_extension.include_paths() + [
         sysconfig.get_paths()["include"],
-        str(REFERENCE / "cpp" / "include"),
-        str(REFERENCE / "cuda" / "include"),
+        str(root / "cpp" / "include"),
+        str(root / "cuda" / "include"),
     ]
     tmp = OUT.with_suffix(".so.tmp")
     cmd = [

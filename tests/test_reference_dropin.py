@@ -23,8 +23,9 @@ import pytest
 from oracle import build_ref
 
 ROOT = Path(__file__).resolve().parents[1]
-REF_PKG = build_ref.REFERENCE / "python" / "cudaforge"
-REF_TESTS = build_ref.REFERENCE / "tests" / "python"
+_REF_ROOT = build_ref.reference_root() or ROOT / "missing-reference"
+REF_PKG = _REF_ROOT / "python" / "cudaforge"
+REF_TESTS = _REF_ROOT / "tests" / "python"
 DROPIN = ROOT / "oracle" / "_ref" / "dropin"
 
 STUB = '''"""The reference package with another build's extension module first on its path."""
@@ -36,23 +37,25 @@ exec(compile(open(__file__).read(), __file__, "exec"))
 '''
 
 
-def _make_stub() -> Path:
-    pkg = DROPIN / "cudaforge"
+def make_stub(dropin: Path, ref_pkg: Path) -> Path:
+    """A ``cudaforge`` package under ``dropin`` that runs the reference package at
+    ``ref_pkg`` with this build's extension modules first on its path."""
+    pkg = dropin / "cudaforge"
     pkg.mkdir(parents=True, exist_ok=True)
-    (pkg / "__init__.py").write_text(STUB.format(ref=str(REF_PKG)))
+    (pkg / "__init__.py").write_text(STUB.format(ref=str(ref_pkg)))
     for name in ("_C.so", "libcudaforge_b200.so"):
         link = pkg / name
         if link.is_symlink() or link.exists():
             link.unlink()
         link.symlink_to(ROOT / "cuda_force_b200" / name)
-    return DROPIN
+    return dropin
 
 
 @pytest.mark.skipif(not (REF_PKG / "ops.py").exists(), reason="reference tree not available")
 def test_reference_operator_tests_pass_with_this_extension():
-    root = _make_stub()
+    root = make_stub(DROPIN, REF_PKG)
     env = dict(os.environ, PYTHONDONTWRITEBYTECODE="1",
-               PYTHONPATH=os.pathsep.join([str(root), str(build_ref.REFERENCE)]))
+               PYTHONPATH=os.pathsep.join([str(root), str(_REF_ROOT)]))
     files = [str(REF_TESTS / f) for f in ("test_ops.py", "test_autograd.py",
                                            "test_constant_parity.py", "test_lora.py")]
     probe = ("from cudaforge import ops; r = ops.backend_report(); "
