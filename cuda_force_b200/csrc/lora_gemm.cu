@@ -115,6 +115,20 @@ __device__ __forceinline__ bool aborted(const int *abort_flag) {
   return *reinterpret_cast<const volatile int *>(abort_flag) != 0;
 }
 
+// Tile t of a grid of `rows` x `cols` tiles, walked in bands of `band` rows
+// with the row index fastest inside a band: the CTAs of one wave then share
+// a few column blocks (each read from DRAM about once per band) while the
+// band's row blocks stay resident in L2.
+__device__ __forceinline__ void band_order(int t, int rows, int cols, int band, int &row,
+                                           int &col) {
+  const int per_band = band * cols;
+  const int b = t / per_band;
+  const int in_band = min(band, rows - b * band);
+  const int i = t - b * per_band;
+  row = b * band + i % in_band;
+  col = i / in_band;
+}
+
 template <int BN, bool kBf16>
 __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
     lora_gemm_kernel(const __grid_constant__ CUtensorMap tm_a,
@@ -913,11 +927,13 @@ __global__ void __launch_bounds__(DecCfg<BT>::kThreads, DecCfg<BT>::kMinBlocks)
         break;
       }
       uint4 codes[kGroups];
-      const uint8_t *raw = raw_ring + rs * C::kRawBytes + sub * kBK;
+      const uint8_t *raw = raw_ring + rs * C::kRawBytes;
 #pragma unroll
       for (int g = 0; g < kGroups; ++g) {
+        // row r's 16-byte chunk j sits at chunk j ^ (r & 7) (TMA 128-byte swizzle)
         const int r = (cw + g * kConvWarps) * 8 + sub_row;
-        codes[g] = *reinterpret_cast<const uint4 *>(raw + r * (kBK * C::kRawKb) + chunk * 16);
+        const int j = (sub * (kBK / 16) + chunk) ^ (r & 7);
+        codes[g] = *reinterpret_cast<const uint4 *>(raw + r * (kBK * C::kRawKb) + j * 16);
       }
       if (__any_sync(0xffffffffu,
                      !ptx::mbar_wait(&conv_empty[c], c_phase ^ 1u, kWaitLimitNs, false))) {
@@ -1519,6 +1535,8 @@ struct F32Params {
   float out_scale;
   float *out;       // [M, ldo] fp32
   int n_tiles_n;
+  int n_tiles_m;
+  int band_m;       // row blocks per band of the tile walk (band_order)
   int n_tiles;
   unsigned *err;
 };
@@ -1586,8 +1604,10 @@ __global__ void __launch_bounds__(F32Cfg::kThreads, 1)
       uint32_t outstanding = 0, issue_parity = 0;
       bool dep_ready = false;
       for (int tile = blockIdx.x; tile < p.n_tiles && !aborted(abort_flag); tile += gridDim.x) {
-        const int m0 = (tile / p.n_tiles_n) * 128;
-        const int n0 = (tile % p.n_tiles_n) * C::BN;
+        int mb, nb;
+        band_order(tile, p.n_tiles_m, p.n_tiles_n, p.band_m, mb, nb);
+        const int m0 = mb * 128;
+        const int n0 = nb * C::BN;
         for (int it = 0; it < num_iters; ++it) {
           if (!ptx::mbar_wait(&empty[stage], phase ^ 1)) {
             record_timeout(p.err, abort_flag);
@@ -1697,8 +1717,10 @@ __global__ void __launch_bounds__(F32Cfg::kThreads, 1)
         break;
       }
       ptx::tc_fence_after();
-      const int m0 = (tile / p.n_tiles_n) * 128;
-      const int n0 = (tile % p.n_tiles_n) * C::BN;
+      int mb, nb;
+      band_order(tile, p.n_tiles_m, p.n_tiles_n, p.band_m, mb, nb);
+      const int m0 = mb * 128;
+      const int n0 = nb * C::BN;
       const int row = m0 + quarter * 32 + lane;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * C::BN;
       float *out_row = p.out + static_cast<int64_t>(row) * p.ldo;
@@ -2164,6 +2186,7 @@ struct SwigluParams {
   const float *g_scales;
   const float *u_scales;
   int n_tiles_w;
+  int n_tiles_t;            // 256-token blocks; tiles run token-fastest over all of them
   int n_tiles;
   unsigned *err;
 };
@@ -2225,8 +2248,10 @@ __global__ void __launch_bounds__(SwigluCfg::kThreads, 1)
       uint32_t phase = 0;
       uint32_t outstanding = 0, issue_parity = 0;
       for (int tile = blockIdx.x; tile < p.n_tiles && !aborted(abort_flag); tile += gridDim.x) {
-        const int w0 = (tile % p.n_tiles_w) * kBM;
-        const int t0 = (tile / p.n_tiles_w) * BT;
+        int tb, fb;
+        band_order(tile, p.n_tiles_t, p.n_tiles_w, p.n_tiles_t, tb, fb);
+        const int w0 = fb * kBM;
+        const int t0 = tb * BT;
         for (int it = 0; it < p.num_kb; ++it) {
           if (!ptx::mbar_wait(&empty[stage], phase ^ 1)) {
             record_timeout(p.err, abort_flag);
@@ -2306,8 +2331,10 @@ __global__ void __launch_bounds__(SwigluCfg::kThreads, 1)
     uint32_t slab = 0;
     int local = 0;
     for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x, ++local) {
-      const int w0 = (tile % p.n_tiles_w) * kBM;
-      const int t0 = (tile / p.n_tiles_w) * BT;
+      int tb, fb;
+      band_order(tile, p.n_tiles_t, p.n_tiles_w, p.n_tiles_t, tb, fb);
+      const int w0 = fb * kBM;
+      const int t0 = tb * BT;
       // The four epilogue warps share named barriers, so they leave together.
       const bool got = ptx::warp_wait(tmem_full, static_cast<uint32_t>(local & 1));
       if (!ptx::named_bar_all(1, 4 * kWarp, got)) {
@@ -2385,7 +2412,9 @@ __global__ void __launch_bounds__(SwigluCfg::kThreads, 1)
     int stage = 0;
     uint32_t phase = 0;
     for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x) {
-      const int w0 = (tile % p.n_tiles_w) * kBM;
+      int tb, fb;
+      band_order(tile, p.n_tiles_t, p.n_tiles_w, p.n_tiles_t, tb, fb);
+      const int w0 = fb * kBM;
       const int n = w0 + r;
       const float *srow =
           n < p.N ? (wt == 0 ? p.g_scales : p.u_scales) + static_cast<int64_t>(n) * p.kb_per_row
@@ -2616,7 +2645,9 @@ int launch_w8_decode(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
   CUtensorMap tm_x, tm_codes, tm_p, tm_bt;
   int st = CF_OK;
   if ((st = make_map(&tm_x, L.x, 2, L.k, L.m, kBK, BT, true))) return st;
-  if ((st = make_map(&tm_codes, L.w, 1, L.k, L.n, kBK * C::kRawKb, kBM, false))) return st;
+  // 128-byte swizzled code rows: a converter warp's eight rows then read
+  // eight different bank groups instead of the same one.
+  if ((st = make_map(&tm_codes, L.w, 1, L.k, L.n, kBK * C::kRawKb, kBM, true))) return st;
   if ((st = make_map(&tm_p, L.ws, 2, r, L.m, r, BT, true))) return st;
   DecParams p{};
   if (L.b_layout == CF_LAYOUT_REF) {
@@ -2802,6 +2833,15 @@ int run_linear(const LinearArgs &L, cudaStream_t stream) {
   return launch_gemm<BN, kBf16>(tm_x, tm_w, tm_p, tm_b, p, stream);
 }
 
+// Row blocks per band of the fp32 kernel's tile walk: as many 128-row blocks
+// of the [m, k] fp32 A operand as fit in 64 MB, so a band stays in L2 while
+// the B column blocks stream past it.
+int f32_band(int m_tiles, int64_t k) {
+  const int64_t block_bytes = 128 * std::max<int64_t>(k, 1) * 4;
+  const int64_t fit = (int64_t{64} << 20) / block_bytes;
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(m_tiles, fit)));
+}
+
 // fp32 call: two launches of lora_f32_kernel (down-projection, then the main
 // product with the adapter as extra k-blocks), the second overlapping the
 // first through programmatic dependent launch.
@@ -2855,6 +2895,8 @@ int run_linear_f32(const LinearArgs &L, cudaStream_t stream) {
   d.out_scale = L.scale;
   d.out = static_cast<float *>(L.ws);
   d.n_tiles_n = 1;
+  d.n_tiles_m = m_tiles;
+  d.band_m = m_tiles;
   d.n_tiles = m_tiles;
   d.err = err;
   if ((st = launch_f32(tm_x, tm_a, tm_x, tm_a, d, false, stream))) return st;
@@ -2868,6 +2910,7 @@ int run_linear_f32(const LinearArgs &L, cudaStream_t stream) {
   p.out_scale = 1.0f;
   p.out = static_cast<float *>(L.y);
   p.n_tiles_n = static_cast<int>((L.n + F32Cfg::BN - 1) / F32Cfg::BN);
+  p.band_m = f32_band(m_tiles, L.k);
   p.n_tiles = m_tiles * p.n_tiles_n;
   return launch_f32(tm_x, tm_w, tm_p, tm_b, p, true, stream);
 }
@@ -2895,7 +2938,9 @@ int run_matmul_f32(const float *a, const float *b, int b_layout, float *c, int64
   p.out_scale = 1.0f;
   p.out = c;
   p.n_tiles_n = static_cast<int>((n + F32Cfg::BN - 1) / F32Cfg::BN);
-  p.n_tiles = static_cast<int>((m + 127) / 128) * p.n_tiles_n;
+  p.n_tiles_m = static_cast<int>((m + 127) / 128);
+  p.band_m = f32_band(p.n_tiles_m, k);
+  p.n_tiles = p.n_tiles_m * p.n_tiles_n;
   p.err = err;
   return launch_f32(tm_a, tm_b, tm_a, tm_b, p, false, stream);
 }
@@ -2953,7 +2998,8 @@ int run_w8_swiglu(const void *x, const int8_t *g_codes, const float *g_scales,
   p.g_scales = g_scales;
   p.u_scales = u_scales;
   p.n_tiles_w = static_cast<int>((n + kBM - 1) / kBM);
-  p.n_tiles = p.n_tiles_w * static_cast<int>((m + C::BT - 1) / C::BT);
+  p.n_tiles_t = static_cast<int>((m + C::BT - 1) / C::BT);
+  p.n_tiles = p.n_tiles_w * p.n_tiles_t;
   p.err = err;
   if ((st = allow_dynamic_smem<w8_swiglu_kernel<kBf16>>(C::kSmemBytes))) return st;
   const int grid = std::max(1, std::min(p.n_tiles, sm_count()));
