@@ -2834,11 +2834,11 @@ int run_linear(const LinearArgs &L, cudaStream_t stream) {
 }
 
 // Row blocks per band of the fp32 kernel's tile walk: as many 128-row blocks
-// of the [m, k] fp32 A operand as fit in 64 MB, so a band stays in L2 while
+// of the [m, k] fp32 A operand as fit in 32 MB, so a band stays in L2 while
 // the B column blocks stream past it.
 int f32_band(int m_tiles, int64_t k) {
   const int64_t block_bytes = 128 * std::max<int64_t>(k, 1) * 4;
-  const int64_t fit = (int64_t{64} << 20) / block_bytes;
+  const int64_t fit = (int64_t{32} << 20) / block_bytes;
   return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(m_tiles, fit)));
 }
 
