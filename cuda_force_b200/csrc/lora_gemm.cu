@@ -1097,20 +1097,26 @@ __global__ void __launch_bounds__(DecCfg<BT>::kThreads, DecCfg<BT>::kMinBlocks)
 // ring stays 5 stages deep. The adapter runs as rank/16 extra iterations of
 // one K = 16 step each (A = 16 columns of B^T, B = 16 columns of P).
 // ---------------------------------------------------------------------------
-template <bool kTmaStore>
+// kBT = 512: one 128 x 512 fp32 accumulator fills TMEM, each converted
+// weight tile feeds two N = 256 MMAs. kBT = 256 (the all-gather calls): two
+// 128 x 256 accumulators, so a tile's epilogue, whose stores cross NVLink,
+// runs while the next tile's main loop fills the other accumulator.
+template <bool kTmaStore, int kBT = 512>
 struct W8WideCfg {
-  static constexpr int BT = 512;
+  static constexpr int BT = kBT;
+  static constexpr int kHalves = kBT / 256;            // N = 256 MMAs per k-step
+  static constexpr int kAccs = 512 / kBT;              // TMEM accumulators
   static constexpr int kBKw = 32;                      // k-block width (elements)
   static constexpr int kRowBytes = kBKw * 2;           // 64 -> 64-byte swizzle
   static constexpr int kABytes = kBM * kRowBytes;      // 8 KB
   static constexpr int kXHalf = 256 * kRowBytes;       // 16 KB
-  static constexpr int kXBytes = 2 * kXHalf;           // 32 KB
+  static constexpr int kXBytes = kHalves * kXHalf;     // 32 KB (16 KB at kBT = 256)
   static constexpr int kRawBytes = kBM * kBKw;         // 4 KB
   // The stage's scales: 128 rows x the aligned group of four 64-element
   // blocks that holds its k-block (one 16-byte TMA row per feature).
   static constexpr int kScaleBytes = kBM * 4 * 4;      // 2 KB
   static constexpr int kStageBytes = kABytes + kXBytes + kRawBytes + kScaleBytes;  // 46 KB
-  static constexpr int kStages = kTmaStore ? 4 : 5;
+  static constexpr int kStages = kBT == 256 ? 6 : (kTmaStore ? 4 : 5);
   static constexpr int kSlabBytes = 32 * kBM * 2;      // 32 tokens x 128 features, 8 KB
   static constexpr int kStagingBytes = kTmaStore ? 2 * kSlabBytes : 0;
   static constexpr int kThreads = 512;
@@ -1126,15 +1132,15 @@ struct OutMaps {
   CUtensorMap map[kMaxOuts];
 };
 
-template <bool kBf16, bool kTmaStore>
-__global__ void __launch_bounds__(W8WideCfg<kTmaStore>::kThreads, 1)
+template <bool kBf16, bool kTmaStore, int kBT>
+__global__ void __launch_bounds__(W8WideCfg<kTmaStore, kBT>::kThreads, 1)
     w8_wide_kernel(const __grid_constant__ CUtensorMap tm_x,
                    const __grid_constant__ CUtensorMap tm_codes,
                    const __grid_constant__ CUtensorMap tm_p,
                    const __grid_constant__ CUtensorMap tm_bt,
                    const __grid_constant__ CUtensorMap tm_scales,
                    const __grid_constant__ OutMaps out_maps, const W8Params p) {
-  using C = W8WideCfg<kTmaStore>;
+  using C = W8WideCfg<kTmaStore, kBT>;
   constexpr int BT = C::BT;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
@@ -1144,9 +1150,9 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore>::kThreads, 1)
   uint64_t *full = bars;
   uint64_t *empty = bars + C::kStages;
   uint64_t *conv_full = bars + 2 * C::kStages;
-  uint64_t *tmem_full = bars + 3 * C::kStages;
-  uint64_t *tmem_empty = tmem_full + 1;
-  uint64_t *drain = tmem_empty + 1;
+  uint64_t *tmem_full = bars + 3 * C::kStages;  // [kAccs]
+  uint64_t *tmem_empty = tmem_full + C::kAccs;  // [kAccs]
+  uint64_t *drain = tmem_empty + C::kAccs;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
   int *abort_flag = reinterpret_cast<int *>(tmem_slot + 1);
 
@@ -1166,8 +1172,10 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore>::kThreads, 1)
       ptx::mbar_init(&empty[s], 1);
       ptx::mbar_init(&conv_full[s], kConvThreads / kWarp);
     }
-    ptx::mbar_init(tmem_full, 1);
-    ptx::mbar_init(tmem_empty, 4);
+    for (int a = 0; a < C::kAccs; ++a) {
+      ptx::mbar_init(&tmem_full[a], 1);
+      ptx::mbar_init(&tmem_empty[a], 4);
+    }
     ptx::mbar_init(drain, 1);
     *abort_flag = 0;
     ptx::fence_mbar_init();
@@ -1202,8 +1210,9 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore>::kThreads, 1)
             const int k0 = it * C::kBKw;
             ptx::mbar_expect_tx(&full[stage], C::kXBytes + C::kRawBytes +
                                                   (p.scale_tma ? C::kScaleBytes : 0));
-            ptx::tma_load_2d(sx, &tm_x, &full[stage], k0, t0);
-            ptx::tma_load_2d(sx + C::kXHalf, &tm_x, &full[stage], k0, t0 + 256);
+            for (int h = 0; h < C::kHalves; ++h) {
+              ptx::tma_load_2d(sx + h * C::kXHalf, &tm_x, &full[stage], k0, t0 + h * 256);
+            }
             ptx::tma_load_2d(sx + C::kXBytes, &tm_codes, &full[stage], k0, w0);
             if (p.scale_tma) {
               ptx::tma_load_2d(sx + C::kXBytes + C::kRawBytes, &tm_scales, &full[stage],
@@ -1223,8 +1232,9 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore>::kThreads, 1)
             } else {
               ptx::tma_load_2d(sa, &tm_bt, &full[stage], j0, w0);
             }
-            ptx::tma_load_2d(sx, &tm_p, &full[stage], j0, t0);
-            ptx::tma_load_2d(sx + C::kXHalf, &tm_p, &full[stage], j0, t0 + 256);
+            for (int h = 0; h < C::kHalves; ++h) {
+              ptx::tma_load_2d(sx + h * C::kXHalf, &tm_p, &full[stage], j0, t0 + h * 256);
+            }
           }
           outstanding |= 1u << stage;
           issue_parity = (issue_parity & ~(1u << stage)) | (phase << stage);
@@ -1251,7 +1261,9 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore>::kThreads, 1)
       int local = 0;
       for (int tile = blockIdx.x; tile < p.n_tiles && !aborted(abort_flag);
            tile += gridDim.x, ++local) {
-        if (!ptx::mbar_wait(tmem_empty, static_cast<uint32_t>(local & 1) ^ 1u)) {
+        const int acc = local % C::kAccs;
+        const uint32_t acc_base = tmem_base + acc * 256;
+        if (!ptx::mbar_wait(&tmem_empty[acc], static_cast<uint32_t>((local / C::kAccs) & 1) ^ 1u)) {
           record_timeout(p.err, abort_flag);
           break;
         }
@@ -1272,8 +1284,8 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore>::kThreads, 1)
           if (main_kb) {
             for (int ks = 0; ks < C::kBKw / kUmmaK; ++ks) {
               const uint64_t adesc = kmajor_desc(sa, C::kRowBytes, ks);
-              for (int h = 0; h < 2; ++h) {
-                ptx::mma_f16(tmem_base + h * 256, adesc,
+              for (int h = 0; h < C::kHalves; ++h) {
+                ptx::mma_f16(acc_base + h * 256, adesc,
                              kmajor_desc(sx + h * C::kXHalf, C::kRowBytes, ks), idesc_main,
                              (it > 0 || ks > 0) ? 1u : 0u);
               }
@@ -1281,8 +1293,8 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore>::kThreads, 1)
           } else {
             const uint64_t adesc = p.extra_b_mn ? mnmajor_desc(sa, 128, kUmmaK * 128, 0)
                                                 : kmajor_desc(sa, kUmmaK * 2, 0);
-            for (int h = 0; h < 2; ++h) {
-              ptx::mma_f16(tmem_base + h * 256, adesc,
+            for (int h = 0; h < C::kHalves; ++h) {
+              ptx::mma_f16(acc_base + h * 256, adesc,
                            kmajor_desc(sx + h * C::kXHalf, kUmmaK * 2, 0), idesc_extra,
                            it > 0 ? 1u : 0u);
             }
@@ -1294,7 +1306,7 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore>::kThreads, 1)
           }
         }
         if (!ok) break;
-        ptx::mma_commit(tmem_full);
+        ptx::mma_commit(&tmem_full[acc]);
       }
       if (aborted(abort_flag)) {
         ptx::mma_commit(drain);
@@ -1312,14 +1324,16 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore>::kThreads, 1)
       const int t0 = (tile / p.n_tiles_w) * BT;
       // With the TMA-store path the four epilogue warps share named barriers,
       // so they decide together whether to go on.
-      bool ok = ptx::warp_wait(tmem_full, static_cast<uint32_t>(local & 1));
+      const int acc = local % C::kAccs;
+      bool ok = ptx::warp_wait(&tmem_full[acc], static_cast<uint32_t>((local / C::kAccs) & 1));
       if constexpr (kTmaStore) ok = ptx::named_bar_all(1, 4 * kWarp, ok);
       if (!ok) {
         if (lane == 0) record_timeout(p.err, abort_flag);
         break;
       }
       ptx::tc_fence_after();
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+      const uint32_t t_row =
+          tmem_base + acc * 256 + (static_cast<uint32_t>(quarter * 32) << 16);
       const int n = w0 + row;
       uint16_t *out = static_cast<uint16_t *>(p.outs[0]);
 #pragma unroll 1
@@ -1385,7 +1399,7 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore>::kThreads, 1)
         }
       }
       ptx::tc_fence_before();
-      ptx::warp_arrive(tmem_empty);
+      ptx::warp_arrive(&tmem_empty[acc]);
       if constexpr (kTmaStore) {
         if (p.done != nullptr && threadIdx.x == kEpiWarp0 * kWarp) {
           // Publish the tile: its stores have completed (not just read
@@ -2705,9 +2719,9 @@ int launch_w8_decode(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
   return check_launch();
 }
 
-template <bool kBf16, bool kTmaStore>
+template <bool kBf16, bool kTmaStore, int kBT>
 int launch_w8_wide(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
-  using C = W8WideCfg<kTmaStore>;
+  using C = W8WideCfg<kTmaStore, kBT>;
   const int r = static_cast<int>(L.r);
   CUtensorMap tm_x, tm_codes, tm_p, tm_bt;
   int st = CF_OK;
@@ -2761,8 +2775,10 @@ int launch_w8_wide(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
   p.mc_out = kTmaStore ? L.mc : nullptr;
   p.rb_per_group = L.rb_per_group;
   p.n_groups = L.n_groups;
-  auto kernel = w8_wide_kernel<kBf16, kTmaStore>;
-  if (int st_ = allow_dynamic_smem<w8_wide_kernel<kBf16, kTmaStore>>(C::kSmemBytes)) return st_;
+  auto kernel = w8_wide_kernel<kBf16, kTmaStore, kBT>;
+  if (int st_ = allow_dynamic_smem<w8_wide_kernel<kBf16, kTmaStore, kBT>>(C::kSmemBytes)) {
+    return st_;
+  }
   const int grid = std::max(1, std::min(p.n_tiles, sm_count()));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
@@ -2792,7 +2808,13 @@ int run_linear(const LinearArgs &L, cudaStream_t stream) {
     if (L.n_dest == 0 && L.m <= 32) return launch_w8_decode<32, kBf16>(L, err, stream);
     if (L.n_dest == 0 && L.m <= 64) return launch_w8_decode<64, kBf16>(L, err, stream);
     if (L.n_dest == 0 && L.m <= 128) return launch_w8_decode<128, kBf16>(L, err, stream);
-    return launch_w8_wide<kBf16, true>(L, err, stream);
+    // The peer-store and multicast all-gathers run 256-token tiles with two
+    // accumulators, so NVLink stores overlap the next tile's main loop. The
+    // copy-engine all-gather counts 512-token row blocks.
+    if ((L.n_dest > 1 || L.mc != nullptr) && L.done == nullptr) {
+      return launch_w8_wide<kBf16, true, 256>(L, err, stream);
+    }
+    return launch_w8_wide<kBf16, true, 512>(L, err, stream);
   }
 
   constexpr int BN = 256;
