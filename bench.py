@@ -704,6 +704,117 @@ class W8Prefill(LoraLinear):
     main_kernel = "w8_wide_kernel (128 x 512 tiles, TMA-store epilogue)"
 
 
+class NormW8Prefill(W8Prefill):
+    """Residual add + RMSNorm folded into the config 4 prefill W8 + LoRA linear."""
+
+    name = "rmsnorm_w8_lora_prefill_4096x4096x11008"
+    main_kernel = ("norm statistics pass + w8_wide_kernel with the norm weight in the "
+                   "conversion and the row scale in the epilogue")
+
+    def __init__(self, dist: Dist, _layers: int = 0):
+        super().__init__(dist, _layers)
+        self.metric = ("residual + RMSNorm + W8+LoRA linear TFLOP/s of the linear "
+                       "(x [4096,4096], W [11008,4096], r 16)")
+
+    def config(self) -> dict:
+        c = super().config()
+        c["norm"] = "residual add + RMSNorm (eps 1e-6), weight 1 + N(0,0.1), folded into the linear"
+        return c
+
+    def setup(self, reference: bool = False) -> None:
+        super().setup(reference)
+        dev = self.dist.device
+        g = torch.Generator(device=dev).manual_seed(13)
+        self.res = torch.randn(self.m, self.k, device=dev, generator=g).to(torch.bfloat16)
+        self.nw = (1 + 0.1 * torch.randn(self.k, device=dev, generator=g)).to(torch.bfloat16)
+        if reference:
+            return
+        self.res_out = torch.empty_like(self.x)
+        self.nws_bytes = self.lib.cf_rmsnorm_lora_linear_int8_workspace_bytes(self.m, self.k, self.r)
+        self.nws = torch.empty(self.nws_bytes, dtype=torch.uint8, device=dev)
+        self.launches_per_step = 4
+
+    def step(self, stream) -> None:
+        from cuda_force_b200 import _abi
+
+        _abi.check(self.lib.cf_rmsnorm_lora_linear_int8(
+            self.x.data_ptr(), self.res.data_ptr(), self.nw.data_ptr(), 1e-6,
+            self.codes.data_ptr(), self.scales.data_ptr(), self.a.data_ptr(), _abi.CF_LAYOUT_REF,
+            self.b.data_ptr(), _abi.CF_LAYOUT_REF, self.y.data_ptr(), self.res_out.data_ptr(),
+            self.m, self.k, self.n, self.r, self.scale, _abi.CF_DTYPE_BF16, self.nws.data_ptr(),
+            self.nws_bytes, stream.cuda_stream), self.name)
+
+    def verify(self) -> None:
+        from oracle import linear_ref, norm_ref
+
+        rows = torch.randperm(self.m, generator=torch.Generator().manual_seed(0))[:128]
+        normed, summed = norm_ref.fused_residual_rmsnorm(self.x[rows.to(self.x.device)],
+                                                         self.res[rows.to(self.x.device)],
+                                                         self.nw, 1e-6)
+        ref = linear_ref.lora_linear(normed, self._w_t(), self.a, self.b, self.scale)
+        err = linear_ref.max_rel_error(self.y[rows.to(self.y.device)], ref)
+        assert err <= 2e-2, f"{self.name}: max relative error {err}"
+        assert torch.equal(self.res_out[rows.to(self.x.device)].cpu(), summed)
+
+    def extra_record(self, steps: int, flush) -> dict:
+        """The unfused route timed the same way: the norm kernel writes the normalised
+        rows, then the plain W8 linear reads them."""
+        from cuda_force_b200 import _abi
+
+        normed = torch.empty_like(self.x)
+        stream = torch.cuda.current_stream(self.dist.device)
+
+        def unfused():
+            _abi.check(self.lib.cf_fused_residual_rmsnorm(
+                self.x.data_ptr(), self.res.data_ptr(), self.nw.data_ptr(), _abi.CF_DTYPE_BF16,
+                normed.data_ptr(), self.res_out.data_ptr(), self.m, self.k, 1e-6,
+                _abi.CF_DTYPE_BF16, stream.cuda_stream), "norm")
+            _abi.check(self.lib.cf_lora_linear_int8(
+                normed.data_ptr(), self.codes.data_ptr(), self.scales.data_ptr(),
+                self.a.data_ptr(), _abi.CF_LAYOUT_REF, self.b.data_ptr(), _abi.CF_LAYOUT_REF,
+                self.y.data_ptr(), self.m, self.k, self.n, self.r, self.scale,
+                _abi.CF_DTYPE_BF16, self.ws.data_ptr(), self.ws_bytes, stream.cuda_stream), "lin")
+
+        for _ in range(3):
+            unfused()
+        times = []
+        for i in range(steps):
+            if flush is not None:
+                flush.fill_(i & 0xFF)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            unfused()
+            e1.record(stream)
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1))
+        ms = statistics.mean(times)
+        return {"unfused_ms_per_step": round(ms, 5),
+                "unfused_tflops": round(self.work_per_step / ms / 1e9, 1),
+                "how": "cf_fused_residual_rmsnorm (normalised rows written) then "
+                       "cf_lora_linear_int8, same flush and CUDA events"}
+
+    def e2e(self, steps: int) -> dict:
+        import cuda_force_b200 as cf
+
+        dev = self.dist.device
+        hx, hr = self.x.cpu().pin_memory(), self.res.cpu().pin_memory()
+        hy = torch.empty(self.m, self.n, dtype=torch.bfloat16).pin_memory()
+
+        def one():
+            y, _ = cf.rmsnorm_lora_linear_int8(hx.to(dev, non_blocking=True),
+                                               hr.to(dev, non_blocking=True), self.nw,
+                                               self.codes, self.scales, self.a, self.b,
+                                               self.scale, 1e-6)
+            hy.copy_(y, non_blocking=True)
+
+        return timed_e2e(self, one, steps, 2 * hx.numel() * 2, hy.numel() * 2,
+                         "cuda_force_b200.rmsnorm_lora_linear_int8 (x, residual in / y out)")
+
+    def cpu_sample(self):
+        fn, work, kind, sample = super().cpu_sample()
+        return fn, work, kind, sample + " (norm not included)"
+
+
 class LoraF32(LoraLinear):
     """fp32 LoRA linear (the reference's own CUDA dtype), benchmark config 3 shapes."""
 
@@ -1328,7 +1439,7 @@ class W8ColumnShardedPeer(W8ColumnSharded):
 
 WORKLOADS = {w.name: w for w in (LlamaStackQuant, Config1Quant, Config1Dequant, LoraLinear,
                                 W8Decode, W8Prefill, W8ColumnSharded, W8ColumnShardedNccl,
-                                W8ColumnShardedPeer,
+                                W8ColumnShardedPeer, NormW8Prefill,
                                 LoraF32, MergeQuant,
                                 W8SwiGLU, ResidualRMSNorm)}
 
@@ -1408,6 +1519,7 @@ def measure(wl, args, dist: Dist, cpu_seconds: float) -> dict:
     copy_ref = size_matched_copy(wl.work_per_step, dist.device, flush) if wl.bound == "hbm" else None
     exchange = (wl.exchange_record(total_ms / args.steps, args.steps)
                 if hasattr(wl, "exchange_record") else None)
+    extra = wl.extra_record(args.steps, flush) if hasattr(wl, "extra_record") else None
     e2e = wl.e2e(max(1, min(args.steps, args.e2e_steps)))
 
     cpu = None
@@ -1447,6 +1559,8 @@ def measure(wl, args, dist: Dist, cpu_seconds: float) -> dict:
         result["per_gpu"] = round(value / dist.world, 3)
     if exchange is not None:
         result["comm"] = exchange
+    if extra is not None:
+        result["unfused"] = extra
     return result
 
 

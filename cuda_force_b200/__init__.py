@@ -21,6 +21,7 @@ from cuda_force_b200.ops import (
     quantize_int8,
     quantize_int8_many,
     rmsnorm,
+    rmsnorm_lora_linear_int8,
     w8_swiglu_int8,
 )
 
@@ -44,5 +45,6 @@ __all__ = [
     "quantize_int8",
     "quantize_int8_many",
     "rmsnorm",
+    "rmsnorm_lora_linear_int8",
     "w8_swiglu_int8",
 ]

@@ -79,6 +79,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _int, [_p, _p, _p, _int, _p, _p, _i64, _i64, ctypes.c_float, _int, _p]),
     "cf_lora_merge_quantize_int8": (
         _int, [_p, _p, _p, _i64, _i64, _i64, ctypes.c_float, _int, _p, _p, _p]),
+    "cf_rmsnorm_lora_linear_int8_workspace_bytes": (ctypes.c_size_t, [_i64, _i64, _i64]),
+    "cf_rmsnorm_lora_linear_int8": (
+        _int,
+        [_p, _p, _p, ctypes.c_float, _p, _p, _p, _int, _p, _int, _p, _p, _i64, _i64, _i64, _i64,
+         ctypes.c_float, _int, _p, ctypes.c_size_t, _p],
+    ),
     "cf_lora_linear_noalloc": (
         _int,
         [_p, _p, _int, _p, _int, _p, _int, _p, _i64, _i64, _i64, _i64, ctypes.c_float, _int, _p],

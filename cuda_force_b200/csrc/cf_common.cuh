@@ -39,6 +39,12 @@ int sm_count();
 // Address of the current device's error word (cached per device).
 unsigned *device_error_word();
 
+// Residual add and the RMS statistics of each row (norm.cu): residual_out =
+// x + residual (when residual is given) and row_scale[r] = 1/sqrt(mean of the
+// row's squares + eps), without writing a normalised row.
+int residual_rms_stats(const void *x, const void *residual, void *residual_out, float *row_scale,
+                       int64_t rows, int64_t cols, float eps, int dtype, cudaStream_t s);
+
 inline bool aligned_to(const void *p, uintptr_t bytes) {
   return (reinterpret_cast<uintptr_t>(p) & (bytes - 1)) == 0;
 }

@@ -608,6 +608,10 @@ struct W8Params {
   // multicast object); when set, the epilogue writes every slab once with
   // multimem stores instead of one TMA store per destination.
   void *mc_out;
+  // Folded RMSNorm (kNorm): each code is also multiplied by the norm weight of
+  // its input feature, and each token's output by its row scale.
+  const uint16_t *norm_w;   // [K] in the activation dtype
+  const float *row_scale;   // [M]
   int n_tiles_w;
   int n_tiles;
   unsigned *err;
@@ -1132,7 +1136,7 @@ struct OutMaps {
   CUtensorMap map[kMaxOuts];
 };
 
-template <bool kBf16, bool kTmaStore, int kBT>
+template <bool kBf16, bool kTmaStore, int kBT, bool kNorm>
 __global__ void __launch_bounds__(W8WideCfg<kTmaStore, kBT>::kThreads, 1)
     w8_wide_kernel(const __grid_constant__ CUtensorMap tm_x,
                    const __grid_constant__ CUtensorMap tm_codes,
@@ -1339,8 +1343,19 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore, kBT>::kThreads, 1)
 #pragma unroll 1
       for (int c = 0; c < BT / 32; ++c) {
         uint32_t v[32];
+        float rs_lane = 1.0f;
+        if constexpr (kNorm) {
+          const int t = t0 + c * 32 + lane;
+          rs_lane = t < p.M ? __ldg(p.row_scale + t) : 0.0f;
+        }
         ptx::tmem_ld_32x32b_x32(t_row + c * 32, v);
         ptx::tmem_ld_wait();
+        if constexpr (kNorm) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            v[j] = __float_as_uint(__uint_as_float(v[j]) * __shfl_sync(0xffffffffu, rs_lane, j));
+          }
+        }
         if constexpr (kTmaStore) {
           // Stage a 32-token x 128-feature slab (token-major, 256-byte rows)
           // and let the TMA engine store it to every destination; the slab
@@ -1451,6 +1466,14 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore, kBT>::kThreads, 1)
           const uint4 codes = *reinterpret_cast<const uint4 *>(raw + r * C::kBKw + half * 16);
           const uint32_t words[4] = {codes.x, codes.y, codes.z, codes.w};
           const uint64_t sc2 = ptx::splat_f32x2(s_cur);
+          uint32_t wv[8];  // kNorm: norm weights of this lane's 16 input features
+          if constexpr (kNorm) {
+            const uint4 *wsrc = reinterpret_cast<const uint4 *>(
+                p.norm_w + static_cast<int64_t>(it) * C::kBKw + half * 16);
+            const uint4 w0v = __ldg(wsrc), w1v = __ldg(wsrc + 1);
+            wv[0] = w0v.x; wv[1] = w0v.y; wv[2] = w0v.z; wv[3] = w0v.w;
+            wv[4] = w1v.x; wv[5] = w1v.y; wv[6] = w1v.z; wv[7] = w1v.w;
+          }
           uint32_t outw[8];
 #pragma unroll
           for (int wd = 0; wd < 4; ++wd) {
@@ -1460,7 +1483,22 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore, kBT>::kThreads, 1)
               const uint32_t b0 = __byte_perm(u, 0x4B000000u, 0x7440u | (2 * h));
               const uint32_t b1 = __byte_perm(u, 0x4B000000u, 0x7440u | (2 * h + 1));
               float lo, hi;
-              ptx::dequant_pair(b0, b1, sc2, lo, hi);
+              if constexpr (kNorm) {
+                // (code * block scale * norm weight), the product rounded once
+                const uint32_t wp = wv[2 * wd + h];
+                float wlo, whi;
+                if constexpr (kBf16) {
+                  wlo = __uint_as_float(wp << 16);
+                  whi = __uint_as_float(wp & 0xffff0000u);
+                } else {
+                  const float2 f2 = __half22float2(*reinterpret_cast<const __half2 *>(&wp));
+                  wlo = f2.x;
+                  whi = f2.y;
+                }
+                ptx::dequant_pair(b0, b1, ptx::pack_f32x2(s_cur * wlo, s_cur * whi), lo, hi);
+              } else {
+                ptx::dequant_pair(b0, b1, sc2, lo, hi);
+              }
               outw[2 * wd + h] = kBf16 ? ptx::pack_bf16x2(lo, hi) : ptx::pack_f16x2(lo, hi);
             }
           }
@@ -2601,6 +2639,9 @@ struct LinearArgs {
   int64_t col0 = 0;
   int self_dest = 0;  // index in dest of this GPU's own copy
   void *mc = nullptr;  // multicast address of the destination (multimem epilogue)
+  // Folded RMSNorm (wide kernel only): x is the un-normalised residual sum.
+  const void *norm_w = nullptr;
+  const float *row_scale = nullptr;
   // Row-group completion counters for a copy-engine all-gather (wide kernel).
   unsigned *done = nullptr;
   int rb_per_group = 1;
@@ -2719,7 +2760,7 @@ int launch_w8_decode(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
   return check_launch();
 }
 
-template <bool kBf16, bool kTmaStore, int kBT>
+template <bool kBf16, bool kTmaStore, int kBT, bool kNorm = false>
 int launch_w8_wide(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
   using C = W8WideCfg<kTmaStore, kBT>;
   const int r = static_cast<int>(L.r);
@@ -2775,8 +2816,10 @@ int launch_w8_wide(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
   p.mc_out = kTmaStore ? L.mc : nullptr;
   p.rb_per_group = L.rb_per_group;
   p.n_groups = L.n_groups;
-  auto kernel = w8_wide_kernel<kBf16, kTmaStore, kBT>;
-  if (int st_ = allow_dynamic_smem<w8_wide_kernel<kBf16, kTmaStore, kBT>>(C::kSmemBytes)) {
+  p.norm_w = static_cast<const uint16_t *>(L.norm_w);
+  p.row_scale = L.row_scale;
+  auto kernel = w8_wide_kernel<kBf16, kTmaStore, kBT, kNorm>;
+  if (int st_ = allow_dynamic_smem<w8_wide_kernel<kBf16, kTmaStore, kBT, kNorm>>(C::kSmemBytes)) {
     return st_;
   }
   const int grid = std::max(1, std::min(p.n_tiles, sm_count()));
@@ -2805,6 +2848,7 @@ int run_linear(const LinearArgs &L, cudaStream_t stream) {
   }
   if (st != CF_OK) return st;
   if (L.int8) {
+    if (L.norm_w != nullptr) return launch_w8_wide<kBf16, true, 512, true>(L, err, stream);
     if (L.n_dest == 0 && L.m <= 32) return launch_w8_decode<32, kBf16>(L, err, stream);
     if (L.n_dest == 0 && L.m <= 64) return launch_w8_decode<64, kBf16>(L, err, stream);
     if (L.n_dest == 0 && L.m <= 128) return launch_w8_decode<128, kBf16>(L, err, stream);
@@ -3062,6 +3106,34 @@ int validate_and_run(const LinearArgs &L, cf_stream_t stream) {
   return L.dtype == CF_DTYPE_BF16 ? run_linear<true>(L, s) : run_linear<false>(L, s);
 }
 
+// A'[k, j] = w[k] * A[k, j] in the dtype ([K, r], K-major rows of r): the
+// norm weight folded into the down-projection, so P' = scale * h A' needs no
+// normalised copy of h. `a` is [K, r] (a_t = 0) or [r, K] (a_t = 1).
+template <typename T>
+__global__ void weight_adapter_kernel(const T *a, int a_t, const T *w, T *out, int64_t k,
+                                      int64_t r) {
+  const int64_t total = k * r;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t kk = i / r, j = i % r;
+    const float v = static_cast<float>(a[a_t ? j * k + kk : i]) * static_cast<float>(w[kk]);
+    out[i] = static_cast<T>(v);
+  }
+}
+
+size_t align256(size_t b) { return (b + 255) & ~static_cast<size_t>(255); }
+
+// Workspace of cf_rmsnorm_lora_linear_int8: the folded route needs the row
+// scales, A' and P; the route for short token counts (decode kernel) needs a
+// normalised copy of x and P.
+size_t norm_linear_workspace(int64_t m, int64_t k, int64_t r) {
+  if (m <= 0 || k <= 0 || r <= 0) return 0;
+  const size_t p = workspace_bytes(m, r, 2);
+  const size_t folded = align256(static_cast<size_t>(m) * 4) + align256(static_cast<size_t>(k * r) * 2) + p;
+  const size_t plain = align256(static_cast<size_t>(m * k) * 2) + p;
+  return std::max(folded, plain);
+}
+
 }  // namespace
 }  // namespace cfb
 
@@ -3181,6 +3253,72 @@ int cf_lora_linear_int8_allgather(const void *x, const int8_t *w_codes, const fl
   L.ldy = ldy;
   L.col0 = col0;
   if (w_scales != nullptr && !cfb::aligned_to(w_scales, 4)) return CF_ERR_MISALIGNED;
+  return cfb::validate_and_run(L, stream);
+}
+
+size_t cf_rmsnorm_lora_linear_int8_workspace_bytes(int64_t m, int64_t k, int64_t rank) {
+  return cfb::norm_linear_workspace(m, k, rank);
+}
+
+int cf_rmsnorm_lora_linear_int8(const void *x, const void *residual, const void *norm_weight,
+                                float eps, const int8_t *w_codes, const float *w_scales,
+                                const void *a, int a_layout, const void *b, int b_layout, void *y,
+                                void *residual_out, int64_t m, int64_t k, int64_t n, int64_t rank,
+                                float scale, int dtype, void *workspace, size_t workspace_bytes,
+                                cf_stream_t stream) {
+  using namespace cfb;
+  if (m < 0 || k < 0 || n < 0) return CF_ERR_INVALID_ARGUMENT;
+  if (m == 0 || n == 0) return CF_OK;
+  if (x == nullptr || norm_weight == nullptr || (residual == nullptr) != (residual_out == nullptr)) {
+    return CF_ERR_INVALID_ARGUMENT;
+  }
+  if (dtype != CF_DTYPE_BF16 && dtype != CF_DTYPE_F16) return CF_ERR_UNSUPPORTED;
+  if (a_layout != CF_LAYOUT_REF && a_layout != CF_LAYOUT_T) return CF_ERR_INVALID_ARGUMENT;
+  if (rank != 16 && rank != 32 && rank != 64) return CF_ERR_UNSUPPORTED;
+  if (workspace == nullptr || workspace_bytes < norm_linear_workspace(m, k, rank)) {
+    return CF_ERR_WORKSPACE;
+  }
+  if (!aligned_to(workspace, 256) || !aligned_to(norm_weight, 16)) return CF_ERR_MISALIGNED;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  const size_t p_bytes = cfb::workspace_bytes(m, rank, 2);
+  if (m <= 128 || k % kBK != 0) {
+    // Short token counts run on the decode kernel: normalise into the
+    // workspace, then the plain W8 linear.
+    void *normed = ws;
+    if (int st = cf_fused_residual_rmsnorm(x, residual, norm_weight, dtype, normed, residual_out,
+                                           m, k, eps, dtype, stream)) {
+      return st;
+    }
+    return cf_lora_linear_int8(normed, w_codes, w_scales, a, a_layout, b, b_layout, y, m, k, n,
+                               rank, scale, dtype, ws + align256(static_cast<size_t>(m * k) * 2),
+                               p_bytes, stream);
+  }
+  float *row_scale = reinterpret_cast<float *>(ws);
+  void *a_w = ws + align256(static_cast<size_t>(m) * 4);
+  void *p_ws = static_cast<uint8_t *>(a_w) + align256(static_cast<size_t>(k * rank) * 2);
+  if (int st = residual_rms_stats(x, residual, residual_out, row_scale, m, k, eps, dtype, s)) {
+    return st;
+  }
+  const int64_t total = k * rank;
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 1024));
+  const int a_t = a_layout == CF_LAYOUT_T ? 1 : 0;
+  if (dtype == CF_DTYPE_BF16) {
+    weight_adapter_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
+        static_cast<const __nv_bfloat16 *>(a), a_t, static_cast<const __nv_bfloat16 *>(norm_weight),
+        static_cast<__nv_bfloat16 *>(a_w), k, rank);
+  } else {
+    weight_adapter_kernel<__half><<<grid, 256, 0, s>>>(
+        static_cast<const __half *>(a), a_t, static_cast<const __half *>(norm_weight),
+        static_cast<__half *>(a_w), k, rank);
+  }
+  if (int st = check_launch()) return st;
+  const void *h = residual != nullptr ? residual_out : x;
+  cfb::LinearArgs L{h, w_codes, CF_LAYOUT_T, w_scales, a_w, CF_LAYOUT_REF, b, b_layout, y, m, k, n,
+                    rank, scale, dtype, p_ws, p_bytes, true};
+  L.norm_w = norm_weight;
+  L.row_scale = row_scale;
+  if (w_scales != nullptr && !aligned_to(w_scales, 4)) return CF_ERR_MISALIGNED;
   return cfb::validate_and_run(L, stream);
 }
 

@@ -118,7 +118,8 @@ __device__ __forceinline__ float block_sum(float v, float *buf) {
 template <typename T, typename TW, int kV>
 __global__ void __launch_bounds__(kNormThreads)
     residual_rmsnorm_vec_kernel(const T *x, const T *residual, const TW *weight, T *out,
-                                T *residual_out, int64_t rows, int64_t cols, float eps) {
+                                T *residual_out, int64_t rows, int64_t cols, float eps,
+                                float *row_scale) {
   using C = Chunk<T>;
   constexpr int kE = C::kElems;
   __shared__ float red[2][kNormWarps];
@@ -178,6 +179,10 @@ __global__ void __launch_bounds__(kNormThreads)
       }
     }
     const float scale = rsqrtf(block_sum(ss, red[parity]) / static_cast<float>(cols) + eps);
+    if (out == nullptr) {  // statistics only: the row's scale instead of the normalised row
+      if (threadIdx.x == 0) row_scale[row] = scale;
+      continue;
+    }
     if constexpr (kV > 0) {
 #pragma unroll
       for (int i = 0; i < kV; ++i) {
@@ -209,7 +214,8 @@ __global__ void __launch_bounds__(kNormThreads)
 template <typename T, typename TW>
 __global__ void __launch_bounds__(kNormThreads)
     residual_rmsnorm_scalar_kernel(const T *x, const T *residual, const TW *weight, T *out,
-                                   T *residual_out, int64_t rows, int64_t cols, float eps) {
+                                   T *residual_out, int64_t rows, int64_t cols, float eps,
+                                   float *row_scale) {
   __shared__ float red[2][kNormWarps];
   int parity = 0;
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x, parity ^= 1) {
@@ -224,6 +230,10 @@ __global__ void __launch_bounds__(kNormThreads)
       ss = fmaf(v, v, ss);
     }
     const float scale = rsqrtf(block_sum(ss, red[parity]) / static_cast<float>(cols) + eps);
+    if (out == nullptr) {
+      if (threadIdx.x == 0) row_scale[row] = scale;
+      continue;
+    }
     const T *back = residual ? residual_out : x;
     for (int64_t c = threadIdx.x; c < cols; c += kNormThreads) {
       const float v = Elem<T>::load(back + base + c);
@@ -234,37 +244,54 @@ __global__ void __launch_bounds__(kNormThreads)
 
 template <typename T, typename TW, int kV>
 int launch_vec(const void *x, const void *r, const void *w, void *o, void *ro, int64_t rows,
-               int64_t cols, float eps, unsigned grid, cudaStream_t s) {
+               int64_t cols, float eps, float *rs, unsigned grid, cudaStream_t s) {
   residual_rmsnorm_vec_kernel<T, TW, kV><<<grid, kNormThreads, 0, s>>>(
       static_cast<const T *>(x), static_cast<const T *>(r), static_cast<const TW *>(w),
-      static_cast<T *>(o), static_cast<T *>(ro), rows, cols, eps);
+      static_cast<T *>(o), static_cast<T *>(ro), rows, cols, eps, rs);
   return check_launch();
 }
 
 template <typename T, typename TW>
 int norm_dispatch(const void *x, const void *r, const void *w, void *o, void *ro, int64_t rows,
-                  int64_t cols, float eps, cudaStream_t s) {
+                  int64_t cols, float eps, cudaStream_t s, float *rs = nullptr) {
   const int64_t want = static_cast<int64_t>(sm_count()) * 8;
   const unsigned grid = static_cast<unsigned>(rows < want ? rows : want);
   constexpr int kE = Chunk<T>::kElems;
-  const bool vec = cols % kE == 0 && aligned_to(x, 16) && aligned_to(o, 16) &&
+  const bool vec = cols % kE == 0 && aligned_to(x, 16) && (o == nullptr || aligned_to(o, 16)) &&
                    aligned_to(w, 16) && (r == nullptr || (aligned_to(r, 16) && aligned_to(ro, 16)));
   if (!vec) {
     residual_rmsnorm_scalar_kernel<T, TW><<<grid, kNormThreads, 0, s>>>(
         static_cast<const T *>(x), static_cast<const T *>(r), static_cast<const TW *>(w),
-        static_cast<T *>(o), static_cast<T *>(ro), rows, cols, eps);
+        static_cast<T *>(o), static_cast<T *>(ro), rows, cols, eps, rs);
     return check_launch();
   }
   const int64_t per_thread = (cols / kE + kNormThreads - 1) / kNormThreads;
-  if (per_thread <= 1) return launch_vec<T, TW, 1>(x, r, w, o, ro, rows, cols, eps, grid, s);
-  if (per_thread <= 2) return launch_vec<T, TW, 2>(x, r, w, o, ro, rows, cols, eps, grid, s);
+  if (per_thread <= 1) return launch_vec<T, TW, 1>(x, r, w, o, ro, rows, cols, eps, rs, grid, s);
+  if (per_thread <= 2) return launch_vec<T, TW, 2>(x, r, w, o, ro, rows, cols, eps, rs, grid, s);
   if (per_thread <= kMaxResident) {
-    return launch_vec<T, TW, kMaxResident>(x, r, w, o, ro, rows, cols, eps, grid, s);
+    return launch_vec<T, TW, kMaxResident>(x, r, w, o, ro, rows, cols, eps, rs, grid, s);
   }
-  return launch_vec<T, TW, 0>(x, r, w, o, ro, rows, cols, eps, grid, s);
+  return launch_vec<T, TW, 0>(x, r, w, o, ro, rows, cols, eps, rs, grid, s);
 }
 
 }  // namespace
+
+int residual_rms_stats(const void *x, const void *residual, void *residual_out, float *row_scale,
+                       int64_t rows, int64_t cols, float eps, int dtype, cudaStream_t s) {
+  if (rows == 0 || cols == 0) return CF_OK;
+  switch (dtype) {
+    case CF_DTYPE_F32:
+      return norm_dispatch<float, float>(x, residual, x, nullptr, residual_out, rows, cols, eps,
+                                         s, row_scale);
+    case CF_DTYPE_BF16:
+      return norm_dispatch<__nv_bfloat16, __nv_bfloat16>(x, residual, x, nullptr, residual_out,
+                                                         rows, cols, eps, s, row_scale);
+    default:
+      return norm_dispatch<__half, __half>(x, residual, x, nullptr, residual_out, rows, cols,
+                                           eps, s, row_scale);
+  }
+}
+
 }  // namespace cfb
 
 extern "C" {

@@ -337,6 +337,75 @@ def w8_swiglu_int8(
     return y.reshape(*lead, n)
 
 
+def rmsnorm_lora_linear_int8(
+    x: torch.Tensor,
+    residual: torch.Tensor | None,
+    norm_weight: torch.Tensor,
+    w_codes: torch.Tensor,
+    w_scales: torch.Tensor,
+    lora_a: torch.Tensor,
+    lora_b: torch.Tensor,
+    scale: float = 1.0,
+    eps: float = 1e-6,
+) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """``y = lora_linear_int8(rmsnorm(h, norm_weight, eps), ...)`` with ``h = x + residual``.
+
+    The reference's ``fused_residual_rmsnorm`` (ops.py:335-382) followed by the
+    W8 linear, as a LLaMA block chains them (examples/transformer_block.py:
+    84-87), with the normalisation folded into the linear: the normalised
+    activations are never written. Returns ``(y, residual_out)``
+    (``residual_out`` is None without a residual). float16 / bfloat16 only;
+    ``norm_weight`` in x's dtype.
+    """
+    import ctypes
+
+    from cuda_force_b200 import _abi
+
+    if w_codes.dim() != 2:
+        raise ValueError(f"w_codes must be [out_features, in_features], got {tuple(w_codes.shape)}")
+    n, k = w_codes.shape
+    _check_lora_shapes(x, k, n, lora_a, lora_b)
+    if norm_weight.numel() != k:
+        raise ValueError(f"norm_weight must have {k} elements, got {norm_weight.numel()}")
+    if residual is not None and residual.shape != x.shape:
+        raise ValueError(f"x and residual must have the same shape, got {tuple(x.shape)} and "
+                         f"{tuple(residual.shape)}")
+    if x.dtype not in (torch.float16, torch.bfloat16):
+        raise ValueError("rmsnorm_lora_linear_int8 takes float16 or bfloat16 activations")
+    expected = n * k // QUANT_BLOCK_SIZE
+    if k % QUANT_BLOCK_SIZE or w_scales.numel() != expected:
+        raise ValueError(f"expected {expected} block scales for {w_codes.numel()} elements")
+    tensors = [x, norm_weight, w_codes, w_scales, lora_a, lora_b]
+    _require("rmsnorm_lora_linear_int8", *tensors, *([residual] if residual is not None else []))
+    x2, lead = _flatten_tokens(x)
+    m = x2.shape[0]
+    r = lora_a.shape[1]
+    rp = 16 if r <= 16 else 32 if r <= 32 else 64
+    if r > 64:
+        raise ValueError(f"adapter rank {r} above 64 is not supported")
+    a, b = lora_a.to(x.dtype), lora_b.to(x.dtype)
+    if rp != r:  # zero rank padding leaves the product unchanged
+        a = torch.nn.functional.pad(a, (0, rp - r))
+        b = torch.nn.functional.pad(b, (0, 0, 0, rp - r))
+    a, b = a.contiguous(), b.contiguous()
+    res2 = residual.reshape(m, k).contiguous() if residual is not None else None
+    res_out = torch.empty_like(x2) if residual is not None else None
+    y = torch.empty(m, n, dtype=x.dtype, device=x.device)
+    lib = _abi.load()
+    ws = torch.empty(lib.cf_rmsnorm_lora_linear_int8_workspace_bytes(m, k, rp), dtype=torch.uint8,
+                     device=x.device)
+    dtype = _abi.CF_DTYPE_BF16 if x.dtype == torch.bfloat16 else _abi.CF_DTYPE_F16
+    p = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None  # noqa: E731
+    stream = ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)
+    _abi.check(lib.cf_rmsnorm_lora_linear_int8(
+        p(x2), p(res2), p(norm_weight.to(x.dtype).contiguous()), float(eps), p(w_codes.contiguous()),
+        p(w_scales.contiguous().reshape(-1)), p(a), _abi.CF_LAYOUT_REF, p(b), _abi.CF_LAYOUT_REF,
+        p(y), p(res_out), m, k, n, rp, float(scale), dtype, p(ws), ws.numel(), stream),
+        "cf_rmsnorm_lora_linear_int8")
+    return (y.reshape(*lead, n),
+            res_out.reshape(x.shape) if res_out is not None else None)
+
+
 def quantization_error(x: torch.Tensor) -> torch.Tensor:
     """Maximum absolute round-trip error of int8 quantisation (<= scale / 2 per block)."""
     quantised, scales = quantize_int8(x)

@@ -152,6 +152,29 @@ CF_API int cf_lora_linear_int8(const void *x, const int8_t *w_codes, const float
                         int64_t m, int64_t k, int64_t n, int64_t rank, float scale, int dtype,
                         void *workspace, size_t workspace_bytes, cf_stream_t stream);
 
+/* RMSNorm (with an optional residual add) folded into the W8 + LoRA linear:
+ *   residual_out = x + residual                 (when residual is given)
+ *   h = residual given ? residual_out : x
+ *   y = lora_linear_int8(rmsnorm(h, norm_weight, eps), w_codes, w_scales, a, b, scale)
+ * the composition of the reference's fused_residual_rmsnorm and its linear
+ * in a LLaMA block (python/cudaforge/ops.py:335-382 then :289-332, as
+ * examples/transformer_block.py:84-87 chain them; no single counterpart).
+ * For m > 128 the normalised activations are never written: one pass writes
+ * residual_out and each row's 1/rms; the W8 kernel multiplies every code by
+ * the norm weight of its input feature as it converts it and every output
+ * row by its row scale; the adapter's A is pre-multiplied by the norm weight.
+ * m <= 128 normalises into the workspace and runs the decode kernel.
+ * bf16/f16 only; norm_weight in the activation dtype; rank 16, 32 or 64;
+ * workspace >= cf_rmsnorm_lora_linear_int8_workspace_bytes (256-byte aligned). */
+CF_API size_t cf_rmsnorm_lora_linear_int8_workspace_bytes(int64_t m, int64_t k, int64_t rank);
+CF_API int cf_rmsnorm_lora_linear_int8(const void *x, const void *residual,
+                                       const void *norm_weight, float eps, const int8_t *w_codes,
+                                       const float *w_scales, const void *a, int a_layout,
+                                       const void *b, int b_layout, void *y, void *residual_out,
+                                       int64_t m, int64_t k, int64_t n, int64_t rank, float scale,
+                                       int dtype, void *workspace, size_t workspace_bytes,
+                                       cf_stream_t stream);
+
 /* Column-sharded W8 linear with the output all-gather fused into the kernel.
  * This rank computes output features [col0, col0 + n) (its rows of the int8
  * weight, w_codes [n, k], and its columns of b) and writes them into every
