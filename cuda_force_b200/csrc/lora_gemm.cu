@@ -610,7 +610,7 @@ struct W8Params {
   void *mc_out;
   // Folded RMSNorm (kNorm): each code is also multiplied by the norm weight of
   // its input feature, and each token's output by its row scale.
-  const uint16_t *norm_w;   // [K] in the activation dtype
+  const float *norm_w;      // [K] fp32
   const float *row_scale;   // [M]
   int n_tiles_w;
   int n_tiles;
@@ -1119,7 +1119,11 @@ struct W8WideCfg {
   // The stage's scales: 128 rows x the aligned group of four 64-element
   // blocks that holds its k-block (one 16-byte TMA row per feature).
   static constexpr int kScaleBytes = kBM * 4 * 4;      // 2 KB
-  static constexpr int kStageBytes = kABytes + kXBytes + kRawBytes + kScaleBytes;  // 46 KB
+  // Folded RMSNorm: the stage's 32 norm weights (one 64-byte TMA row; the
+  // slot keeps the stage 1 KB-aligned).
+  static constexpr int kNormBytes = 1024;
+  static constexpr int kStageBytes =
+      kABytes + kXBytes + kRawBytes + kScaleBytes + kNormBytes;  // 47 KB (31 KB at kBT 256)
   static constexpr int kStages = kBT == 256 ? 6 : (kTmaStore ? 4 : 5);
   static constexpr int kSlabBytes = 32 * kBM * 2;      // 32 tokens x 128 features, 8 KB
   static constexpr int kStagingBytes = kTmaStore ? 2 * kSlabBytes : 0;
@@ -1143,6 +1147,7 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore, kBT>::kThreads, 1)
                    const __grid_constant__ CUtensorMap tm_p,
                    const __grid_constant__ CUtensorMap tm_bt,
                    const __grid_constant__ CUtensorMap tm_scales,
+                   const __grid_constant__ CUtensorMap tm_norm,
                    const __grid_constant__ OutMaps out_maps, const W8Params p) {
   using C = W8WideCfg<kTmaStore, kBT>;
   constexpr int BT = C::BT;
@@ -1213,7 +1218,12 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore, kBT>::kThreads, 1)
           if (it < p.num_kb) {
             const int k0 = it * C::kBKw;
             ptx::mbar_expect_tx(&full[stage], C::kXBytes + C::kRawBytes +
-                                                  (p.scale_tma ? C::kScaleBytes : 0));
+                                                  (p.scale_tma ? C::kScaleBytes : 0) +
+                                                  (kNorm ? C::kBKw * 4 : 0));
+            if constexpr (kNorm) {
+              ptx::tma_load_2d(sx + C::kXBytes + C::kRawBytes + C::kScaleBytes, &tm_norm,
+                               &full[stage], k0, 0);
+            }
             for (int h = 0; h < C::kHalves; ++h) {
               ptx::tma_load_2d(sx + h * C::kXHalf, &tm_x, &full[stage], k0, t0 + h * 256);
             }
@@ -1466,14 +1476,9 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore, kBT>::kThreads, 1)
           const uint4 codes = *reinterpret_cast<const uint4 *>(raw + r * C::kBKw + half * 16);
           const uint32_t words[4] = {codes.x, codes.y, codes.z, codes.w};
           const uint64_t sc2 = ptx::splat_f32x2(s_cur);
-          uint32_t wv[8];  // kNorm: norm weights of this lane's 16 input features
-          if constexpr (kNorm) {
-            const uint4 *wsrc = reinterpret_cast<const uint4 *>(
-                p.norm_w + static_cast<int64_t>(it) * C::kBKw + half * 16);
-            const uint4 w0v = __ldg(wsrc), w1v = __ldg(wsrc + 1);
-            wv[0] = w0v.x; wv[1] = w0v.y; wv[2] = w0v.z; wv[3] = w0v.w;
-            wv[4] = w1v.x; wv[5] = w1v.y; wv[6] = w1v.z; wv[7] = w1v.w;
-          }
+          // kNorm: the fp32 norm weights of this lane's 16 input features
+          const uint64_t *wsrc = reinterpret_cast<const uint64_t *>(
+              raw + C::kRawBytes + C::kScaleBytes + half * 64);
           uint32_t outw[8];
 #pragma unroll
           for (int wd = 0; wd < 4; ++wd) {
@@ -1484,18 +1489,8 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore, kBT>::kThreads, 1)
               const uint32_t b1 = __byte_perm(u, 0x4B000000u, 0x7440u | (2 * h + 1));
               float lo, hi;
               if constexpr (kNorm) {
-                // (code * block scale * norm weight), the product rounded once
-                const uint32_t wp = wv[2 * wd + h];
-                float wlo, whi;
-                if constexpr (kBf16) {
-                  wlo = __uint_as_float(wp << 16);
-                  whi = __uint_as_float(wp & 0xffff0000u);
-                } else {
-                  const float2 f2 = __half22float2(*reinterpret_cast<const __half2 *>(&wp));
-                  wlo = f2.x;
-                  whi = f2.y;
-                }
-                ptx::dequant_pair(b0, b1, ptx::pack_f32x2(s_cur * wlo, s_cur * whi), lo, hi);
+                // code * (block scale * norm weight), rounded once to the dtype
+                ptx::dequant_pair(b0, b1, ptx::mul_f32x2(sc2, wsrc[2 * wd + h]), lo, hi);
               } else {
                 ptx::dequant_pair(b0, b1, sc2, lo, hi);
               }
@@ -2640,7 +2635,7 @@ struct LinearArgs {
   int self_dest = 0;  // index in dest of this GPU's own copy
   void *mc = nullptr;  // multicast address of the destination (multimem epilogue)
   // Folded RMSNorm (wide kernel only): x is the un-normalised residual sum.
-  const void *norm_w = nullptr;
+  const void *norm_w = nullptr;  // fp32 [K]
   const float *row_scale = nullptr;
   // Row-group completion counters for a copy-engine all-gather (wide kernel).
   unsigned *done = nullptr;
@@ -2816,7 +2811,12 @@ int launch_w8_wide(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
   p.mc_out = kTmaStore ? L.mc : nullptr;
   p.rb_per_group = L.rb_per_group;
   p.n_groups = L.n_groups;
-  p.norm_w = static_cast<const uint16_t *>(L.norm_w);
+  p.norm_w = static_cast<const float *>(L.norm_w);
+  CUtensorMap tm_norm;
+  std::memset(&tm_norm, 0, sizeof(tm_norm));
+  if (kNorm) {
+    if ((st = make_map(&tm_norm, L.norm_w, 4, L.k, 1, C::kBKw, 1, false))) return st;
+  }
   p.row_scale = L.row_scale;
   auto kernel = w8_wide_kernel<kBf16, kTmaStore, kBT, kNorm>;
   if (int st_ = allow_dynamic_smem<w8_wide_kernel<kBf16, kTmaStore, kBT, kNorm>>(C::kSmemBytes)) {
@@ -2832,7 +2832,8 @@ int launch_w8_wide(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
   set_programmatic_dependency(attr[0]);
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  CFB_TRY_CUDA(cudaLaunchKernelEx(&cfg, kernel, tm_x, tm_codes, tm_p, tm_bt, tm_scales, out_maps, p));
+  CFB_TRY_CUDA(cudaLaunchKernelEx(&cfg, kernel, tm_x, tm_codes, tm_p, tm_bt, tm_scales, tm_norm,
+                                  out_maps, p));
   return check_launch();
 }
 
@@ -3110,8 +3111,12 @@ int validate_and_run(const LinearArgs &L, cf_stream_t stream) {
 // norm weight folded into the down-projection, so P' = scale * h A' needs no
 // normalised copy of h. `a` is [K, r] (a_t = 0) or [r, K] (a_t = 1).
 template <typename T>
-__global__ void weight_adapter_kernel(const T *a, int a_t, const T *w, T *out, int64_t k,
-                                      int64_t r) {
+__global__ void weight_adapter_kernel(const T *a, int a_t, const T *w, T *out, float *w32,
+                                      int64_t k, int64_t r) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < k;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    w32[i] = static_cast<float>(w[i]);
+  }
   const int64_t total = k * r;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -3129,7 +3134,8 @@ size_t align256(size_t b) { return (b + 255) & ~static_cast<size_t>(255); }
 size_t norm_linear_workspace(int64_t m, int64_t k, int64_t r) {
   if (m <= 0 || k <= 0 || r <= 0) return 0;
   const size_t p = workspace_bytes(m, r, 2);
-  const size_t folded = align256(static_cast<size_t>(m) * 4) + align256(static_cast<size_t>(k * r) * 2) + p;
+  const size_t folded = align256(static_cast<size_t>(m) * 4) + align256(static_cast<size_t>(k) * 4) +
+                        align256(static_cast<size_t>(k * r) * 2) + p;
   const size_t plain = align256(static_cast<size_t>(m * k) * 2) + p;
   return std::max(folded, plain);
 }
@@ -3295,7 +3301,8 @@ int cf_rmsnorm_lora_linear_int8(const void *x, const void *residual, const void 
                                p_bytes, stream);
   }
   float *row_scale = reinterpret_cast<float *>(ws);
-  void *a_w = ws + align256(static_cast<size_t>(m) * 4);
+  float *w32 = reinterpret_cast<float *>(ws + align256(static_cast<size_t>(m) * 4));
+  void *a_w = reinterpret_cast<uint8_t *>(w32) + align256(static_cast<size_t>(k) * 4);
   void *p_ws = static_cast<uint8_t *>(a_w) + align256(static_cast<size_t>(k * rank) * 2);
   if (int st = residual_rms_stats(x, residual, residual_out, row_scale, m, k, eps, dtype, s)) {
     return st;
@@ -3306,17 +3313,17 @@ int cf_rmsnorm_lora_linear_int8(const void *x, const void *residual, const void 
   if (dtype == CF_DTYPE_BF16) {
     weight_adapter_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
         static_cast<const __nv_bfloat16 *>(a), a_t, static_cast<const __nv_bfloat16 *>(norm_weight),
-        static_cast<__nv_bfloat16 *>(a_w), k, rank);
+        static_cast<__nv_bfloat16 *>(a_w), w32, k, rank);
   } else {
     weight_adapter_kernel<__half><<<grid, 256, 0, s>>>(
         static_cast<const __half *>(a), a_t, static_cast<const __half *>(norm_weight),
-        static_cast<__half *>(a_w), k, rank);
+        static_cast<__half *>(a_w), w32, k, rank);
   }
   if (int st = check_launch()) return st;
   const void *h = residual != nullptr ? residual_out : x;
   cfb::LinearArgs L{h, w_codes, CF_LAYOUT_T, w_scales, a_w, CF_LAYOUT_REF, b, b_layout, y, m, k, n,
                     rank, scale, dtype, p_ws, p_bytes, true};
-  L.norm_w = norm_weight;
+  L.norm_w = w32;
   L.row_scale = row_scale;
   if (w_scales != nullptr && !aligned_to(w_scales, 4)) return CF_ERR_MISALIGNED;
   return cfb::validate_and_run(L, stream);

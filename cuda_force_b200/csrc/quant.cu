@@ -118,11 +118,6 @@ __device__ __forceinline__ float load_scalar<__half>(const __half *p) {
   return __half2float(__ldg(p));
 }
 
-__device__ __forceinline__ unsigned pack4(int a, int b, int c, int d) {
-  return (static_cast<unsigned>(a) & 0xffu) | ((static_cast<unsigned>(b) & 0xffu) << 8) |
-         ((static_cast<unsigned>(c) & 0xffu) << 16) | (static_cast<unsigned>(d) << 24);
-}
-
 // ---------------------------------------------------------------------------
 // Quantisation core shared by every kernel.
 // ---------------------------------------------------------------------------
