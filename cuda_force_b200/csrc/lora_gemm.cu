@@ -2853,10 +2853,12 @@ int run_linear(const LinearArgs &L, cudaStream_t stream) {
     if (L.n_dest == 0 && L.m <= 32) return launch_w8_decode<32, kBf16>(L, err, stream);
     if (L.n_dest == 0 && L.m <= 64) return launch_w8_decode<64, kBf16>(L, err, stream);
     if (L.n_dest == 0 && L.m <= 128) return launch_w8_decode<128, kBf16>(L, err, stream);
-    // The peer-store and multicast all-gathers run 256-token tiles with two
-    // accumulators, so NVLink stores overlap the next tile's main loop. The
-    // copy-engine all-gather counts 512-token row blocks.
-    if ((L.n_dest > 1 || L.mc != nullptr) && L.done == nullptr) {
+    // The multicast all-gather runs 256-token tiles with two accumulators, so
+    // its NVLink stores overlap the next tile's main loop (1.81 ms against
+    // 1.86 ms at 8 GPUs, config 5); the peer-store form measured slower so
+    // (1.92 ms against 1.86 ms) and keeps 512-token tiles, as does the
+    // copy-engine form, whose counters count 512-token row blocks.
+    if (L.mc != nullptr && L.done == nullptr) {
       return launch_w8_wide<kBf16, true, 256>(L, err, stream);
     }
     return launch_w8_wide<kBf16, true, 512>(L, err, stream);
