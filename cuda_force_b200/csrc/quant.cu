@@ -580,6 +580,110 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
+// Bulk-copy staged dequantiser: like the TMA quantiser, every warp runs its
+// own pipeline. Lane 0 keeps tiles of 2048 codes and their 32 scales in
+// flight with cp.async.bulk (3 stages); the warp turns a landed tile into
+// 8 KB of fp32 in a double-buffered staging slot, and lane 0 writes the slot
+// back with one bulk store. Whole tiles only; 16-byte aligned operands.
+struct DequantTmaCfg {
+  static constexpr int kWarps = 8;
+  static constexpr int kThreads = kWarps * kWarp;
+  static constexpr int kTile = 2048;                      // codes per tile
+  static constexpr int kScales = kTile / kQuantBlockSize;  // 32
+  static constexpr int kStages = 3;
+  static constexpr int kInBytes = kTile + kScales * 4;     // 2176
+  static constexpr int kOutBufs = 2;
+  static constexpr int kOutBytes = kTile * 4;              // 8 KB
+  static constexpr int kWarpBytes = kStages * kInBytes + kOutBufs * kOutBytes + 64;
+  static constexpr size_t kSmemBytes = static_cast<size_t>(kWarps) * kWarpBytes;
+  static_assert(kInBytes % 16 == 0 && kWarpBytes % 16 == 0, "bulk copy alignment");
+};
+
+__global__ void __launch_bounds__(DequantTmaCfg::kThreads, 1)
+    dequantize_tma_kernel(const int8_t *__restrict__ codes, const float *__restrict__ scales,
+                          float *__restrict__ out, int64_t ntiles, unsigned *error_word) {
+  using C = DequantTmaCfg;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int lane = threadIdx.x & (kWarp - 1);
+  const int warp = threadIdx.x / kWarp;
+  uint8_t *mine = smem + warp * C::kWarpBytes;
+  uint8_t *out_buf = mine + C::kStages * C::kInBytes;
+  uint64_t *full = reinterpret_cast<uint64_t *>(out_buf + C::kOutBufs * C::kOutBytes);
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * C::kWarps + warp;
+  const int64_t step = static_cast<int64_t>(gridDim.x) * C::kWarps;
+  const int64_t n_mine = first < ntiles ? (ntiles - first + step - 1) / step : 0;
+  if (lane == 0) {
+    for (int s = 0; s < C::kStages; ++s) ptx::mbar_init(&full[s], 1);
+    ptx::fence_mbar_init();
+  }
+  __syncwarp();
+  int p_stage = 0;
+  auto issue_load = [&](int64_t j) {
+    const int64_t tile = first + j * step;
+    uint8_t *dst = mine + p_stage * C::kInBytes;
+    ptx::mbar_expect_tx(&full[p_stage], C::kInBytes);
+    ptx::bulk_load(dst, codes + tile * C::kTile, C::kTile, &full[p_stage]);
+    ptx::bulk_load(dst + C::kTile, scales + tile * C::kScales, C::kScales * 4, &full[p_stage]);
+    p_stage = p_stage + 1 == C::kStages ? 0 : p_stage + 1;
+  };
+  if (lane == 0) {
+    for (int64_t j = 0; j < n_mine && j < C::kStages - 1; ++j) issue_load(j);
+  }
+  int64_t issued = n_mine < C::kStages - 1 ? n_mine : C::kStages - 1;
+  bool aborted = false;
+  int s = 0, ob = 0;
+  uint32_t parity = 0;
+  for (int64_t j = 0; j < n_mine; ++j) {
+    const bool ok = ptx::mbar_wait_idle(&full[s], parity);
+    if (__any_sync(0xffffffffu, !ok)) {
+      if (lane == 0) atomicOr(error_word, kDevErrTimeout);
+      aborted = true;
+      break;
+    }
+    const uint8_t *in = mine + s * C::kInBytes;
+    const float *sc = reinterpret_cast<const float *>(in + C::kTile);
+    float *dst = reinterpret_cast<float *>(out_buf + ob * C::kOutBytes);
+    // Lane l handles codes [16 i + 4 l, +4) of each 512-code quarter: 4-byte
+    // shared loads and 16-byte shared stores, both conflict-free.
+#pragma unroll
+    for (int i = 0; i < C::kTile / (kWarp * 4); ++i) {
+      const int e = i * (kWarp * 4) + lane * 4;
+      const uint32_t w = *reinterpret_cast<const uint32_t *>(in + e);
+      const float scale = sc[e / kQuantBlockSize];
+      const int q0 = static_cast<int>(static_cast<int8_t>(w & 0xffu));
+      const int q1 = static_cast<int>(static_cast<int8_t>((w >> 8) & 0xffu));
+      const int q2 = static_cast<int>(static_cast<int8_t>((w >> 16) & 0xffu));
+      const int q3 = static_cast<int>(static_cast<int8_t>(w >> 24));
+      *reinterpret_cast<float4 *>(dst + e) =
+          make_float4(__fmul_rn(static_cast<float>(q0), scale), __fmul_rn(static_cast<float>(q1), scale),
+                      __fmul_rn(static_cast<float>(q2), scale), __fmul_rn(static_cast<float>(q3), scale));
+    }
+    ptx::fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      const int64_t tile = first + j * step;
+      ptx::bulk_store(out + tile * C::kTile, dst, C::kOutBytes);
+      ptx::bulk_commit();
+      // The input stage read just now is refilled next; the staging slot
+      // written next was last read by the store of tile j + 1 - kOutBufs.
+      if (issued < n_mine) issue_load(issued++);
+      ptx::bulk_wait_read<C::kOutBufs - 1>();
+    }
+    __syncwarp();
+    if (++s == C::kStages) {
+      s = 0;
+      parity ^= 1u;
+    }
+    ob ^= 1;
+  }
+  if (lane == 0) {
+    ptx::bulk_wait_all();
+    if (aborted) {
+      for (int st = 0; st < C::kStages; ++st) ptx::mbar_wait(&full[st], 0, 100000000ull);
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kThreads)
     dequantize_scalar_kernel(const int8_t *__restrict__ codes, const float *__restrict__ scales,
                              float *__restrict__ out, int64_t first, int64_t count) {
@@ -779,6 +883,27 @@ int cf_dequantize_int8(const int8_t *codes, const float *scales, float *output, 
   if (count == 0) return CF_OK;
   if (codes == nullptr || scales == nullptr || output == nullptr) return CF_ERR_INVALID_ARGUMENT;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  using DC = cfb::DequantTmaCfg;
+  if (cfb::aligned_to(codes, 16) && cfb::aligned_to(scales, 16) && cfb::aligned_to(output, 16) &&
+      count >= DC::kTile) {
+    // Whole 2048-code tiles through the bulk-copy kernel, the rest below.
+    if (int st = cfb::allow_dynamic_smem<cfb::dequantize_tma_kernel>(DC::kSmemBytes)) return st;
+    unsigned *err = cfb::device_error_word();
+    if (err == nullptr) return cfb::record_cuda_error(cudaGetLastError());
+    const int64_t ntiles = count / DC::kTile;
+    const int64_t ctas = (ntiles + DC::kWarps - 1) / DC::kWarps;
+    const unsigned grid = static_cast<unsigned>(
+        std::max<int64_t>(1, std::min<int64_t>(ctas, cfb::sm_count())));
+    cfb::dequantize_tma_kernel<<<grid, DC::kThreads, DC::kSmemBytes, s>>>(codes, scales, output,
+                                                                          ntiles, err);
+    if (int st = cfb::check_launch()) return st;
+    const int64_t done = ntiles * DC::kTile;
+    codes += done;
+    scales += done / cfb::kQuantBlockSize;
+    output += done;
+    count -= done;
+    if (count == 0) return CF_OK;
+  }
   const bool vec_ok = cfb::aligned_to(codes, 4) && cfb::aligned_to(output, 16);
   const int64_t nunits = vec_ok ? count / cfb::kDequantUnitElems : 0;
   if (nunits > 0) {
