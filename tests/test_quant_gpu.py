@@ -232,3 +232,15 @@ def test_quantization_error_is_within_half_a_step(dtype, size, cuda_device):
     ref_codes, ref_scales = quant_ref.quantize(torch_to_numpy_input(x))
     ref = torch.from_numpy(quant_ref.dequantize(ref_codes, ref_scales))
     assert err.item() == (x.float() - ref).abs().max().item()
+
+
+def test_dequantise_of_a_large_tensor_takes_the_bulk_path_bit_exact(cuda_device):
+    # 2^26 elements and more run on the bulk-copy dequantiser (whole 2048-code
+    # tiles), the remainder (here 4096 + 37 elements) on the register path.
+    n = (1 << 26) + 4096 + 37
+    g = torch.Generator(device=cuda_device).manual_seed(26)
+    codes = torch.randint(-127, 128, (n,), generator=g, device=cuda_device, dtype=torch.int8)
+    scales = torch.rand((n + 63) // 64, generator=g, device=cuda_device) * 0.1
+    out = cf.dequantize_int8(codes, scales)
+    ref = quant_ref.dequantize(codes.cpu().numpy(), scales.cpu().numpy())
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), ref.view(np.uint32))
