@@ -35,6 +35,8 @@ def _reference(x, gc, gs, uc, us, dtype):
     (129, 512, 1000, torch.float16),
     (1, 256, 136, torch.bfloat16),
     (4096, 4096, 11008, torch.bfloat16),
+    (200, 320, 384, torch.bfloat16),    # K/64 not a multiple of 4: the two-accumulator kernel
+    (700, 2048, 1000, torch.float16),   # N not a multiple of 64
 ])
 def test_swiglu_matches_the_reference_composition(m, k, n, dtype, cuda_device):
     g = torch.Generator(device=cuda_device).manual_seed(m + n)
