@@ -1140,12 +1140,7 @@ struct OutMaps {
   CUtensorMap map[kMaxOuts];
 };
 
-// kSwiglu: the LLaMA gate and up projections with SwiGLU. A tile's 128 MMA
-// rows are 64 gate features (rows 0-63, from the gate codes) and the same 64
-// up features (rows 64-127, from the up codes), so each converted tile still
-// feeds 512 tokens; the epilogue pairs row f with row 64 + f through shared
-// memory and writes only h = silu(g) * u for the 64 features.
-template <bool kBf16, bool kTmaStore, int kBT, bool kNorm, bool kSwiglu = false>
+template <bool kBf16, bool kTmaStore, int kBT, bool kNorm>
 __global__ void __launch_bounds__(W8WideCfg<kTmaStore, kBT>::kThreads, 1)
     w8_wide_kernel(const __grid_constant__ CUtensorMap tm_x,
                    const __grid_constant__ CUtensorMap tm_codes,
@@ -1153,13 +1148,9 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore, kBT>::kThreads, 1)
                    const __grid_constant__ CUtensorMap tm_bt,
                    const __grid_constant__ CUtensorMap tm_scales,
                    const __grid_constant__ CUtensorMap tm_norm,
-                   const __grid_constant__ CUtensorMap tm_ucodes,
-                   const __grid_constant__ CUtensorMap tm_uscales,
                    const __grid_constant__ OutMaps out_maps, const W8Params p) {
   using C = W8WideCfg<kTmaStore, kBT>;
   constexpr int BT = C::BT;
-  constexpr int kTileW = kSwiglu ? kBM / 2 : kBM;  // output features per tile
-  static_assert(!kSwiglu || (kTmaStore && kBT == 512 && !kNorm), "SwiGLU tile form");
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -1215,7 +1206,7 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore, kBT>::kThreads, 1)
       uint32_t outstanding = 0, issue_parity = 0;
       bool dep_ready = false;
       for (int tile = blockIdx.x; tile < p.n_tiles && !aborted(abort_flag); tile += gridDim.x) {
-        const int w0 = (tile % p.n_tiles_w) * kTileW;
+        const int w0 = (tile % p.n_tiles_w) * kBM;
         const int t0 = (tile / p.n_tiles_w) * BT;
         for (int it = 0; it < num_iters; ++it) {
           if (!ptx::mbar_wait(&empty[stage], phase ^ 1)) {
@@ -1240,12 +1231,6 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore, kBT>::kThreads, 1)
             if (p.scale_tma) {
               ptx::tma_load_2d(sx + C::kXBytes + C::kRawBytes, &tm_scales, &full[stage],
                                (it / 2) & ~3, w0);
-            }
-            if constexpr (kSwiglu) {  // the up rows: 64..127 of the tile
-              ptx::tma_load_2d(sx + C::kXBytes + (kBM / 2) * C::kBKw, &tm_ucodes, &full[stage],
-                               k0, w0);
-              ptx::tma_load_2d(sx + C::kXBytes + C::kRawBytes + (kBM / 2) * 16, &tm_uscales,
-                               &full[stage], (it / 2) & ~3, w0);
             }
           } else {
             if (!dep_ready) {  // P comes from the down-projection launched just before
@@ -1349,7 +1334,7 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore, kBT>::kThreads, 1)
     uint32_t slab = 0;
     int local = 0;
     for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x, ++local) {
-      const int w0 = (tile % p.n_tiles_w) * kTileW;
+      const int w0 = (tile % p.n_tiles_w) * kBM;
       const int t0 = (tile / p.n_tiles_w) * BT;
       // With the TMA-store path the four epilogue warps share named barriers,
       // so they decide together whether to go on.
@@ -1381,60 +1366,7 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore, kBT>::kThreads, 1)
             v[j] = __float_as_uint(__uint_as_float(v[j]) * __shfl_sync(0xffffffffu, rs_lane, j));
           }
         }
-        if constexpr (kSwiglu) {
-          // Rows 64-127 (up) leave their 32 rounded values in the slab's upper
-          // half; rows 0-63 (gate) pair them with their own and write h for
-          // feature w0 + row into the lower half (token-major, 128-byte rows).
-          const bool elected = threadIdx.x == kEpiWarp0 * kWarp;
-          if (elected) ptx::bulk_wait_read<1>();
-          ptx::named_bar_sync(1, 4 * kWarp);
-          uint16_t *stg = reinterpret_cast<uint16_t *>(staging + (slab & 1) * C::kSlabBytes);
-          uint32_t *ubuf = reinterpret_cast<uint32_t *>(stg + 32 * (kBM / 2));  // [64][16] bf16x2
-          if (row >= kBM / 2) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 2) {
-              const float a0 = __uint_as_float(v[j]), a1 = __uint_as_float(v[j + 1]);
-              ubuf[(row - kBM / 2) * 16 + (((j / 2) + row) & 15)] =
-                  kBf16 ? ptx::pack_bf16x2(a0, a1) : ptx::pack_f16x2(a0, a1);
-            }
-          }
-          ptx::named_bar_sync(1, 4 * kWarp);
-          if (row < kBM / 2) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 2) {
-              const float a0 = __uint_as_float(v[j]), a1 = __uint_as_float(v[j + 1]);
-              const uint32_t gp = kBf16 ? ptx::pack_bf16x2(a0, a1) : ptx::pack_f16x2(a0, a1);
-              const uint32_t up = ubuf[row * 16 + (((j / 2) + row + kBM / 2) & 15)];
-              float g0, g1, u0, u1;
-              if constexpr (kBf16) {
-                g0 = __uint_as_float(gp << 16);
-                g1 = __uint_as_float(gp & 0xffff0000u);
-                u0 = __uint_as_float(up << 16);
-                u1 = __uint_as_float(up & 0xffff0000u);
-              } else {
-                const float2 gf = __half22float2(*reinterpret_cast<const __half2 *>(&gp));
-                const float2 uf = __half22float2(*reinterpret_cast<const __half2 *>(&up));
-                g0 = gf.x;
-                g1 = gf.y;
-                u0 = uf.x;
-                u1 = uf.y;
-              }
-              // silu(g) * u in fp32 from the rounded projections, rounded once
-              const float h0 = g0 / (1.0f + __expf(-g0)) * u0;
-              const float h1 = g1 / (1.0f + __expf(-g1)) * u1;
-              const uint32_t hp = kBf16 ? ptx::pack_bf16x2(h0, h1) : ptx::pack_f16x2(h0, h1);
-              stg[j * (kBM / 2) + row] = static_cast<uint16_t>(hp & 0xffffu);
-              stg[(j + 1) * (kBM / 2) + row] = static_cast<uint16_t>(hp >> 16);
-            }
-          }
-          ptx::fence_proxy_async_smem();
-          ptx::named_bar_sync(1, 4 * kWarp);
-          if (elected) {
-            ptx::tma_store_2d(&out_maps.map[0], stg, w0, t0 + c * 32);
-            ptx::bulk_commit();
-          }
-          ++slab;
-        } else if constexpr (kTmaStore) {
+        if constexpr (kTmaStore) {
           // Stage a 32-token x 128-feature slab (token-major, 256-byte rows)
           // and let the TMA engine store it to every destination; the slab
           // buffer is double-buffered against the stores still reading it.
@@ -1520,7 +1452,7 @@ __global__ void __launch_bounds__(W8WideCfg<kTmaStore, kBT>::kThreads, 1)
     int stage = 0;
     uint32_t phase = 0;
     for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x) {
-      const int w0 = (tile % p.n_tiles_w) * kTileW;
+      const int w0 = (tile % p.n_tiles_w) * kBM;
       const int n = w0 + r;
       const float *srow = n < p.N && !p.scale_tma
                               ? p.w_scales + static_cast<int64_t>(n) * p.kb_per_row : nullptr;
@@ -2901,7 +2833,7 @@ int launch_w8_wide(const LinearArgs &L, unsigned *err, cudaStream_t stream) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   CFB_TRY_CUDA(cudaLaunchKernelEx(&cfg, kernel, tm_x, tm_codes, tm_p, tm_bt, tm_scales, tm_norm,
-                                  tm_norm, tm_norm, out_maps, p));
+                                  out_maps, p));
   return check_launch();
 }
 
@@ -3123,41 +3055,6 @@ int run_w8_swiglu(const void *x, const int8_t *g_codes, const float *g_scales,
   if (err == nullptr) return record_cuda_error(cudaGetLastError());
   CUtensorMap tm_x, tm_g, tm_u, tm_y;
   int st = CF_OK;
-  if (k % 256 == 0 && aligned_to(g_scales, 16) && aligned_to(u_scales, 16)) {
-    // The interleaved form on the wide kernel: 64 gate + 64 up rows per tile.
-    using W = W8WideCfg<true, 512>;
-    CUtensorMap tm_gs, tm_us, tm_unused;
-    std::memset(&tm_unused, 0, sizeof(tm_unused));
-    if ((st = make_map(&tm_x, x, 2, k, m, W::kBKw, 256, true))) return st;
-    if ((st = make_map(&tm_g, g_codes, 1, k, n, W::kBKw, kBM / 2, false))) return st;
-    if ((st = make_map(&tm_u, u_codes, 1, k, n, W::kBKw, kBM / 2, false))) return st;
-    if ((st = make_map(&tm_gs, g_scales, 4, k / kQuantBlockSize, n, 4, kBM / 2, false))) return st;
-    if ((st = make_map(&tm_us, u_scales, 4, k / kQuantBlockSize, n, 4, kBM / 2, false))) return st;
-    OutMaps out_maps;
-    std::memset(&out_maps, 0, sizeof(out_maps));
-    if ((st = make_map(&out_maps.map[0], y, 2, n, m, kBM / 2, 32, false))) return st;
-    W8Params p{};
-    p.M = static_cast<int>(m);
-    p.N = static_cast<int>(n);
-    p.num_kb = static_cast<int>(k / W::kBKw);
-    p.extra_ksteps = 0;
-    p.kb_per_row = static_cast<int>(k / kQuantBlockSize);
-    p.scale_tma = 1;
-    p.ldo = static_cast<int>(n);
-    p.n_outs = 1;
-    p.outs[0] = y;
-    p.n_tiles_w = static_cast<int>((n + kBM / 2 - 1) / (kBM / 2));
-    p.n_tiles = p.n_tiles_w * static_cast<int>((m + W::BT - 1) / W::BT);
-    p.err = err;
-    auto kernel = w8_wide_kernel<kBf16, true, 512, false, true>;
-    if ((st = allow_dynamic_smem<w8_wide_kernel<kBf16, true, 512, false, true>>(W::kSmemBytes))) {
-      return st;
-    }
-    const int grid = std::max(1, std::min(p.n_tiles, sm_count()));
-    kernel<<<grid, W::kThreads, W::kSmemBytes, stream>>>(tm_x, tm_g, tm_unused, tm_unused, tm_gs,
-                                                         tm_unused, tm_u, tm_us, out_maps, p);
-    return check_launch();
-  }
   if ((st = make_map(&tm_x, x, 2, k, m, C::kBKw, C::BT, true))) return st;
   if ((st = make_map(&tm_g, g_codes, 1, k, n, C::kBKw, kBM, false))) return st;
   if ((st = make_map(&tm_u, u_codes, 1, k, n, C::kBKw, kBM, false))) return st;
