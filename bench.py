@@ -1146,6 +1146,49 @@ class W8SwiGLU:
             stream.cuda_stream)
         _abi.check(st, self.name)
 
+    def extra_record(self, steps: int, flush) -> dict:
+        """The unfused route timed the same way: the gate and the up projection as two
+        W8 linears (a zero rank-16 adapter, the smallest the entry point takes), then
+        torch's silu(g) * u."""
+        from cuda_force_b200 import _abi
+
+        dev = self.dist.device
+        r = 16
+        a = torch.zeros(self.k, r, dtype=torch.bfloat16, device=dev)
+        b = torch.zeros(r, self.n, dtype=torch.bfloat16, device=dev)
+        g = torch.empty(self.m, self.n, dtype=torch.bfloat16, device=dev)
+        u = torch.empty_like(g)
+        ws_bytes = self.lib.cf_lora_linear_workspace_bytes(self.m, r)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+        stream = torch.cuda.current_stream(dev)
+
+        def unfused():
+            for codes, scales, out in ((self.gc, self.gs, g), (self.uc, self.us, u)):
+                _abi.check(self.lib.cf_lora_linear_int8(
+                    self.x.data_ptr(), codes.data_ptr(), scales.data_ptr(), a.data_ptr(),
+                    _abi.CF_LAYOUT_REF, b.data_ptr(), _abi.CF_LAYOUT_REF, out.data_ptr(),
+                    self.m, self.k, self.n, r, 1.0, _abi.CF_DTYPE_BF16, ws.data_ptr(), ws_bytes,
+                    stream.cuda_stream), "w8 projection")
+            torch.mul(torch.nn.functional.silu(g), u, out=self.y)
+
+        for _ in range(3):
+            unfused()
+        times = []
+        for i in range(steps):
+            if flush is not None:
+                flush.fill_(i & 0xFF)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            unfused()
+            e1.record(stream)
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1))
+        ms = statistics.mean(times)
+        return {"unfused_ms_per_step": round(ms, 5),
+                "unfused_tflops": round(self.work_per_step / ms / 1e9, 1),
+                "how": "two cf_lora_linear_int8 calls (zero rank-16 adapter) then torch "
+                       "silu(g) * u, same flush and CUDA events"}
+
     def verify(self) -> None:
         from oracle import linear_ref
 
