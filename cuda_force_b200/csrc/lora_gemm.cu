@@ -2853,14 +2853,9 @@ int run_linear(const LinearArgs &L, cudaStream_t stream) {
     if (L.n_dest == 0 && L.m <= 32) return launch_w8_decode<32, kBf16>(L, err, stream);
     if (L.n_dest == 0 && L.m <= 64) return launch_w8_decode<64, kBf16>(L, err, stream);
     if (L.n_dest == 0 && L.m <= 128) return launch_w8_decode<128, kBf16>(L, err, stream);
-    // The multicast all-gather runs 256-token tiles with two accumulators, so
-    // its NVLink stores overlap the next tile's main loop (1.81 ms against
-    // 1.86 ms at 8 GPUs, config 5); the peer-store form measured slower so
-    // (1.92 ms against 1.86 ms) and keeps 512-token tiles, as does the
-    // copy-engine form, whose counters count 512-token row blocks.
-    if (L.mc != nullptr && L.done == nullptr) {
-      return launch_w8_wide<kBf16, true, 256>(L, err, stream);
-    }
+    // Every call runs 512-token tiles (the 256-token, two-accumulator form
+    // kept for measurement overlapped the multicast stores at 8 GPUs, 1.81
+    // against 1.86 ms, but was 35 % slower at 2 GPUs and on one GPU).
     return launch_w8_wide<kBf16, true, 512>(L, err, stream);
   }
 
