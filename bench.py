@@ -1265,8 +1265,10 @@ class W8ColumnSharded:
         self.dist = dist
         if self.comm is None:
             self.comm = COMM_MODE
-        if self.comm == "auto":
-            self.comm = "mc" if dist.world > 1 and _multicast_ok(dist) else "fused"
+        if self.comm == "auto" and dist.world == 1:
+            self.comm = "fused"
+        # At N > 1 "auto" is resolved in setup(): asking whether the GPUs support
+        # multicast imports this package, which the reference arm must not.
 
     def flops(self) -> float:
         return 2.0 * self.m * self.n * self.k + 2.0 * self.m * self.r * (self.k + self.n)
@@ -1277,7 +1279,11 @@ class W8ColumnSharded:
                 "rank": self.r, "alpha": self.alpha, "weight": "block-64 int8 codes + fp32 scales",
                 "parallelism": f"column-sharded over {g} GPU(s): {self.n // g} output features "
                                f"per rank, x and A replicated; all-gather of y "
-                               + ("fused into the GEMM epilogue: each 16-byte piece written "
+                               + ("fused into the GEMM epilogue: multimem stores through y's "
+                                  "NVLink multicast address where the GPUs support it, else "
+                                  "TMA stores into every rank's copy" if self.comm == "auto"
+                                  and g > 1 else
+                                  "fused into the GEMM epilogue: each 16-byte piece written "
                                   "once through y's NVLink multicast address (multimem.st), "
                                   "the switch delivers it to every rank" if self.comm == "mc"
                                   and g > 1 else
@@ -1317,6 +1323,8 @@ class W8ColumnSharded:
         self.fused = None
         if reference:
             return
+        if self.comm == "auto":
+            self.comm = "mc" if _multicast_ok(self.dist) else "fused"
         if self.dist.world > 1 and self.comm in ("fused", "ce", "mc"):
             from cuda_force_b200.sharding import FusedGatherLinear
 

@@ -92,3 +92,23 @@ def test_headline_line_lists_every_benchmark_config():
         "w8_lora_decode_32x4096x11008", "w8_lora_prefill_4096x4096x11008",
         "w8_lora_70b_colshard_16384x8192x28672"}
     assert all(name in bench.WORKLOADS for name in bench.PER_CONFIG + bench.PER_CONFIG_MULTI)
+
+
+def test_config5_workloads_at_two_ranks_import_nothing_until_set_up(tmp_path):
+    # The reference arm builds every per_config workload at N > 1 too; choosing the
+    # multicast exchange (which asks this package about the GPUs) waits for setup().
+    import subprocess
+    import sys
+
+    script = tmp_path / "two_ranks.py"
+    script.write_text(
+        "import sys\n"
+        f"sys.path.insert(0, {str(bench.ROOT)!r})\n"
+        "import bench\n"
+        "class D:\n    world, rank, local_rank = 2, 0, 0\n"
+        "for cls in (bench.W8ColumnSharded, bench.W8ColumnShardedNccl, bench.W8ColumnShardedPeer):\n"
+        "    wl = cls(D())\n"
+        "    wl.config()\n"
+        "assert 'cuda_force_b200' not in sys.modules\n")
+    out = subprocess.run([sys.executable, str(script)], capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stderr[-2000:]
